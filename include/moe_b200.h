@@ -1,0 +1,143 @@
+/*
+ * moe_b200.h — C ABI of the B200 (sm_100a) MoE-layer library, libmoe_b200.so.
+ *
+ * The reference (flaneur2020/naiwa-rs) installs a routed-experts operator into its model through
+ * a Rust trait pair in its mistral.rs fork:
+ *
+ *   RoutedExpertsProvider::build(&self, ctx: ExpertLoadContext)
+ *       -> Result<Option<Arc<dyn RoutedExperts>>>              src/moe/provider.rs:316-615
+ *   RoutedExperts::forward(&self, xs: &Tensor, topk_weights: Tensor, topk_ids: &Tensor)
+ *       -> Result<Tensor>                                        src/moe/cached_layer.rs:524-664,
+ *                                                                src/moe/expert.rs:59-117
+ *
+ * Each entry point below names the reference interface it replaces. The ABI carries plain
+ * pointers, sizes and status codes only: no Rust, candle or torch types. Device pointers are
+ * CUDA device addresses on the layer's device; `stream` is a cudaStream_t (NULL = legacy stream).
+ *
+ * Ownership: the library owns expert weights (device copies, repacked for the kernels), routers,
+ * scratch and cache slots. The caller owns x, ids, weights and y of every call. Errors never
+ * abort: every call returns a moe_status, and moe_last_error() gives the message of the last
+ * failing call on the calling thread (the reference bails with messages, e.g. route.rs:52-68).
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  MOE_OK = 0,
+  MOE_ERR_INVALID = 1,     /* bad argument, shape or unsupported combination */
+  MOE_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+  MOE_ERR_OOM = 3,         /* device or pinned allocation failed */
+  MOE_ERR_TIMEOUT = 4,     /* a bounded device-side wait gave up (doorbells, paging fences) */
+  MOE_ERR_BAD_IDS = 5,     /* a routed expert id >= num_experts (reference route.rs:52-68) */
+  MOE_ERR_UNSUPPORTED = 6, /* feature not built for this configuration */
+  MOE_ERR_WORKER = 7       /* a latched host-worker error (reference executor.rs:242-253) */
+} moe_status;
+
+/* Expert weight formats. Host/device inputs are GGML stacks [E, N, K] (gate/up N=I,K=H;
+ * down N=H,K=I), the byte layout src/moe/expert.rs:123-145 slices. */
+typedef enum {
+  MOE_DTYPE_BF16 = 0,          /* 2 B / weight, row-major */
+  MOE_DTYPE_Q8_0 = 1,          /* 34 B / 32 weights: f16 d, int8 qs[32] */
+  MOE_DTYPE_Q4_K = 2,          /* 144 B / 256 weights: f16 d, f16 dmin, u8 scales[12], u8 qs[128] */
+  MOE_DTYPE_FP8_E4M3_B128 = 3  /* 1 B / weight e4m3 + one f32 scale per 128x128 block ([E, N/128, K/128]) */
+} moe_wdtype;
+
+typedef enum {
+  MOE_ROUTER_SOFTMAX = 0,        /* softmax over all experts, top-k of it, no renormalisation */
+  MOE_ROUTER_SOFTMAX_RENORM = 1, /* softmax, top-k, renormalised over the k (Qwen3-MoE) */
+  MOE_ROUTER_SIGMOID_GROUP = 2   /* sigmoid scores + bias, group-limited top-k (DeepSeek-V3) */
+} moe_router_mode;
+
+typedef struct moe_layer moe_layer;
+
+typedef struct {
+  int num_experts;      /* E   (reference: ctx.config.num_experts) */
+  int top_k;            /* k   (config.num_experts_per_tok) */
+  int hidden;           /* H   (config.hidden_size), multiple of 256 for quantized formats */
+  int inter;            /* I   (config.moe_intermediate_size) */
+  int wdtype;           /* moe_wdtype */
+  /* Stacked projections in GGML layout; host or device memory per `weights_on_device`.
+   * For MOE_DTYPE_FP8_E4M3_B128 the *_scale arrays give the [E, N/128, K/128] f32 block scales. */
+  const void* gate;
+  const void* up;
+  const void* down;
+  const float* gate_scale;
+  const float* up_scale;
+  const float* down_scale;
+  int weights_on_device; /* 0: host pointers, 1: device pointers on `device` */
+  /* Router (the fork's gate linear; kept on the CPU for prediction at provider.rs:618-629). */
+  const uint16_t* router_weight; /* [E, H] bf16, same memory kind as the weights; may be NULL */
+  const float* router_bias;      /* [E] f32 selection bias for MOE_ROUTER_SIGMOID_GROUP; may be NULL */
+  int router_mode;               /* moe_router_mode */
+  int n_group;                   /* groups for MOE_ROUTER_SIGMOID_GROUP */
+  int topk_group;                /* groups kept */
+  float routed_scale;            /* multiplier on routed weights (1.0 when unused) */
+  int device;                    /* CUDA ordinal (reference: ctx.layer_device) */
+  int max_tokens;                /* largest T of one forward call; sizes scratch at create */
+} moe_layer_desc;
+
+/* Replaces RoutedExpertsProvider::build (src/moe/provider.rs:316-615): validates the shape,
+ * copies and repacks the expert stacks into device memory, allocates scratch for max_tokens. */
+moe_status moe_layer_create(const moe_layer_desc* desc, moe_layer** out);
+
+/* Replaces the provider's warmup (src/moe/provider.rs:192-303): grows scratch to max_tokens. */
+moe_status moe_layer_warmup(moe_layer* layer, int max_tokens);
+
+/* Router + top-k for T tokens, upstream of RoutedExperts::forward in the reference's fork model
+ * (its CPU restatement is CachedLayer::predict, cached_layer.rs:1236-1249 with top_k_ids
+ * :358-363). x: [T, H] bf16 device; ids: [T, k] u32 device; weights: [T, k] f32 device. ids are
+ * ordered by score, largest first, ties to the lowest expert id. */
+moe_status moe_route(moe_layer* layer, const void* x, int T, uint32_t* ids, float* weights, void* stream);
+
+/* Replaces RoutedExperts::forward(xs, topk_weights, topk_ids) (cached_layer.rs:524-664,
+ * expert.rs:59-117): y[t] = sum_j weights[t,j] * down(silu(gate x_t) * up x_t) of expert ids[t,j].
+ * x, y: [T, H] bf16 device; ids [T, width] u32; weights [T, width] f32. `width` may differ from
+ * top_k (weight-0 padded rows, gpu.rs:100-131). Ids >= num_experts fail with MOE_ERR_BAD_IDS
+ * (reported by the next call that synchronises; checked on device, no host read). */
+moe_status moe_forward(moe_layer* layer, const void* x, int T, const uint32_t* ids, const float* weights,
+                       int width, void* y, void* stream);
+
+/* Releases everything the layer owns (the provider's Drop). Safe on NULL. */
+void moe_layer_destroy(moe_layer* layer);
+
+/* Number of device bytes the layer holds (weights + scratch); the slot pricing of
+ * src/moe/slot.rs:76-111 extended to scratch. */
+int64_t moe_layer_device_bytes(const moe_layer* layer);
+
+/* Reads and clears the device-side error word of the layer (bad ids seen by a forward).
+ * Synchronises `stream`. Returns MOE_OK or the latched status. */
+moe_status moe_layer_check(moe_layer* layer, void* stream);
+
+/* Message of the last failing call on this thread; returns its length. */
+size_t moe_last_error(char* buf, size_t n);
+
+/* ---- stateless kernels (the layer calls the same code) ----------------------------------- */
+
+/* Router logits + top-k without a layer. w_router: [E, H] bf16; bias: [E] f32 or NULL. */
+moe_status moe_route_tokens(const void* x, const void* w_router, const float* bias, int T, int H, int E, int k,
+                            int mode, int n_group, int topk_group, float routed_scale, uint32_t* ids,
+                            float* weights, void* stream);
+
+/* Expert histogram + stable token->expert permutation of n_pairs routed pairs (the grouping the
+ * reference does in Gpu::submit, gpu.rs:103-132, and rings::group_rows, rings.rs:68-156).
+ * counts [E], offsets [E+1] (exclusive prefix), perm [n_pairs] (sorted position -> pair index,
+ * stable), active [E] (experts with count > 0, ascending) and n_active [1], all int32 device.
+ * workspace: device scratch of moe_plan_workspace_bytes(n_pairs, E) bytes. */
+moe_status moe_plan_pairs(const uint32_t* ids, int n_pairs, int E, int32_t* counts, int32_t* offsets,
+                          int32_t* perm, int32_t* active, int32_t* n_active, void* workspace,
+                          size_t workspace_bytes, int32_t* error_word, void* stream);
+size_t moe_plan_workspace_bytes(int n_pairs, int E);
+
+/* Library version string. */
+const char* moe_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
