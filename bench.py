@@ -1,0 +1,447 @@
+#!/usr/bin/env python
+"""MoE-layer tokens/s on B200 — BASELINE config 2 (Qwen3-30B-A3B-shaped decode layer, Q8_0).
+
+Workload ("step"): a ragged decode sweep — batches of T = 1, 2, 4, ..., 256 tokens — each pushed
+through a stack of 48 distinct MoE layers (hidden 2048, 128 experts, top-8 renormalised softmax,
+moe_intermediate 768, SwiGLU, Q8_0 weights ~ N(0, 0.02), router ~ N(0, 0.02), activations
+~ N(0, 1), seeded). Per (T, layer): router + top-k (moe_route) then the routed experts
+(moe_forward). The metric counts tokens through one MoE layer: 511 tokens x 48 layers per step.
+The 48 layers hold 30.8 GB of expert weights, far more than the 126 MB L2, so every layer reads
+its experts from HBM (no L2 flush needed).
+
+`value` is device time of CUDA-graph replays with inputs resident in HBM; `e2e` is the same sweep
+through the public API (eager calls) with the activations copied in from pinned host memory and
+the outputs copied back, inside the timed region.
+
+--impl reference times the reference's CPU expert path (restated in the oracle: CPU router +
+two-pass fused Q8_0 decode, all host threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "naiwa-rs_b200"))
+sys.path.insert(0, ROOT)
+
+E, K_TOP, H, I = 128, 8, 2048, 768
+RAGGED = [1, 2, 4, 8, 16, 32, 64, 128, 256]
+BYTES_PER_EXPERT = 3 * I * H * 34 // 32  # 5,013,504 B of Q8_0 per expert (gate + up + down)
+METRIC = "MoE-layer tokens/s per B200 (decode, Qwen3-30B-A3B-shaped Q8_0 layer, ragged batch 1-256)"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_info():
+    model = "unknown"
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                model = ln.split(":", 1)[1].strip()
+                break
+    except Exception:
+        pass
+    return model, os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------------------------------------
+# reference arm: the CPU path of the reference, restated in the oracle
+# ---------------------------------------------------------------------------------------------
+
+def reference_sample_layer(seed: int = 2):
+    import numpy as np
+
+    from oracle import oracle as O
+
+    rng = np.random.Generator(np.random.Philox(seed))
+    q = []
+    for shape in ((E, I, H), (E, I, H), (E, H, I)):
+        w = rng.standard_normal(shape, dtype=np.float32)
+        w *= np.float32(0.02)
+        q.append(O.quantize(O.DT_Q8_0, w)[0])
+        del w
+    router = O.f32_to_bf16((rng.standard_normal((E, H), dtype=np.float32) * np.float32(0.02)))
+    xs = {T: O.f32_to_bf16(rng.standard_normal((T, H), dtype=np.float32)) for T in RAGGED}
+    return q, router, xs
+
+
+def reference_sweep(q, router, xs, threads):
+    from oracle import oracle as O
+
+    tokens = 0
+    for T in RAGGED:
+        x = xs[T]
+        ids, w = O.route(O.router_logits(x, router), K_TOP, 1)
+        O.fused_moe_decode_q8_0(q[0], q[1], q[2], O.bf16_to_f32(x).reshape(T, H), ids, w, E, H, I, threads)
+        tokens += T
+    return tokens
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    model, ncpu = cpu_info()
+    q, router, xs = reference_sample_layer()
+    for _ in range(args.warmup):
+        reference_sweep(q, router, xs, ncpu)
+    t0 = time.perf_counter()
+    tokens = 0
+    for _ in range(args.steps):
+        tokens += reference_sweep(q, router, xs, ncpu)
+    dt = time.perf_counter() - t0
+    value = tokens / dt
+    sample = (f"one Qwen3-30B-A3B-shaped Q8_0 MoE layer (E128 k8 H2048 I768), ragged sweep T=1..256 "
+              f"(511 tokens) per step; CPU router + two-pass fused decode; {ncpu} threads on {model}")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 weights, f32 compute",
+        "data": "synthetic (seeded Philox normal weights/activations)",
+        "config": {"workload": "cfg2 decode sweep, 1 layer per step (bounded CPU sample)", "layers": 1},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": ncpu, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------------
+
+def cpu_baseline_from_layer(stacks_host, router_host, budget_s=12.0):
+    """Oracle fused decode (the reference's CPU path) over the same layer's bytes, all host threads,
+    repeated ragged sweeps until ~budget_s of CPU work."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    model, ncpu = cpu_info()
+    rng = np.random.Generator(np.random.Philox(7))
+    xs = {T: O.f32_to_bf16(rng.standard_normal((T, H), dtype=np.float32)) for T in RAGGED}
+    reference_sweep(stacks_host, router_host, xs, ncpu)  # warm
+    t0 = time.perf_counter()
+    tokens = sweeps = 0
+    while time.perf_counter() - t0 < budget_s or sweeps == 0:
+        tokens += reference_sweep(stacks_host, router_host, xs, ncpu)
+        sweeps += 1
+    dt = time.perf_counter() - t0
+    return {"value": tokens / dt, "unit": "tokens/s", "cores": ncpu, "kind": "port",
+            "sample": f"{sweeps} ragged sweeps (T=1..256) through layer 0 of the same stack; CPU router + "
+                      f"two-pass fused Q8_0 decode; {ncpu} threads on {model}"}
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    import moe_b200 as M
+    from moe_b200 import synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    L = args.layers
+    provider = M.RoutedExpertsProvider()
+    cfg = M.MoeConfig(num_experts=E, num_experts_per_tok=K_TOP, hidden_size=H, moe_intermediate_size=I,
+                      router_mode=M.ROUTER_SOFTMAX_RENORM)
+    layers = []
+    host_layer0 = None
+    for li in range(L):
+        g, u, d = synth.expert_stacks(E, H, I, M.DTYPE_Q8_0, 0.02, seed=1000 + li, device=dev)
+        router = synth.router_weight(E, H, 0.02, seed=5000 + li, device=dev)
+        ctx = M.ExpertLoadContext(layer=li, device=local, config=cfg, wdtype=M.DTYPE_Q8_0, gate=g, up=u, down=d,
+                                  router_weight=router, max_tokens=max(RAGGED))
+        layers.append(provider.build(ctx))
+        if li == 0 and rank == 0 and world == 1 and not args.no_cpu_baseline:
+            host_layer0 = ([t.cpu().numpy() for t in (g, u, d)], router.view(torch.int16).cpu().numpy().view(np.uint16))
+        del g, u, d, router
+    torch.cuda.empty_cache()
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(77 + rank)
+    xs = {T: torch.randn((T, H), generator=gen, device=dev).to(torch.bfloat16) for T in RAGGED}
+    ids = {T: torch.empty((T, K_TOP), dtype=torch.int32, device=dev) for T in RAGGED}
+    wts = {T: torch.empty((T, K_TOP), dtype=torch.float32, device=dev) for T in RAGGED}
+    ys = {T: torch.empty((T, H), dtype=torch.bfloat16, device=dev) for T in RAGGED}
+
+    def sweep(Ts=RAGGED):
+        for T in Ts:
+            for layer in layers:
+                layer.route(xs[T], out_ids=ids[T], out_weights=wts[T])
+                layer.forward(xs[T], wts[T], ids[T], out=ys[T])
+
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup)):
+            sweep()
+    torch.cuda.synchronize()
+    for layer in layers:
+        layer.check()
+
+    # one CUDA graph per step (9 batch sizes x 48 layers x (route + forward))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        sweep()
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    tokens_per_step = sum(RAGGED) * L
+    with ClockSampler(local) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms = ev0.elapsed_time(ev1) / args.steps
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = tokens_per_step * world / (ms / 1e3)
+
+    # ---- algorithmic bytes: distinct experts each layer reads, from this step's routing ----------
+    distinct = {}
+    for T in RAGGED:
+        tot = 0
+        for layer in layers:
+            layer.route(xs[T], out_ids=ids[T], out_weights=wts[T])
+            tot += int(torch.unique(ids[T]).numel())
+        distinct[T] = tot
+    torch.cuda.synchronize()
+    act_bytes = {T: L * (T * H * 2 * 2 + T * K_TOP * 8 + E * H * 2) for T in RAGGED}  # x, y, ids+w, router
+    weight_bytes = {T: distinct[T] * BYTES_PER_EXPERT for T in RAGGED}
+
+    # ---- stage timing: the same step with events around plan / gate-up / down / combine ---------
+    nev = len(RAGGED) * L
+    evs = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(5)] for _ in range(nev)]
+    import ctypes
+
+    ev_arrays = []
+    for row in evs:
+        for e_ in row:
+            e_.record(stream)
+        ev_arrays.append((ctypes.c_void_p * 5)(*[e_.cuda_event for e_ in row]))
+    torch.cuda.synchronize()
+    lib = M.lib()
+
+    def marked_sweep():
+        i = 0
+        for T in RAGGED:
+            for layer in layers:
+                layer.route(xs[T], out_ids=ids[T], out_weights=wts[T])
+                st = ctypes.c_void_p(stream.cuda_stream)
+                rc = lib.moe_forward_marked(layer._h, xs[T].data_ptr(), T, ids[T].data_ptr(), wts[T].data_ptr(),
+                                            K_TOP, ys[T].data_ptr(), st, ev_arrays[i])
+                M._lib.check(rc)
+                i += 1
+
+    mgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(mgraph, stream=stream):
+        marked_sweep()
+    torch.cuda.synchronize()
+    mgraph.replay()
+    torch.cuda.synchronize()
+    stage = {"plan": 0.0, "gate_up": 0.0, "down": 0.0, "combine": 0.0}
+    per_T_expert_ms = {T: 0.0 for T in RAGGED}
+    i = 0
+    for T in RAGGED:
+        for _ in range(L):
+            row = evs[i]
+            d = [row[j].elapsed_time(row[j + 1]) for j in range(4)]
+            stage["plan"] += d[0]
+            stage["gate_up"] += d[1]
+            stage["down"] += d[2]
+            stage["combine"] += d[3]
+            per_T_expert_ms[T] += d[1] + d[2]
+            i += 1
+    expert_ms = stage["gate_up"] + stage["down"]
+    total_w_bytes = sum(weight_bytes.values())
+    hbm_peak, peak_kind = peaks()
+    achieved = total_w_bytes / (expert_ms / 1e3) / 1e9
+    per_batch = {}
+    for T in RAGGED:
+        gbs = weight_bytes[T] / (per_T_expert_ms[T] / 1e3) / 1e9
+        per_batch[str(T)] = {"expert_gemv_gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 3),
+                             "distinct_experts_per_layer": round(distinct[T] / L, 2),
+                             "expert_ms_per_layer": round(per_T_expert_ms[T] / L, 4)}
+
+    # ---- e2e: public API, activations from pinned host memory, outputs back to the host ---------
+    hx = {T: xs[T].cpu().pin_memory() for T in RAGGED}
+    hy = {T: torch.empty((T, H), dtype=torch.bfloat16).pin_memory() for T in RAGGED}
+    dx = {T: torch.empty_like(xs[T]) for T in RAGGED}
+    h2d = sum(T * H * 2 for T in RAGGED)
+    d2h = h2d
+
+    def e2e_step():
+        for T in RAGGED:
+            dx[T].copy_(hx[T], non_blocking=True)
+            cur = dx[T]
+            for layer in layers:
+                layer.route(cur, out_ids=ids[T], out_weights=wts[T])
+                layer.forward(cur, wts[T], ids[T], out=ys[T])
+            hy[T].copy_(ys[T], non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = tokens_per_step * world / (e2e_ms / 1e3)
+
+    for layer in layers:
+        layer.check()
+    del graph, mgraph
+    cpu_base = None
+    if host_layer0 is not None:
+        cpu_base = cpu_baseline_from_layer(host_layer0[0], host_layer0[1], budget_s=args.cpu_seconds)
+
+    launches_per_step = len(RAGGED) * L * 5  # route, plan, gate/up, down, combine
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q8_0 weights, f16 tensor-core MMA, f32 accumulate",
+            "data": "synthetic: seeded N(0,0.02) Q8_0 experts and router, N(0,1) bf16 activations",
+            "config": {"workload": "BASELINE config 2: Qwen3-30B-A3B-shaped MoE decode, E128 top-8 renorm-softmax "
+                                   "H2048 I768 Q8_0; ragged batches T=1,2,4,...,256 through 48 distinct layers",
+                       "layers": L, "tokens_per_step": tokens_per_step, "ragged_batches": RAGGED,
+                       "l2": "inputs larger than L2 (30.8 GB of expert weights cycled per step)",
+                       "parallelism": f"replicas x{world} (each GPU its own batch, no collective)"},
+            "roofline": {"kernel": "expert_gemv (gate/up+SwiGLU and down*weight, Q8_0)", "bound": "hbm",
+                         "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "peak_source": peak_kind,
+                         "traffic": None,
+                         "algorithmic_bytes": "5,013,504 B per distinct expert per layer (Q8_0 gate+up+down)"},
+            "stage_ms_per_step": {k: round(v, 3) for k, v in stage.items()},
+            "per_batch": per_batch,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu_base,
+        }
+        print(json.dumps(out), flush=True)
+    for layer in layers:
+        layer.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

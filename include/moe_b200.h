@@ -59,8 +59,8 @@ typedef struct moe_layer moe_layer;
 typedef struct {
   int num_experts;      /* E   (reference: ctx.config.num_experts) */
   int top_k;            /* k   (config.num_experts_per_tok) */
-  int hidden;           /* H   (config.hidden_size), multiple of 256 for quantized formats */
-  int inter;            /* I   (config.moe_intermediate_size) */
+  int hidden;           /* H   (config.hidden_size), multiple of 32 */
+  int inter;            /* I   (config.moe_intermediate_size), multiple of 32 */
   int wdtype;           /* moe_wdtype */
   /* Stacked projections in GGML layout; host or device memory per `weights_on_device`.
    * For MOE_DTYPE_FP8_E4M3_B128 the *_scale arrays give the [E, N/128, K/128] f32 block scales. */
@@ -102,6 +102,13 @@ moe_status moe_route(moe_layer* layer, const void* x, int T, uint32_t* ids, floa
  * (reported by the next call that synchronises; checked on device, no host read). */
 moe_status moe_forward(moe_layer* layer, const void* x, int T, const uint32_t* ids, const float* weights,
                        int width, void* y, void* stream);
+
+/* moe_forward with five caller-created CUDA events recorded on `stream` around its stages:
+ * events[0] before the plan, [1] after the plan, [2] after gate/up, [3] after down, [4] after the
+ * combine (recorded as external events, so they also become event nodes of a captured graph).
+ * The per-stage timing probe the reference keeps behind NAIWA_STEP_BUDGET (src/stats/budget.rs). */
+moe_status moe_forward_marked(moe_layer* layer, const void* x, int T, const uint32_t* ids, const float* weights,
+                              int width, void* y, void* stream, void* const* events);
 
 /* Releases everything the layer owns (the provider's Drop). Safe on NULL. */
 void moe_layer_destroy(moe_layer* layer);

@@ -1,0 +1,432 @@
+// layer.cu — the moe_layer object and the C ABI (include/moe_b200.h).
+//
+// moe_layer plays the role of the reference's per-MoE-block operator: GpuCacheMoeProvider::build
+// (src/moe/provider.rs:316-615) creates it from the block's expert stacks, and its forward is
+// RoutedExperts::forward (src/moe/cached_layer.rs:524-664 / src/moe/expert.rs:59-117). Here every
+// expert is resident in HBM (180 GB holds every config of this path), so the per-call work is:
+// plan (histogram + stable permute) -> gate/up+SwiGLU -> down*weight -> combine, all on the
+// caller's stream with no host synchronisation, so a sequence of calls captures into one CUDA graph.
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "moe_internal.cuh"
+#include <cmath>
+
+namespace moe {
+
+// ---- errors ----------------------------------------------------------------------------------
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+moe_status fail(moe_status st, const std::string& msg) {
+  g_last_error = msg;
+  return st;
+}
+
+moe_status cuda_fail(cudaError_t e, const char* what) {
+  g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+  return e == cudaErrorMemoryAllocation ? MOE_ERR_OOM : MOE_ERR_CUDA;
+}
+
+// ---- device guard ------------------------------------------------------------------------------
+
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = true;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace moe
+
+using namespace moe;
+
+struct moe_layer {
+  moe_layer_desc d{};
+  int dev = 0;
+  int sms = 148;
+  // weights (device layout)
+  uint8_t* gu_q = nullptr;
+  uint8_t* gu_s = nullptr;
+  uint8_t* dn_q = nullptr;
+  uint8_t* dn_s = nullptr;
+  int64_t gu_q_stride = 0, gu_s_stride = 0, dn_q_stride = 0, dn_s_stride = 0;
+  __nv_bfloat16* router_w = nullptr;
+  float* router_b = nullptr;
+  // scratch
+  int cap_pairs = 0;
+  int32_t* counts = nullptr;
+  int32_t* offsets = nullptr;
+  int32_t* perm = nullptr;
+  int32_t* active = nullptr;
+  int32_t* n_active = nullptr;
+  int32_t* err = nullptr;
+  void* plan_ws = nullptr;
+  size_t plan_ws_bytes = 0;
+  float* h = nullptr;
+  float* ypair = nullptr;
+  int64_t weight_bytes = 0;
+  int64_t scratch_bytes = 0;
+};
+
+static void free_scratch(moe_layer* L) {
+  cudaFree(L->counts);
+  cudaFree(L->offsets);
+  cudaFree(L->perm);
+  cudaFree(L->active);
+  cudaFree(L->n_active);
+  cudaFree(L->err);
+  cudaFree(L->plan_ws);
+  cudaFree(L->h);
+  cudaFree(L->ypair);
+  L->counts = L->offsets = L->perm = L->active = L->n_active = L->err = nullptr;
+  L->plan_ws = nullptr;
+  L->h = L->ypair = nullptr;
+  L->cap_pairs = 0;
+  L->scratch_bytes = 0;
+}
+
+template <class T>
+static moe_status dalloc(T** p, size_t bytes, int64_t* acct) {
+  void* v = nullptr;
+  cudaError_t e = cudaMalloc(&v, bytes ? bytes : 16);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+  *p = static_cast<T*>(v);
+  if (acct) *acct += (int64_t)(bytes ? bytes : 16);
+  return MOE_OK;
+}
+
+static moe_status alloc_scratch(moe_layer* L, int max_tokens) {
+  const int64_t cap64 = (int64_t)max_tokens * L->d.top_k;
+  if (cap64 > (1 << 28)) return fail(MOE_ERR_INVALID, "max_tokens * top_k too large");
+  const int cap = (int)cap64;
+  if (cap <= L->cap_pairs && L->counts) return MOE_OK;
+  free_scratch(L);
+  const int E = L->d.num_experts, H = L->d.hidden, I = L->d.inter;
+  int64_t acc = 0;
+  MOE_TRY(dalloc(&L->counts, sizeof(int32_t) * E, &acc));
+  MOE_TRY(dalloc(&L->offsets, sizeof(int32_t) * (E + 1), &acc));
+  MOE_TRY(dalloc(&L->perm, sizeof(int32_t) * cap, &acc));
+  MOE_TRY(dalloc(&L->active, sizeof(int32_t) * E, &acc));
+  MOE_TRY(dalloc(&L->n_active, sizeof(int32_t), &acc));
+  MOE_TRY(dalloc(&L->err, sizeof(int32_t), &acc));
+  MOE_CUDA_TRY(cudaMemset(L->err, 0, sizeof(int32_t)));
+  L->plan_ws_bytes = plan_workspace_bytes(cap, E);
+  MOE_TRY(dalloc(&L->plan_ws, L->plan_ws_bytes, &acc));
+  MOE_TRY(dalloc(&L->h, sizeof(float) * (size_t)cap * I, &acc));
+  MOE_TRY(dalloc(&L->ypair, sizeof(float) * (size_t)cap * H, &acc));
+  L->cap_pairs = cap;
+  L->scratch_bytes = acc;
+  return MOE_OK;
+}
+
+static void free_weights(moe_layer* L) {
+  cudaFree(L->gu_q);
+  cudaFree(L->gu_s);
+  cudaFree(L->dn_q);
+  cudaFree(L->dn_s);
+  cudaFree(L->router_w);
+  cudaFree(L->router_b);
+  L->gu_q = L->gu_s = L->dn_q = L->dn_s = nullptr;
+  L->router_w = nullptr;
+  L->router_b = nullptr;
+}
+
+static int64_t ggml_bytes(int wdtype, int64_t n) {
+  switch (wdtype) {
+    case MOE_DTYPE_BF16: return n * 2;
+    case MOE_DTYPE_Q8_0: return n / 32 * 34;
+    case MOE_DTYPE_Q4_K: return n / 256 * 144;
+    case MOE_DTYPE_FP8_E4M3_B128: return n;
+  }
+  return -1;
+}
+
+// Source bytes on the device: either the caller's device pointer or a temporary upload.
+static moe_status stage_source(const void* src, int64_t bytes, bool on_device, uint8_t** out, bool* owned) {
+  if (on_device) {
+    *out = (uint8_t*)src;
+    *owned = false;
+    return MOE_OK;
+  }
+  MOE_TRY(dalloc(out, (size_t)bytes, nullptr));
+  *owned = true;
+  cudaError_t e = cudaMemcpy(*out, src, (size_t)bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(*out);
+    *out = nullptr;
+    return cuda_fail(e, "cudaMemcpy(weights)");
+  }
+  return MOE_OK;
+}
+
+static moe_status validate_desc(const moe_layer_desc* d) {
+  if (!d) return fail(MOE_ERR_INVALID, "moe_layer_create: null desc");
+  if (d->num_experts <= 0 || d->num_experts > 1024) return fail(MOE_ERR_INVALID, "num_experts must be in 1..1024");
+  if (d->top_k <= 0 || d->top_k > d->num_experts || d->top_k > 32)
+    return fail(MOE_ERR_INVALID, "top_k must be in 1..min(num_experts, 32)");
+  if (d->hidden <= 0 || d->inter <= 0) return fail(MOE_ERR_INVALID, "hidden and inter must be positive");
+  if (d->hidden % 32 || d->inter % 32)
+    return fail(MOE_ERR_INVALID, "hidden and inter must be multiples of 32 (one Q8_0 block / two k16 MMA steps)");
+  if (d->wdtype != MOE_DTYPE_BF16 && d->wdtype != MOE_DTYPE_Q8_0)
+    return fail(MOE_ERR_UNSUPPORTED, "weight format not built for the decode path yet");
+  if (!d->gate || !d->up || !d->down) return fail(MOE_ERR_INVALID, "null expert stack");
+  if (d->max_tokens <= 0) return fail(MOE_ERR_INVALID, "max_tokens must be positive");
+  return MOE_OK;
+}
+
+extern "C" {
+
+moe_status moe_layer_create(const moe_layer_desc* desc, moe_layer** out) {
+  if (!out) return fail(MOE_ERR_INVALID, "moe_layer_create: null out");
+  *out = nullptr;
+  MOE_TRY(validate_desc(desc));
+  DeviceGuard guard(desc->device);
+  if (!guard.ok) return fail(MOE_ERR_CUDA, "moe_layer_create: cannot select device");
+  moe_layer* L = new moe_layer();
+  L->d = *desc;
+  L->dev = desc->device;
+  cudaDeviceGetAttribute(&L->sms, cudaDevAttrMultiProcessorCount, L->dev);
+  const int E = desc->num_experts, H = desc->hidden, I = desc->inter, w = desc->wdtype;
+  const bool on_dev = desc->weights_on_device != 0;
+  auto cleanup = [&](moe_status st) {
+    free_weights(L);
+    free_scratch(L);
+    delete L;
+    return st;
+  };
+  L->gu_q_stride = device_q_bytes(w, 2 * I, H);
+  L->gu_s_stride = device_s_bytes(w, 2 * I, H);
+  L->dn_q_stride = device_q_bytes(w, H, I);
+  L->dn_s_stride = device_s_bytes(w, H, I);
+  int64_t acct = 0;
+  moe_status st;
+  if ((st = dalloc(&L->gu_q, (size_t)(L->gu_q_stride * E), &acct)) != MOE_OK) return cleanup(st);
+  if ((st = dalloc(&L->dn_q, (size_t)(L->dn_q_stride * E), &acct)) != MOE_OK) return cleanup(st);
+  if (L->gu_s_stride && (st = dalloc(&L->gu_s, (size_t)(L->gu_s_stride * E), &acct)) != MOE_OK) return cleanup(st);
+  if (L->dn_s_stride && (st = dalloc(&L->dn_s, (size_t)(L->dn_s_stride * E), &acct)) != MOE_OK) return cleanup(st);
+  {
+    const int64_t gb = ggml_bytes(w, (int64_t)E * I * H);
+    uint8_t *g = nullptr, *u = nullptr, *dn = nullptr;
+    bool og = false, ou = false, od = false;
+    st = stage_source(desc->gate, gb, on_dev, &g, &og);
+    if (st == MOE_OK) st = stage_source(desc->up, gb, on_dev, &u, &ou);
+    if (st == MOE_OK) st = stage_source(desc->down, gb, on_dev, &dn, &od);
+    if (st == MOE_OK) st = repack_projection(w, g, u, E, I, H, L->gu_q, L->gu_s, 0);
+    if (st == MOE_OK) st = repack_projection(w, dn, nullptr, E, H, I, L->dn_q, L->dn_s, 0);
+    cudaError_t se = cudaDeviceSynchronize();
+    if (og) cudaFree(g);
+    if (ou) cudaFree(u);
+    if (od) cudaFree(dn);
+    if (st != MOE_OK) return cleanup(st);
+    if (se != cudaSuccess) return cleanup(cuda_fail(se, "repack"));
+  }
+  if (desc->router_weight) {
+    const size_t rb = (size_t)E * H * 2;
+    if ((st = dalloc(&L->router_w, rb, &acct)) != MOE_OK) return cleanup(st);
+    cudaError_t e = cudaMemcpy(L->router_w, desc->router_weight, rb, on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMemcpy(router)"));
+  }
+  if (desc->router_bias) {
+    if ((st = dalloc(&L->router_b, sizeof(float) * E, &acct)) != MOE_OK) return cleanup(st);
+    cudaError_t e = cudaMemcpy(L->router_b, desc->router_bias, sizeof(float) * E,
+                               on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMemcpy(router bias)"));
+  }
+  L->weight_bytes = acct;
+  // the desc keeps no caller pointers beyond create
+  L->d.gate = L->d.up = L->d.down = nullptr;
+  L->d.gate_scale = L->d.up_scale = L->d.down_scale = nullptr;
+  L->d.router_weight = nullptr;
+  L->d.router_bias = nullptr;
+  if ((st = alloc_scratch(L, desc->max_tokens)) != MOE_OK) return cleanup(st);
+  *out = L;
+  return MOE_OK;
+}
+
+moe_status moe_layer_warmup(moe_layer* L, int max_tokens) {
+  if (!L) return fail(MOE_ERR_INVALID, "moe_layer_warmup: null layer");
+  if (max_tokens <= 0) return fail(MOE_ERR_INVALID, "moe_layer_warmup: max_tokens must be positive");
+  DeviceGuard guard(L->dev);
+  MOE_CUDA_TRY(cudaDeviceSynchronize());
+  MOE_TRY(alloc_scratch(L, max_tokens));
+  L->d.max_tokens = max_tokens > L->d.max_tokens ? max_tokens : L->d.max_tokens;
+  return MOE_OK;
+}
+
+moe_status moe_route(moe_layer* L, const void* x, int T, uint32_t* ids, float* weights, void* stream) {
+  if (!L) return fail(MOE_ERR_INVALID, "moe_route: null layer");
+  if (!L->router_w) return fail(MOE_ERR_INVALID, "moe_route: layer was created without router weights");
+  DeviceGuard guard(L->dev);
+  RouteParams p{static_cast<const __nv_bfloat16*>(x), L->router_w, L->router_b, ids, weights, T, L->d.hidden,
+                L->d.num_experts, L->d.top_k, L->d.router_mode, L->d.n_group, L->d.topk_group,
+                L->d.routed_scale};
+  return route_tokens(p, static_cast<cudaStream_t>(stream));
+}
+
+// Row tiles per CTA: the largest of 8/4/2/1 that still gives >= 2 CTAs per SM for the expected
+// number of distinct experts (uniform routing: E (1 - (1 - 1/E)^pairs)).
+static int pick_rowt(int tiles, double est_active, int sms) {
+  for (int r = 8; r >= 1; r >>= 1) {
+    if (r > tiles) continue;
+    if (est_active * ceil_div(tiles, r) >= 2.0 * sms) return r;
+  }
+  return 1;
+}
+
+static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_t* ids, const float* weights,
+                               int width, void* y, void* stream, void* const* events);
+
+moe_status moe_forward(moe_layer* L, const void* x, int T, const uint32_t* ids, const float* weights, int width,
+                       void* y, void* stream) {
+  return forward_impl(L, x, T, ids, weights, width, y, stream, nullptr);
+}
+
+moe_status moe_forward_marked(moe_layer* L, const void* x, int T, const uint32_t* ids, const float* weights,
+                              int width, void* y, void* stream, void* const* events) {
+  if (!events) return fail(MOE_ERR_INVALID, "moe_forward_marked: null events");
+  for (int i = 0; i < 5; ++i)
+    if (!events[i]) return fail(MOE_ERR_INVALID, "moe_forward_marked: null event");
+  return forward_impl(L, x, T, ids, weights, width, y, stream, events);
+}
+
+}  // extern "C"
+
+static moe_status mark(void* const* events, int i, cudaStream_t st) {
+  if (!events) return MOE_OK;
+  MOE_CUDA_TRY(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[i]), st, cudaEventRecordExternal));
+  return MOE_OK;
+}
+
+static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_t* ids, const float* weights,
+                               int width, void* y, void* stream, void* const* events) {
+  if (!L) return fail(MOE_ERR_INVALID, "moe_forward: null layer");
+  if (T < 0 || width <= 0) return fail(MOE_ERR_INVALID, "moe_forward: need T >= 0 and width > 0");
+  if (T == 0) return MOE_OK;
+  if (!x || !ids || !weights || !y) return fail(MOE_ERR_INVALID, "moe_forward: null pointer");
+  if (((uintptr_t)x | (uintptr_t)ids | (uintptr_t)weights) & 3)
+    return fail(MOE_ERR_INVALID, "moe_forward: x, ids and weights must be 4-byte aligned");
+  if ((uintptr_t)y & 7) return fail(MOE_ERR_INVALID, "moe_forward: y must be 8-byte aligned");
+  const int64_t n64 = (int64_t)T * width;
+  if (n64 > L->cap_pairs)
+    return fail(MOE_ERR_INVALID, "moe_forward: T * width exceeds the scratch sized at create/warmup (call "
+                                 "moe_layer_warmup with a larger max_tokens)");
+  DeviceGuard guard(L->dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int n_pairs = (int)n64;
+  const int E = L->d.num_experts, H = L->d.hidden, I = L->d.inter;
+  PlanOut po{L->counts, L->offsets, L->perm, L->active, L->n_active, L->err};
+  MOE_TRY(mark(events, 0, st));
+  MOE_TRY(plan_pairs(ids, n_pairs, E, po, L->plan_ws, L->plan_ws_bytes, st));
+  MOE_TRY(mark(events, 1, st));
+  const int max_active = n_pairs < E ? n_pairs : E;
+  const double est = (double)E * (1.0 - std::pow(1.0 - 1.0 / E, (double)n_pairs));
+
+  ExpertParams gp{};
+  gp.wq = L->gu_q;
+  gp.wsc = L->gu_s;
+  gp.q_stride = L->gu_q_stride;
+  gp.s_stride = L->gu_s_stride;
+  gp.N = 2 * I;
+  gp.K = H;
+  gp.tiles = 2 * I / 16;
+  gp.kb_count = H / 32;
+  gp.phase = 0;
+  gp.tpp = choose_tpp(H);
+  gp.width = width;
+  gp.n_pairs = n_pairs;
+  gp.x = static_cast<const __nv_bfloat16*>(x);
+  gp.out = L->h;
+  gp.offsets = L->offsets;
+  gp.perm = L->perm;
+  gp.active = L->active;
+  gp.n_active = L->n_active;
+  MOE_TRY(launch_expert_gemv(L->d.wdtype, gp, max_active, pick_rowt(gp.tiles, est, L->sms), st));
+  MOE_TRY(mark(events, 2, st));
+
+  ExpertParams dp = gp;
+  dp.wq = L->dn_q;
+  dp.wsc = L->dn_s;
+  dp.q_stride = L->dn_q_stride;
+  dp.s_stride = L->dn_s_stride;
+  dp.N = H;
+  dp.K = I;
+  dp.tiles = H / 16;
+  dp.kb_count = I / 32;
+  dp.phase = 1;
+  dp.tpp = choose_tpp(I);
+  dp.x = nullptr;
+  dp.h_in = L->h;
+  dp.route_w = weights;
+  dp.out = L->ypair;
+  MOE_TRY(launch_expert_gemv(L->d.wdtype, dp, max_active, pick_rowt(dp.tiles, est, L->sms), st));
+  MOE_TRY(mark(events, 3, st));
+  MOE_TRY(launch_combine(L->ypair, ids, T, width, H, E, y, st));
+  return mark(events, 4, st);
+}
+
+extern "C" {
+
+void moe_layer_destroy(moe_layer* L) {
+  if (!L) return;
+  DeviceGuard guard(L->dev);
+  cudaDeviceSynchronize();
+  free_weights(L);
+  free_scratch(L);
+  delete L;
+}
+
+int64_t moe_layer_device_bytes(const moe_layer* L) { return L ? L->weight_bytes + L->scratch_bytes : 0; }
+
+moe_status moe_layer_check(moe_layer* L, void* stream) {
+  if (!L) return fail(MOE_ERR_INVALID, "moe_layer_check: null layer");
+  DeviceGuard guard(L->dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t v = 0;
+  MOE_CUDA_TRY(cudaMemcpyAsync(&v, L->err, sizeof(v), cudaMemcpyDeviceToHost, st));
+  MOE_CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int32_t), st));
+  MOE_CUDA_TRY(cudaStreamSynchronize(st));
+  if (v == MOE_ERR_BAD_IDS) return fail(MOE_ERR_BAD_IDS, "routed expert id >= num_experts");
+  if (v != 0) return fail((moe_status)v, "device error word set");
+  return MOE_OK;
+}
+
+size_t moe_last_error(char* buf, size_t n) {
+  if (buf && n) {
+    size_t m = g_last_error.size() < n - 1 ? g_last_error.size() : n - 1;
+    memcpy(buf, g_last_error.data(), m);
+    buf[m] = 0;
+  }
+  return g_last_error.size();
+}
+
+moe_status moe_route_tokens(const void* x, const void* w_router, const float* bias, int T, int H, int E, int k,
+                            int mode, int n_group, int topk_group, float routed_scale, uint32_t* ids,
+                            float* weights, void* stream) {
+  RouteParams p{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w_router), bias, ids,
+                weights, T, H, E, k, mode, n_group, topk_group, routed_scale};
+  return route_tokens(p, static_cast<cudaStream_t>(stream));
+}
+
+moe_status moe_plan_pairs(const uint32_t* ids, int n_pairs, int E, int32_t* counts, int32_t* offsets,
+                          int32_t* perm, int32_t* active, int32_t* n_active, void* workspace,
+                          size_t workspace_bytes, int32_t* error_word, void* stream) {
+  PlanOut o{counts, offsets, perm, active, n_active, error_word};
+  return plan_pairs(ids, n_pairs, E, o, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+size_t moe_plan_workspace_bytes(int n_pairs, int E) { return plan_workspace_bytes(n_pairs, E); }
+
+const char* moe_version(void) { return "moe_b200 0.1 (sm_100a)"; }
+
+}  // extern "C"

@@ -1,0 +1,133 @@
+// moe_common.cuh — shared device helpers of libmoe_b200.so (sm_100a only).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "moe_b200.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "libmoe_b200 is built for sm_100a only"
+#endif
+
+namespace moe {
+
+// ---- host-side error plumbing --------------------------------------------------------------
+
+void set_error(const std::string& msg);
+moe_status fail(moe_status st, const std::string& msg);
+moe_status cuda_fail(cudaError_t e, const char* what);
+
+#define MOE_CUDA_TRY(expr)                                   \
+  do {                                                       \
+    cudaError_t _e = (expr);                                 \
+    if (_e != cudaSuccess) return ::moe::cuda_fail(_e, #expr); \
+  } while (0)
+
+#define MOE_TRY(expr)                      \
+  do {                                     \
+    moe_status _s = (expr);                \
+    if (_s != MOE_OK) return _s;           \
+  } while (0)
+
+inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+// ---- device helpers -------------------------------------------------------------------------
+
+constexpr unsigned FULL = 0xffffffffu;
+
+// Deterministic exp, bit-identical to the CPU oracle's orc_exp: Cody-Waite reduction with a
+// two-constant ln2 split, the degree-7 Taylor polynomial of e^r in Horner form with fused
+// multiply-adds, then exact scaling by 2^n. Every operation is an explicitly rounded intrinsic so
+// the compiler cannot contract or reorder it.
+__device__ __forceinline__ float det_exp(float x) {
+  if (x != x) return x;
+  if (x > 0x1.62e430p+6f) return __int_as_float(0x7f800000);
+  if (x < -104.0f) return 0.0f;
+  float n = rintf(__fmul_rn(x, 0x1.715476p+0f));
+  float r = __fmaf_rn(-n, 0x1.62e400p-1f, x);
+  r = __fmaf_rn(-n, 0x1.7f7d1cp-20f, r);
+  float p = 0x1.a01a02p-13f;
+  p = __fmaf_rn(p, r, 0x1.6c16c2p-10f);
+  p = __fmaf_rn(p, r, 0x1.111112p-7f);
+  p = __fmaf_rn(p, r, 0x1.555556p-5f);
+  p = __fmaf_rn(p, r, 0x1.555556p-3f);
+  p = __fmaf_rn(p, r, 0x1.000000p-1f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  int ni = (int)n;
+  if (ni > 127) { p = __fmul_rn(p, 0x1p127f); ni -= 127; }
+  if (ni < -126) { p = __fmul_rn(p, 0x1p-64f); ni += 64; }
+  return __fmul_rn(p, __int_as_float((ni + 127) << 23));
+}
+
+__device__ __forceinline__ float det_sigmoid(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, det_exp(-x))); }
+
+// Rust f32::total_cmp order as an unsigned key (larger key = later in the order).
+__device__ __forceinline__ uint32_t total_key_u(float f) {
+  int32_t b = __float_as_int(f);
+  b ^= (int32_t)(((uint32_t)(b >> 31)) >> 1);
+  return (uint32_t)b ^ 0x80000000u;
+}
+
+// Streaming 16-byte load that does not allocate in L1 (weights are read once per launch).
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint4 ldg_nc(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint4 lds128(const void* p) {
+  uint4 v;
+  uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+
+// D = A(16x16, row) * B(16x8, col) + C, f32 accumulate (warp-level tensor-core MMA).
+__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL, v, o));
+  return v;
+}
+
+}  // namespace moe

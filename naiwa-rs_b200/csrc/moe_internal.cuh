@@ -1,0 +1,64 @@
+// moe_internal.cuh — kernel parameter blocks and launchers shared between translation units.
+#pragma once
+#include "moe_common.cuh"
+
+namespace moe {
+
+struct RouteParams {
+  const __nv_bfloat16* x;  // [T, H]
+  const __nv_bfloat16* w;  // [E, H]
+  const float* bias;       // [E] or null
+  uint32_t* ids;           // [T, k]
+  float* weights;          // [T, k]
+  int T, H, E, k, mode, n_group, topk_group;
+  float routed_scale;
+};
+moe_status route_tokens(const RouteParams& p, cudaStream_t st);
+
+struct PlanOut {
+  int32_t* counts;    // [E]
+  int32_t* offsets;   // [E+1]
+  int32_t* perm;      // [n_pairs]
+  int32_t* active;    // [E]
+  int32_t* n_active;  // [1]
+  int32_t* err;       // [1] or null
+};
+moe_status plan_pairs(const uint32_t* ids, int n_pairs, int E, const PlanOut& o, void* ws, size_t ws_bytes,
+                      cudaStream_t st);
+size_t plan_workspace_bytes(int n_pairs, int E);
+
+struct ExpertParams {
+  const uint8_t* wq;   // fragment-native weights, expert-major
+  const uint8_t* wsc;  // Q8_0 scales (null for BF16)
+  int64_t q_stride;    // bytes per expert
+  int64_t s_stride;
+  int N;               // device rows (gate/up: 2I with 8+8 interleave; down: H)
+  int K;               // columns (gate/up: H; down: I)
+  int tiles;           // N / 16
+  int kb_count;        // K / 32
+  int phase;           // 0: gate/up (+SwiGLU) -> h ; 1: down (* w) -> ypair
+  int tpp;             // tokens per pass, multiple of 8, <= 32
+  int width;           // pairs per token
+  int n_pairs;
+  const __nv_bfloat16* x;     // phase 0: [T, K] bf16 activations
+  const float* h_in;          // phase 1: [n_pairs (sorted), K] f32
+  const float* route_w;       // phase 1: [n_pairs] routing weights (pair order)
+  float* out;                 // phase 0: h [n_pairs (sorted), N/2]; phase 1: ypair [n_pairs, N]
+  const int32_t* offsets;     // [E+1]
+  const int32_t* perm;        // [n_pairs] sorted position -> pair
+  const int32_t* active;      // [E]
+  const int32_t* n_active;    // [1]
+  int units_per_expert;
+};
+moe_status launch_expert_gemv(int wdtype, ExpertParams p, int max_active, int rowt, cudaStream_t st);
+moe_status launch_combine(const float* ypair, const uint32_t* ids, int T, int width, int H, int E, void* y,
+                          cudaStream_t st);
+int choose_tpp(int K);
+size_t expert_smem_bytes(int K, int tpp);
+
+int64_t device_q_bytes(int wdtype, int N, int K);
+int64_t device_s_bytes(int wdtype, int N, int K);
+moe_status repack_projection(int wdtype, const uint8_t* a, const uint8_t* b, int E, int N_src, int K, uint8_t* dq,
+                             uint8_t* ds, cudaStream_t st);
+
+}  // namespace moe

@@ -1,0 +1,220 @@
+// plan.cu — expert histogram + stable token->expert permutation of the routed pairs.
+//
+// The reference groups routed pairs per expert on the host: per bank in pair order in Gpu::submit
+// (src/moe/stages/gpu.rs:103-132), per row in input order in rings::group_rows
+// (src/moe/rings.rs:146-156); the grouped kernels of its fork sort again on the device. Here the
+// grouping is one stable counting sort on the device: pair p = t*width + j goes to position
+// offsets[id_p] + (number of earlier pairs with the same id). The result is a pure function of the
+// ids, so it is bit-exact against the oracle's orc_permute.
+//
+// Ranks inside a chunk of 1024 pairs come from __match_any_sync (lanes with the same id) plus an
+// exclusive prefix of per-warp counts over the warps in order; chunks are laid end to end in
+// order. Small calls (decode) run the whole plan in one CTA; large ones (prefill, EP dispatch) use
+// a histogram / scan / scatter kernel triple over chunk-private counts.
+#include "moe_internal.cuh"
+
+namespace moe {
+
+constexpr int PLAN_THREADS = 1024;
+constexpr int PLAN_WARPS = PLAN_THREADS / 32;
+constexpr int PLAN_CHUNK = PLAN_THREADS;
+constexpr int PLAN_MAX_E = 1024;
+constexpr int PLAN_SINGLE_MAX = 8 * PLAN_CHUNK;
+
+// Exclusive scan of v over the block (blockDim.x == 1024), returns the prefix, *total the sum.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(FULL, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int s = warp_sums[lane];
+    int z = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(FULL, z, o);
+      if (lane >= o) z += y;
+    }
+    warp_sums[lane] = z - s;  // exclusive warp base
+    if (lane == 31) warp_sums[32] = z;
+  }
+  __syncthreads();
+  int r = x - v + warp_sums[warp];
+  *total = warp_sums[32];
+  __syncthreads();
+  return r;
+}
+
+// Ranks the pairs of one chunk [c0, c0 + 1024) stably and scatters them to perm.
+// base[e]: first free position of expert e before this chunk (advanced by the chunk's counts).
+// whist: [PLAN_WARPS][E] shared scratch.
+__device__ __forceinline__ void rank_chunk(const uint32_t* __restrict__ ids, int n_pairs, int E, int c0,
+                                           int* base, int* whist, int32_t* __restrict__ perm) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < PLAN_WARPS * E; i += PLAN_THREADS) whist[i] = 0;
+  __syncthreads();
+  const int p = c0 + threadIdx.x;
+  const bool valid = p < n_pairs;
+  uint32_t id = valid ? ids[p] : 0xffffffffu;
+  const bool good = valid && id < (uint32_t)E;
+  unsigned grp = __match_any_sync(FULL, good ? id : 0xfffffffeu);
+  const int lrank = __popc(grp & ((1u << lane) - 1u));
+  if (good && lrank == 0) whist[warp * E + id] = __popc(grp);
+  __syncthreads();
+  // exclusive prefix over warps for every expert; the chunk total advances base
+  for (int e = threadIdx.x; e < E; e += PLAN_THREADS) {
+    int run = 0;
+    for (int w = 0; w < PLAN_WARPS; ++w) {
+      int c = whist[w * E + e];
+      whist[w * E + e] = run;
+      run += c;
+    }
+    whist[PLAN_WARPS * E + e] = run;  // chunk count of e (one extra row of scratch)
+  }
+  __syncthreads();
+  if (good) perm[base[id] + whist[warp * E + id] + lrank] = p;
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += PLAN_THREADS) base[e] += whist[PLAN_WARPS * E + e];
+  __syncthreads();
+}
+
+
+// Whole plan in one CTA (n_pairs <= PLAN_SINGLE_MAX).
+__global__ void __launch_bounds__(PLAN_THREADS) plan_single_kernel(const uint32_t* __restrict__ ids, int n_pairs,
+                                                                    int E, PlanOut o) {
+  extern __shared__ int psm[];
+  int* cnt = psm;                      // [E]
+  int* base = cnt + PLAN_MAX_E;        // [E]
+  int* wsum = base + PLAN_MAX_E;       // [33]
+  int* whist = wsum + 64;              // [(PLAN_WARPS + 1) * E]
+  for (int e = threadIdx.x; e < E; e += PLAN_THREADS) cnt[e] = 0;
+  __syncthreads();
+  int bad = 0;
+  for (int p = threadIdx.x; p < n_pairs; p += PLAN_THREADS) {
+    uint32_t id = ids[p];
+    if (id < (uint32_t)E) atomicAdd(&cnt[id], 1);
+    else bad = 1;
+  }
+  if (bad && o.err) atomicExch(o.err, (int)MOE_ERR_BAD_IDS);
+  __syncthreads();
+  // offsets (exclusive scan of counts) and the active list (scan of count > 0), E <= 1024
+  int c = threadIdx.x < E ? cnt[threadIdx.x] : 0;
+  int total;
+  int off = block_exclusive_scan(c, wsum, &total);
+  int a = block_exclusive_scan(c > 0 ? 1 : 0, wsum, &total);
+  if (threadIdx.x < E) {
+    o.counts[threadIdx.x] = c;
+    o.offsets[threadIdx.x] = off;
+    base[threadIdx.x] = off;
+    if (c > 0) o.active[a] = threadIdx.x;
+  }
+  if (threadIdx.x == E - 1) o.offsets[E] = off + c;
+  if (threadIdx.x == 0) *o.n_active = total;
+  __syncthreads();
+  for (int c0 = 0; c0 < n_pairs; c0 += PLAN_CHUNK) rank_chunk(ids, n_pairs, E, c0, base, whist, o.perm);
+}
+
+// Large plans: per-chunk histograms -> scan -> per-chunk stable scatter.
+__global__ void __launch_bounds__(PLAN_THREADS) plan_hist_kernel(const uint32_t* __restrict__ ids, int n_pairs, int E,
+                                                                  int32_t* __restrict__ chunk_counts, int32_t* err) {
+  extern __shared__ int psm[];
+  for (int e = threadIdx.x; e < E; e += PLAN_THREADS) psm[e] = 0;
+  __syncthreads();
+  const int p = blockIdx.x * PLAN_CHUNK + threadIdx.x;
+  if (p < n_pairs) {
+    uint32_t id = ids[p];
+    if (id < (uint32_t)E) atomicAdd(&psm[id], 1);
+    else if (err) atomicExch(err, (int)MOE_ERR_BAD_IDS);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += PLAN_THREADS) chunk_counts[(size_t)blockIdx.x * E + e] = psm[e];
+}
+
+__global__ void __launch_bounds__(PLAN_THREADS) plan_scan_kernel(int n_chunks, int E, int32_t* __restrict__ chunk_counts,
+                                                                  PlanOut o) {
+  __shared__ int wsum[64];
+  const int e = threadIdx.x;
+  int total_e = 0;
+  if (e < E)
+    for (int c = 0; c < n_chunks; ++c) total_e += chunk_counts[(size_t)c * E + e];
+  int total;
+  int off = block_exclusive_scan(total_e, wsum, &total);
+  int a = block_exclusive_scan(total_e > 0 ? 1 : 0, wsum, &total);
+  if (e < E) {
+    o.counts[e] = total_e;
+    o.offsets[e] = off;
+    if (total_e > 0) o.active[a] = e;
+    int run = off;  // chunk bases in place
+    for (int c = 0; c < n_chunks; ++c) {
+      int v = chunk_counts[(size_t)c * E + e];
+      chunk_counts[(size_t)c * E + e] = run;
+      run += v;
+    }
+  }
+  if (e == E - 1) o.offsets[E] = off + total_e;
+  if (e == 0) *o.n_active = total;
+}
+
+__global__ void __launch_bounds__(PLAN_THREADS) plan_scatter_kernel(const uint32_t* __restrict__ ids, int n_pairs, int E,
+                                                                     const int32_t* __restrict__ chunk_base,
+                                                                     int32_t* __restrict__ perm) {
+  extern __shared__ int psm[];
+  int* base = psm;                 // [E]
+  int* whist = psm + PLAN_MAX_E;   // [(PLAN_WARPS + 1) * E]
+  for (int e = threadIdx.x; e < E; e += PLAN_THREADS) base[e] = chunk_base[(size_t)blockIdx.x * E + e];
+  __syncthreads();
+  rank_chunk(ids, n_pairs, E, blockIdx.x * PLAN_CHUNK, base, whist, perm);
+}
+
+size_t plan_workspace_bytes(int n_pairs, int E) {
+  if (n_pairs <= PLAN_SINGLE_MAX) return 0;
+  return (size_t)ceil_div(n_pairs, PLAN_CHUNK) * E * sizeof(int32_t);
+}
+
+static size_t single_smem(int E) { return (size_t)(2 * PLAN_MAX_E + 64 + (PLAN_WARPS + 1) * E) * sizeof(int); }
+static size_t scatter_smem(int E) { return (size_t)(PLAN_MAX_E + (PLAN_WARPS + 1) * E) * sizeof(int); }
+
+moe_status plan_pairs(const uint32_t* ids, int n_pairs, int E, const PlanOut& o, void* ws, size_t ws_bytes,
+                      cudaStream_t st) {
+  if (E <= 0 || E > PLAN_MAX_E) return fail(MOE_ERR_INVALID, "moe_plan_pairs: need 0 < E <= 1024");
+  if (n_pairs < 0) return fail(MOE_ERR_INVALID, "moe_plan_pairs: n_pairs < 0");
+  if (!o.counts || !o.offsets || !o.perm || !o.active || !o.n_active)
+    return fail(MOE_ERR_INVALID, "moe_plan_pairs: null output");
+  if (n_pairs > 0 && !ids) return fail(MOE_ERR_INVALID, "moe_plan_pairs: null ids");
+  if (((uintptr_t)ids | (uintptr_t)o.counts | (uintptr_t)o.offsets | (uintptr_t)o.perm | (uintptr_t)o.active |
+       (uintptr_t)o.n_active | (uintptr_t)o.err) & 3)
+    return fail(MOE_ERR_INVALID, "moe_plan_pairs: arrays must be 4-byte aligned");
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev & 63]) {
+    MOE_CUDA_TRY(cudaFuncSetAttribute(plan_single_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)single_smem(PLAN_MAX_E)));
+    MOE_CUDA_TRY(cudaFuncSetAttribute(plan_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)scatter_smem(PLAN_MAX_E)));
+    attr_done[dev & 63] = true;
+  }
+  if (n_pairs <= PLAN_SINGLE_MAX) {
+    plan_single_kernel<<<1, PLAN_THREADS, single_smem(E), st>>>(ids, n_pairs, E, o);
+    MOE_CUDA_TRY(cudaGetLastError());
+    return MOE_OK;
+  }
+  const int n_chunks = ceil_div(n_pairs, PLAN_CHUNK);
+  if (!ws || ws_bytes < plan_workspace_bytes(n_pairs, E))
+    return fail(MOE_ERR_INVALID, "moe_plan_pairs: workspace too small");
+  int32_t* chunk = static_cast<int32_t*>(ws);
+  plan_hist_kernel<<<n_chunks, PLAN_THREADS, E * sizeof(int), st>>>(ids, n_pairs, E, chunk, o.err);
+  MOE_CUDA_TRY(cudaGetLastError());
+  plan_scan_kernel<<<1, PLAN_THREADS, 0, st>>>(n_chunks, E, chunk, o);
+  MOE_CUDA_TRY(cudaGetLastError());
+  plan_scatter_kernel<<<n_chunks, PLAN_THREADS, scatter_smem(E), st>>>(ids, n_pairs, E, chunk, o.perm);
+  MOE_CUDA_TRY(cudaGetLastError());
+  return MOE_OK;
+}
+
+}  // namespace moe

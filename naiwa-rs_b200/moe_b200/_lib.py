@@ -1,0 +1,105 @@
+"""ctypes binding of libmoe_b200.so (the C ABI declared in include/moe_b200.h).
+
+The library is the product: every entry point here calls sm_100a kernels. If the shared library
+is missing or fails to load, importing this module raises; there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+from . import _build
+
+MOE_OK = 0
+MOE_ERR_INVALID = 1
+MOE_ERR_CUDA = 2
+MOE_ERR_OOM = 3
+MOE_ERR_TIMEOUT = 4
+MOE_ERR_BAD_IDS = 5
+MOE_ERR_UNSUPPORTED = 6
+MOE_ERR_WORKER = 7
+
+STATUS_NAMES = {
+    0: "MOE_OK", 1: "MOE_ERR_INVALID", 2: "MOE_ERR_CUDA", 3: "MOE_ERR_OOM", 4: "MOE_ERR_TIMEOUT",
+    5: "MOE_ERR_BAD_IDS", 6: "MOE_ERR_UNSUPPORTED", 7: "MOE_ERR_WORKER",
+}
+
+DTYPE_BF16, DTYPE_Q8_0, DTYPE_Q4_K, DTYPE_FP8_E4M3_B128 = 0, 1, 2, 3
+ROUTER_SOFTMAX, ROUTER_SOFTMAX_RENORM, ROUTER_SIGMOID_GROUP = 0, 1, 2
+
+
+class MoeError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {msg}")
+        self.status = status
+
+
+class LayerDesc(ctypes.Structure):
+    _fields_ = [
+        ("num_experts", ctypes.c_int),
+        ("top_k", ctypes.c_int),
+        ("hidden", ctypes.c_int),
+        ("inter", ctypes.c_int),
+        ("wdtype", ctypes.c_int),
+        ("gate", ctypes.c_void_p),
+        ("up", ctypes.c_void_p),
+        ("down", ctypes.c_void_p),
+        ("gate_scale", ctypes.c_void_p),
+        ("up_scale", ctypes.c_void_p),
+        ("down_scale", ctypes.c_void_p),
+        ("weights_on_device", ctypes.c_int),
+        ("router_weight", ctypes.c_void_p),
+        ("router_bias", ctypes.c_void_p),
+        ("router_mode", ctypes.c_int),
+        ("n_group", ctypes.c_int),
+        ("topk_group", ctypes.c_int),
+        ("routed_scale", ctypes.c_float),
+        ("device", ctypes.c_int),
+        ("max_tokens", ctypes.c_int),
+    ]
+
+
+LIB_PATH = _build.LIB
+_lib = None
+
+
+def lib():
+    """Load libmoe_b200.so (building it first when the sources are newer)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH) or os.environ.get("MOE_B200_REBUILD") == "1":
+            _build.build()
+        L = ctypes.CDLL(LIB_PATH)
+        P, i, f = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+        sigs = {
+            "moe_layer_create": (i, [ctypes.POINTER(LayerDesc), ctypes.POINTER(ctypes.c_void_p)]),
+            "moe_layer_warmup": (i, [P, i]),
+            "moe_route": (i, [P, P, i, P, P, P]),
+            "moe_forward": (i, [P, P, i, P, P, i, P, P]),
+            "moe_forward_marked": (i, [P, P, i, P, P, i, P, P, ctypes.POINTER(ctypes.c_void_p)]),
+            "moe_layer_destroy": (None, [P]),
+            "moe_layer_device_bytes": (ctypes.c_int64, [P]),
+            "moe_layer_check": (i, [P, P]),
+            "moe_last_error": (ctypes.c_size_t, [ctypes.c_char_p, ctypes.c_size_t]),
+            "moe_route_tokens": (i, [P, P, P, i, i, i, i, i, i, i, f, P, P, P]),
+            "moe_plan_pairs": (i, [P, i, i, P, P, P, P, P, P, ctypes.c_size_t, P, P]),
+            "moe_plan_workspace_bytes": (ctypes.c_size_t, [i, i]),
+            "moe_version": (ctypes.c_char_p, []),
+        }
+        for name, (res, args) in sigs.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(1024)
+    lib().moe_last_error(buf, 1024)
+    return buf.value.decode(errors="replace")
+
+
+def check(status: int):
+    if status != MOE_OK:
+        raise MoeError(status, last_error())

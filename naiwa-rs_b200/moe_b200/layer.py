@@ -1,0 +1,258 @@
+"""Host-side mirror of the reference's routed-experts operator interface over libmoe_b200.so.
+
+Reference (naiwa-rs, in its mistral.rs fork's `moe_offload` module):
+  RoutedExpertsProvider::build(&self, ctx: ExpertLoadContext) -> Result<Option<Arc<dyn RoutedExperts>>>
+      src/moe/provider.rs:316-615
+  RoutedExperts::forward(&self, xs, topk_weights, topk_ids) -> Result<Tensor>
+      src/moe/cached_layer.rs:524-664, src/moe/expert.rs:59-117
+
+Argument meaning follows the reference: `xs` is [B, S, H] (or [T, H]) in the model dtype (bf16),
+`topk_weights` [B*S, k] f32, `topk_ids` [B*S, k] u32/int; the result is a new tensor shaped like
+`xs`. Errors raise MoeError (the reference's candle_core::Result bails). Tensors are torch CUDA
+tensors; torch supplies device memory and the current stream, the kernels are the library's.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from typing import Any, Optional
+
+import numpy as np
+
+from . import _lib
+from ._lib import LayerDesc, MoeError, check, lib
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _ptr(t) -> int:
+    return 0 if t is None else int(t.data_ptr())
+
+
+def _stream(stream=None) -> int:
+    torch = _torch()
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return int(stream.cuda_stream)
+
+
+@dataclass
+class MoeConfig:
+    """The fields of the reference's ctx.config the operator reads (provider.rs:316-370)."""
+
+    num_experts: int
+    num_experts_per_tok: int
+    hidden_size: int
+    moe_intermediate_size: int
+    router_mode: int = _lib.ROUTER_SOFTMAX_RENORM
+    n_group: int = 1
+    topk_group: int = 1
+    routed_scaling_factor: float = 1.0
+
+
+@dataclass
+class ExpertLoadContext:
+    """What the reference's provider receives per MoE block (provider.rs:316-370): the layer site,
+    its device, the config, and the expert stacks (`expert_qtensors()` -> gate, up, down stacked
+    [E, N, K] in GGML byte layout). Stacks may be host numpy uint8 arrays or CUDA uint8 tensors."""
+
+    layer: int
+    device: int
+    config: MoeConfig
+    wdtype: int
+    gate: Any
+    up: Any
+    down: Any
+    gate_scale: Any = None
+    up_scale: Any = None
+    down_scale: Any = None
+    router_weight: Any = None  # [E, H] bf16 (torch tensor or numpy uint16)
+    router_bias: Any = None    # [E] f32
+    max_tokens: int = 256
+    _keep: list = field(default_factory=list)
+
+
+def _as_ptr(obj, keep: list, on_device: bool):
+    """Raw pointer of a numpy array or torch tensor; numpy arrays are kept alive in `keep`."""
+    if obj is None:
+        return None
+    if isinstance(obj, np.ndarray):
+        if on_device:
+            raise MoeError(_lib.MOE_ERR_INVALID, "mixed host and device inputs")
+        a = np.ascontiguousarray(obj)
+        keep.append(a)
+        return a.ctypes.data
+    torch = _torch()
+    if isinstance(obj, torch.Tensor):
+        if obj.is_cuda != on_device:
+            raise MoeError(_lib.MOE_ERR_INVALID, "mixed host and device inputs")
+        t = obj.contiguous()
+        keep.append(t)
+        return t.data_ptr()
+    raise TypeError(type(obj))
+
+
+class RoutedExperts:
+    """One MoE layer's routed experts, resident on a B200 (the reference's CachedExperts with
+    every expert in its cache). Created by RoutedExpertsProvider.build."""
+
+    def __init__(self, ctx: ExpertLoadContext):
+        torch = _torch()
+        cfg = ctx.config
+        self.layer = ctx.layer
+        self.device = ctx.device
+        self.config = cfg
+        self.hidden = cfg.hidden_size
+        self.top_k = cfg.num_experts_per_tok
+        self.num_experts = cfg.num_experts
+        self.wdtype = ctx.wdtype
+        on_dev = isinstance(ctx.gate, torch.Tensor) and ctx.gate.is_cuda
+        keep: list = []
+        d = LayerDesc()
+        d.num_experts = cfg.num_experts
+        d.top_k = cfg.num_experts_per_tok
+        d.hidden = cfg.hidden_size
+        d.inter = cfg.moe_intermediate_size
+        d.wdtype = ctx.wdtype
+        d.gate = _as_ptr(ctx.gate, keep, on_dev)
+        d.up = _as_ptr(ctx.up, keep, on_dev)
+        d.down = _as_ptr(ctx.down, keep, on_dev)
+        d.gate_scale = _as_ptr(ctx.gate_scale, keep, on_dev)
+        d.up_scale = _as_ptr(ctx.up_scale, keep, on_dev)
+        d.down_scale = _as_ptr(ctx.down_scale, keep, on_dev)
+        d.weights_on_device = 1 if on_dev else 0
+        d.router_weight = _as_ptr(ctx.router_weight, keep, on_dev)
+        d.router_bias = _as_ptr(ctx.router_bias, keep, on_dev)
+        d.router_mode = cfg.router_mode
+        d.n_group = cfg.n_group
+        d.topk_group = cfg.topk_group
+        d.routed_scale = cfg.routed_scaling_factor
+        d.device = ctx.device
+        d.max_tokens = ctx.max_tokens
+        handle = ctypes.c_void_p()
+        if on_dev:
+            torch.cuda.synchronize(ctx.device)
+        check(lib().moe_layer_create(ctypes.byref(d), ctypes.byref(handle)))
+        self._h = handle
+        self.max_tokens = ctx.max_tokens
+
+    # -- lifecycle ------------------------------------------------------------------------------
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            lib().moe_layer_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def warmup(self, max_tokens: int):
+        """Size scratch for `max_tokens` (the reference's provider warmup, provider.rs:192-303)."""
+        check(lib().moe_layer_warmup(self._h, int(max_tokens)))
+        self.max_tokens = max(self.max_tokens, int(max_tokens))
+
+    def device_bytes(self) -> int:
+        return int(lib().moe_layer_device_bytes(self._h))
+
+    def check(self, stream=None):
+        """Raise MoeError when a previous forward latched a device-side error (bad ids)."""
+        check(lib().moe_layer_check(self._h, ctypes.c_void_p(_stream(stream))))
+
+    # -- the operator -------------------------------------------------------------------------------
+    def route(self, xs, out_ids=None, out_weights=None, stream=None):
+        """Router + top-k for xs [.., H] bf16 -> (ids [T, k] int32 view of u32, weights [T, k] f32)."""
+        torch = _torch()
+        x2 = xs.reshape(-1, self.hidden)
+        if x2.dtype != torch.bfloat16 or not x2.is_cuda:
+            raise MoeError(_lib.MOE_ERR_INVALID, "route: xs must be a CUDA bf16 tensor")
+        x2 = x2.contiguous()
+        T = x2.shape[0]
+        ids = out_ids if out_ids is not None else torch.empty((T, self.top_k), dtype=torch.int32, device=x2.device)
+        w = out_weights if out_weights is not None else torch.empty((T, self.top_k), dtype=torch.float32,
+                                                                    device=x2.device)
+        check(lib().moe_route(self._h, _ptr(x2), T, _ptr(ids), _ptr(w), ctypes.c_void_p(_stream(stream))))
+        return ids, w
+
+    def forward(self, xs, topk_weights, topk_ids, out=None, stream=None):
+        """sum_j topk_weights[t, j] * expert(topk_ids[t, j])(xs[t]) for every token, in xs's shape."""
+        torch = _torch()
+        shape = xs.shape
+        x2 = xs.reshape(-1, self.hidden)
+        if x2.dtype != torch.bfloat16 or not x2.is_cuda:
+            raise MoeError(_lib.MOE_ERR_INVALID, "forward: xs must be a CUDA bf16 tensor")
+        x2 = x2.contiguous()
+        T = x2.shape[0]
+        ids = topk_ids.reshape(T, -1)
+        if ids.dtype not in (torch.int32, torch.uint32) or not ids.is_cuda:
+            ids = ids.to(device=x2.device, dtype=torch.int32)
+        ids = ids.contiguous()
+        w = topk_weights.reshape(T, -1)
+        if w.dtype != torch.float32 or not w.is_cuda:
+            w = w.to(device=x2.device, dtype=torch.float32)
+        w = w.contiguous()
+        if w.shape != ids.shape:
+            raise MoeError(_lib.MOE_ERR_INVALID, "forward: topk_weights and topk_ids shapes differ")
+        width = ids.shape[1]
+        y = out if out is not None else torch.empty_like(x2)
+        check(lib().moe_forward(self._h, _ptr(x2), T, _ptr(ids), _ptr(w), width, _ptr(y),
+                                ctypes.c_void_p(_stream(stream))))
+        return y.reshape(shape)
+
+    __call__ = forward
+
+
+class RoutedExpertsProvider:
+    """Builds the per-layer operator (GpuCacheMoeProvider::build, provider.rs:316-615)."""
+
+    def __init__(self):
+        self.layers: dict[int, RoutedExperts] = {}
+
+    def build(self, ctx: ExpertLoadContext) -> Optional[RoutedExperts]:
+        layer = RoutedExperts(ctx)
+        self.layers[ctx.layer] = layer
+        return layer
+
+    def warmup(self, max_tokens: int):
+        for layer in self.layers.values():
+            layer.warmup(max_tokens)
+
+
+# ---- stateless kernels ---------------------------------------------------------------------------
+
+def route_tokens(x, w_router, k: int, mode: int, bias=None, n_group: int = 1, topk_group: int = 1,
+                 routed_scale: float = 1.0, stream=None):
+    """Router logits + top-k without a layer: x [T, H] bf16, w_router [E, H] bf16 (CUDA)."""
+    torch = _torch()
+    T, H = x.shape
+    E = w_router.shape[0]
+    ids = torch.empty((T, k), dtype=torch.int32, device=x.device)
+    w = torch.empty((T, k), dtype=torch.float32, device=x.device)
+    check(lib().moe_route_tokens(_ptr(x.contiguous()), _ptr(w_router.contiguous()), _ptr(bias), T, H, E, k, mode,
+                                 n_group, topk_group, float(routed_scale), _ptr(ids), _ptr(w),
+                                 ctypes.c_void_p(_stream(stream))))
+    return ids, w
+
+
+def plan_pairs(ids, num_experts: int, stream=None):
+    """Histogram + stable permutation of routed pairs -> (counts, offsets, perm, active, error_word)."""
+    torch = _torch()
+    flat = ids.reshape(-1).to(torch.int32).contiguous()
+    n = flat.numel()
+    dev = flat.device
+    counts = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    offsets = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
+    perm = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+    active = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    n_active = torch.zeros(1, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws_bytes = int(lib().moe_plan_workspace_bytes(n, num_experts))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    check(lib().moe_plan_pairs(_ptr(flat), n, num_experts, _ptr(counts), _ptr(offsets), _ptr(perm), _ptr(active),
+                               _ptr(n_active), _ptr(ws), ws_bytes, _ptr(err), ctypes.c_void_p(_stream(stream))))
+    return counts, offsets, perm[:n], active, n_active, err
