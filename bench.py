@@ -262,8 +262,9 @@ def run_ours(args):
     with torch.cuda.graph(graph, stream=stream):
         sweep()
     torch.cuda.synchronize()
-    for _ in range(args.warmup):
-        graph.replay()
+    with torch.cuda.stream(stream):  # replays run on the current stream
+        for _ in range(args.warmup):
+            graph.replay()
     torch.cuda.synchronize()
 
     def barrier():
@@ -275,10 +276,11 @@ def run_ours(args):
         barrier()
         torch.cuda.synchronize()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ev0.record(stream)
-        for _ in range(args.steps):
-            graph.replay()
-        ev1.record(stream)
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            ev1.record(stream)
         torch.cuda.synchronize()
         barrier()
         ms = ev0.elapsed_time(ev1) / args.steps
@@ -328,7 +330,8 @@ def run_ours(args):
     with torch.cuda.graph(mgraph, stream=stream):
         marked_sweep()
     torch.cuda.synchronize()
-    mgraph.replay()
+    with torch.cuda.stream(stream):
+        mgraph.replay()
     torch.cuda.synchronize()
     stage = {"plan": 0.0, "gate_up": 0.0, "down": 0.0, "combine": 0.0}
     per_T_expert_ms = {T: 0.0 for T in RAGGED}

@@ -7,15 +7,19 @@
 //
 // Work decomposition (B200): one CTA = 8 warps works on one (active expert, chunk of ROWT row
 // tiles of 16 rows). KS = 8 / ROWT warps split the K dimension of each row tile and meet in
-// shared memory. Each warp streams its weight fragments straight from HBM into registers with
-// 16-byte non-allocating loads: the device weight layout is fragment-native, i.e. lane l's 16
-// bytes of a (16-row tile, 32-column block) are exactly its A operand for two m16n8k16 tensor-core
-// MMAs, so a warp reads 512 contiguous bytes per load instruction and never reshuffles. The
-// expert's tokens (up to 32 per pass) sit in shared memory in B-fragment order and are reused by
-// every row tile of the CTA. Q8_0 dequantises in registers to f16 (int8 -> f16 by the 0x6400
-// exponent trick, minus the 1152 bias, times the block's f16 scale); activations are staged as f16
-// with a per-token power-of-two scale, so nothing overflows f16 and the scale is undone exactly
-// in the epilogue. BF16 weights feed bf16 MMAs directly.
+// shared memory (KS = 1 keeps everything in registers). Each warp streams its weight fragments
+// straight from HBM into registers with 16-byte non-allocating loads, three groups of four
+// 32-column blocks in flight: the device weight layout is fragment-native, i.e. lane l's 16 bytes
+// of a (16-row tile, 32-column block) are exactly its A operand for two m16n8k16 tensor-core MMAs,
+// so a warp reads 512 contiguous bytes per load instruction and never reshuffles. The expert's
+// tokens (up to 32 per pass) are staged once per CTA into shared memory in B-fragment order, one
+// warp per token row with 16-byte loads, and reused by every row tile of the CTA.
+//
+// Precision: Q8_0 quants enter the MMA as exact f16 integers (int8 -> f16 through the 0x6400
+// exponent trick minus the 1152 bias) and each block's f16 scale is applied in f32 to the MMA
+// partial sum, so the weights are never rounded. Activations are staged as f16 with a per-token
+// power-of-two scale (a bf16 value scaled into f16's range is exact); the scale is undone in the
+// epilogue. BF16 weights feed bf16 MMAs with bf16 activations unchanged.
 #include "moe_internal.cuh"
 
 namespace moe {
@@ -24,63 +28,180 @@ constexpr int EXP_THREADS = 256;
 constexpr int EXP_WARPS = 8;
 constexpr int MAX_TPP = 32;  // tokens per pass (4 n-tiles of 8)
 
+// ---- weight fragment streams ---------------------------------------------------------------------
 
-// ---- weight fragment decoders -----------------------------------------------------------------
-
+// Q8_0: per (tile, block) 512 B of quants; per (tile, group of 4 blocks) 128 B of scales holding
+// {d(row g), d(row g+8)} for the 4 blocks at byte g*16.
 struct WQ8 {
   static constexpr bool kF16 = true;
-  // 512 B per (tile, block); scales: per (tile, group of 4 blocks) 8 rows x 4 blocks x {s_g, s_g+8}
-  __device__ static __forceinline__ const uint8_t* qptr(const ExpertParams& p, int e, int tile, int kb, int lane) {
-    return p.wq + (int64_t)e * p.q_stride + ((int64_t)tile * p.kb_count + kb) * 512 + lane * 16;
+  static constexpr int GROUP = 4;  // blocks per pipeline stage
+  struct Stage {
+    uint4 q[GROUP];
+    uint4 s;
+  };
+  __device__ static __forceinline__ void load(const ExpertParams& p, int e, int tile, int kb0, int kb_end, int lane,
+                                              Stage& st) {
+    const uint8_t* qb = p.wq + (int64_t)e * p.q_stride + ((int64_t)tile * p.kb_count + kb0) * 512 + lane * 16;
+#pragma unroll
+    for (int u = 0; u < GROUP; ++u)
+      if (kb0 + u < kb_end) st.q[u] = ldg_stream(qb + u * 512);
+    if (kb0 < kb_end) {
+      const int kbg_count = (p.kb_count + 3) >> 2;
+      st.s = ldg_stream(p.wsc + (int64_t)e * p.s_stride + ((int64_t)tile * kbg_count + (kb0 >> 2)) * 128 +
+                        (lane >> 2) * 16);
+    }
   }
-  __device__ static __forceinline__ const uint8_t* sptr(const ExpertParams& p, int e, int tile, int kbg, int lane) {
-    const int kbg_count = (p.kb_count + 3) >> 2;
-    return p.wsc + (int64_t)e * p.s_stride + ((int64_t)tile * kbg_count + kbg) * 128 + (lane >> 2) * 16;
-  }
-  // q: the lane's 16 quant bytes of one block; s2: {s_g, s_g+8} of that block (f16x2)
-  __device__ static __forceinline__ void decode(uint4 q, uint32_t s2, uint32_t (&a0)[4], uint32_t (&a1)[4]) {
-    const __half2 sg = __half2half2(__low2half(*reinterpret_cast<__half2*>(&s2)));
-    const __half2 sh = __half2half2(__high2half(*reinterpret_cast<__half2*>(&s2)));
+  // exact int8 -> f16 of the lane's 16 quant bytes: a0 (k16 step 0), a1 (step 1)
+  __device__ static __forceinline__ void quants(uint4 q, uint32_t (&a0)[4], uint32_t (&a1)[4]) {
     const __half2 bias = __float2half2_rn(1152.0f);
-    uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
-    uint32_t* dst[2] = {a0, a1};
+    const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
+      uint32_t* dst = s ? a1 : a0;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        uint32_t word = w[2 * s + h];
-        uint32_t lo = __byte_perm(word, 0x64646464u, 0x4140);  // (row g)   1024 + u
-        uint32_t hi = __byte_perm(word, 0x64646464u, 0x4342);  // (row g+8) 1024 + u
+        uint32_t lo = __byte_perm(w[2 * s + h], 0x64646464u, 0x4140);  // row g:   1024 + u
+        uint32_t hi = __byte_perm(w[2 * s + h], 0x64646464u, 0x4342);  // row g+8: 1024 + u
         __half2 vlo = __hsub2(*reinterpret_cast<__half2*>(&lo), bias);
         __half2 vhi = __hsub2(*reinterpret_cast<__half2*>(&hi), bias);
-        vlo = __hmul2(vlo, sg);
-        vhi = __hmul2(vhi, sh);
-        dst[s][2 * h + 0] = *reinterpret_cast<uint32_t*>(&vlo);
-        dst[s][2 * h + 1] = *reinterpret_cast<uint32_t*>(&vhi);
+        dst[2 * h + 0] = *reinterpret_cast<uint32_t*>(&vlo);
+        dst[2 * h + 1] = *reinterpret_cast<uint32_t*>(&vhi);
+      }
+    }
+  }
+  template <int NTM>
+  __device__ static __forceinline__ void compute(const Stage& st, int kb0, int kb_end, const uint32_t* xs, int ntm,
+                                                 int nt_used, int lane, float (&acc)[NTM][4]) {
+    const uint32_t sw[4] = {st.s.x, st.s.y, st.s.z, st.s.w};
+#pragma unroll
+    for (int u = 0; u < GROUP; ++u) {
+      const int kb = kb0 + u;
+      if (kb >= kb_end) break;
+      uint32_t a0[4], a1[4];
+      quants(st.q[u], a0, a1);
+      const __half2 s2 = *reinterpret_cast<const __half2*>(&sw[u]);
+      const float slo = __low2float(s2), shi = __high2float(s2);
+#pragma unroll
+      for (int t = 0; t < NTM; ++t) {
+        if (t < nt_used) {
+          uint4 b = lds128(xs + ((kb * ntm + t) * 32 + lane) * 4);
+          float tmp[4] = {0.f, 0.f, 0.f, 0.f};
+          mma_f16(tmp, a0, b.x, b.y);
+          mma_f16(tmp, a1, b.z, b.w);
+          acc[t][0] = fmaf(slo, tmp[0], acc[t][0]);
+          acc[t][1] = fmaf(slo, tmp[1], acc[t][1]);
+          acc[t][2] = fmaf(shi, tmp[2], acc[t][2]);
+          acc[t][3] = fmaf(shi, tmp[3], acc[t][3]);
+        }
       }
     }
   }
 };
 
+// BF16: per (tile, block) 1 KB = two k16 steps of 512 B; lane's 16 B = its 8 A values.
 struct WBF16 {
   static constexpr bool kF16 = false;
-  // 1 KB per (tile, block): two k16 steps of 512 B, lane's 16 B = its 8 A values.
-  __device__ static __forceinline__ const uint8_t* qptr(const ExpertParams& p, int e, int tile, int kb, int lane) {
-    return p.wq + (int64_t)e * p.q_stride + ((int64_t)tile * p.kb_count + kb) * 1024 + lane * 16;
+  static constexpr int GROUP = 2;
+  struct Stage {
+    uint4 q[GROUP][2];
+  };
+  __device__ static __forceinline__ void load(const ExpertParams& p, int e, int tile, int kb0, int kb_end, int lane,
+                                              Stage& st) {
+    const uint8_t* qb = p.wq + (int64_t)e * p.q_stride + ((int64_t)tile * p.kb_count + kb0) * 1024 + lane * 16;
+#pragma unroll
+    for (int u = 0; u < GROUP; ++u)
+      if (kb0 + u < kb_end) {
+        st.q[u][0] = ldg_stream(qb + u * 1024);
+        st.q[u][1] = ldg_stream(qb + u * 1024 + 512);
+      }
+  }
+  template <int NTM>
+  __device__ static __forceinline__ void compute(const Stage& st, int kb0, int kb_end, const uint32_t* xs, int ntm,
+                                                 int nt_used, int lane, float (&acc)[NTM][4]) {
+#pragma unroll
+    for (int u = 0; u < GROUP; ++u) {
+      const int kb = kb0 + u;
+      if (kb >= kb_end) break;
+      const uint32_t a0[4] = {st.q[u][0].x, st.q[u][0].y, st.q[u][0].z, st.q[u][0].w};
+      const uint32_t a1[4] = {st.q[u][1].x, st.q[u][1].y, st.q[u][1].z, st.q[u][1].w};
+#pragma unroll
+      for (int t = 0; t < NTM; ++t) {
+        if (t < nt_used) {
+          uint4 b = lds128(xs + ((kb * ntm + t) * 32 + lane) * 4);
+          mma_bf16(acc[t], a0, b.x, b.y);
+          mma_bf16(acc[t], a1, b.z, b.w);
+        }
+      }
+    }
   }
 };
 
-// ---- staging of the pass's activations into B-fragment order ------------------------------------
-// xs word index of (token n, column pair kp): per (block, n-tile) 32 lanes x 4 words.
-__device__ __forceinline__ int xs_word(int n, int k, int ntm) {
-  const int kb = k >> 5, kk = k & 31, s = kk >> 4, k16 = kk & 15, h = k16 >> 3, c = (k16 & 7) >> 1;
-  const int nt = n >> 3, g = n & 7;
-  return ((kb * ntm + nt) * 32 + g * 4 + c) * 4 + s * 2 + h;
+// ---- staging ------------------------------------------------------------------------------------
+// SMEM layout of the pass's activations: word ((kb * ntm + nt) * 32 + g * 4 + c) * 4 + s * 2 + h
+// holds the (k, k+1) pair k = 32 kb + 16 s + 8 h + 2 c of token 8 nt + g: the B operand of
+// m16n8k16 for lane 4g + c is then one 16-byte load {step0 b0b1, step0 b2b3, step1 b0b1, step1 b2b3}.
+template <bool F16>
+__device__ __forceinline__ void load_chunk(const ExpertParams& p, int src_row, int c, float (&v)[8]) {
+  if (p.phase == 0) {
+    uint4 raw = ldg_nc(p.x + (int64_t)src_row * p.K + c * 8);
+    const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f = __bfloat1622float2(b2[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  } else {
+    const float4* src = reinterpret_cast<const float4*>(p.h_in + (int64_t)src_row * p.K + c * 8);
+    float4 f0 = src[0], f1 = src[1];
+    v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
+    v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+  }
 }
 
-template <class WT, int ROWT>
+// One warp stages one token row: (f16 path) the row's max magnitude gives a power-of-two scale
+// that puts the row in [2^13, 2^14); the second sweep re-reads the row (L1/L2 hit), converts and
+// scatters it into B-fragment order.
+template <bool F16>
+__device__ __forceinline__ void stage_row(const ExpertParams& p, int n, int src_row, uint32_t* xs, int ntm,
+                                          float* tscale, int lane) {
+  const int chunks = p.K >> 3;  // 8 elements per chunk
+  float inv = 1.0f, sc = 1.0f;
+  if (F16) {
+    float m = 0.0f;
+    for (int c = lane; c < chunks; c += 32) {
+      float v[8];
+      load_chunk<F16>(p, src_row, c, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
+    }
+    m = warp_max(m);
+    if (m > 0.0f && m < __int_as_float(0x7f800000)) {
+      int ex;
+      frexpf(m, &ex);  // m < 2^ex
+      const int sh = max(-100, min(100, ex - 14));
+      sc = ldexpf(1.0f, sh);
+      inv = ldexpf(1.0f, -sh);
+    }
+  }
+  if (lane == 0) tscale[n] = sc;
+  const int nt = n >> 3, g = n & 7;
+  for (int c = lane; c < chunks; c += 32) {
+    float v[8];
+    load_chunk<F16>(p, src_row, c, v);
+    const int kb = c >> 2, s = (c >> 1) & 1, h = c & 1;
+    uint32_t* dst = xs + ((kb * ntm + nt) * 32 + g * 4) * 4 + s * 2 + h;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      dst[q * 4] = F16 ? pack_f16x2(v[2 * q] * inv, v[2 * q + 1] * inv) : pack_bf16x2(v[2 * q], v[2 * q + 1]);
+  }
+}
+
+template <class WT, int ROWT, int NTM>
 __global__ void __launch_bounds__(EXP_THREADS, 2) expert_gemv_kernel(ExpertParams p) {
   constexpr int KS = EXP_WARPS / ROWT;
+  constexpr int STAGES = 3;
+  constexpr int G = WT::GROUP;
   extern __shared__ __align__(16) unsigned char smem[];
   const int a_idx = blockIdx.x / p.units_per_expert;
   const int chunk = blockIdx.x % p.units_per_expert;
@@ -88,206 +209,123 @@ __global__ void __launch_bounds__(EXP_THREADS, 2) expert_gemv_kernel(ExpertParam
   const int e = p.active[a_idx];
   const int base = p.offsets[e];
   const int count = p.offsets[e + 1] - base;
-  const int ntm = p.tpp >> 3;
+  const int ntm = NTM;
+  const int tpp = NTM * 8;
   const int K = p.K;
 
-  uint32_t* xs = reinterpret_cast<uint32_t*>(smem);                       // K * tpp halves
-  float* red = reinterpret_cast<float*>(smem + (size_t)K * p.tpp * 2);    // [KS][ROWT*16][tpp]
-  float* tscale = red + (size_t)KS * ROWT * 16 * p.tpp;                   // [tpp]
-  int* srow = reinterpret_cast<int*>(tscale + MAX_TPP);                   // [tpp] source row
-  int* spair = srow + MAX_TPP;                                            // [tpp] original pair
+  uint32_t* xs = reinterpret_cast<uint32_t*>(smem);                      // K * tpp halves
+  float* red = reinterpret_cast<float*>(smem + (size_t)K * tpp * 2);     // [KS][ROWT*16][tpp] (KS > 1)
+  float* tscale = red + (KS > 1 ? (size_t)KS * ROWT * 16 * tpp : 0);     // [tpp]
+  int* spair = reinterpret_cast<int*>(tscale + MAX_TPP);                 // [tpp] original pair
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int rt_local = warp / KS, ks = warp % KS;
   const int tile = chunk * ROWT + rt_local;
   const bool tile_ok = tile < p.tiles;
-  const int kb_per = (p.kb_count + KS - 1) / KS;
-  const int kb_begin = min(ks * kb_per, p.kb_count), kb_end = min(kb_begin + kb_per, p.kb_count);
+  // K range of this warp, in whole groups so a scale load always covers its group
+  const int groups = (p.kb_count + G - 1) / G;
+  const int g_per = (groups + KS - 1) / KS;
+  const int kb_begin = min(ks * g_per * G, p.kb_count);
+  const int kb_end = min(kb_begin + g_per * G, p.kb_count);
 
-  for (int p0 = 0; p0 < count; p0 += p.tpp) {
-    const int ntok = min(p.tpp, count - p0);
+  for (int p0 = 0; p0 < count; p0 += tpp) {
+    const int ntok = min(tpp, count - p0);
     const int nt_used = (ntok + 7) >> 3;
-    // token bookkeeping
-    if (threadIdx.x < p.tpp) {
-      int n = threadIdx.x;
-      if (n < ntok) {
-        int pr = p.perm[base + p0 + n];
-        spair[n] = pr;
-        srow[n] = p.phase == 0 ? pr / p.width : base + p0 + n;
-      } else {
-        spair[n] = -1;
-        srow[n] = -1;
-      }
-    }
-    __syncthreads();
-    // per-token scale: f16 staging normalises each row so its max magnitude is in [2^13, 2^14)
-    for (int n = warp; n < p.tpp; n += EXP_WARPS) {
-      float sc = 1.0f;
-      if (WT::kF16 && n < ntok) {
-        float m = 0.0f;
-        if (p.phase == 0) {
-          const __nv_bfloat162* row = reinterpret_cast<const __nv_bfloat162*>(p.x + (int64_t)srow[n] * K);
-          for (int i = lane; i < K / 2; i += 32) {
-            float2 v = __bfloat1622float2(row[i]);
-            m = fmaxf(m, fmaxf(fabsf(v.x), fabsf(v.y)));
-          }
-        } else {
-          const float2* row = reinterpret_cast<const float2*>(p.h_in + (int64_t)srow[n] * K);
-          for (int i = lane; i < K / 2; i += 32) {
-            float2 v = row[i];
-            m = fmaxf(m, fmaxf(fabsf(v.x), fabsf(v.y)));
-          }
-        }
-        m = warp_max(m);
-        if (m > 0.0f && m < __int_as_float(0x7f800000)) {
-          int ex;
-          frexpf(m, &ex);  // m < 2^ex
-          int sh = max(-100, min(100, ex - 14));
-          sc = ldexpf(1.0f, sh);
-        }
-      }
-      if (lane == 0) tscale[n] = sc;
-    }
-    __syncthreads();
-    // convert + scatter into B-fragment order
-    const int kpairs = K >> 1;
-    for (int i = threadIdx.x; i < p.tpp * kpairs; i += EXP_THREADS) {
-      const int n = i / kpairs, kp = i - n * kpairs, k = kp * 2;
-      uint32_t word = 0u;
-      if (n < ntok) {
-        float2 v;
-        if (p.phase == 0) v = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(p.x + (int64_t)srow[n] * K)[kp]);
-        else v = reinterpret_cast<const float2*>(p.h_in + (int64_t)srow[n] * K)[kp];
-        if (WT::kF16) {
-          const float inv = 1.0f / tscale[n];  // exact: power of two
-          word = pack_f16x2(v.x * inv, v.y * inv);
-        } else {
-          word = pack_bf16x2(v.x, v.y);
-        }
-      }
-      xs[xs_word(n, k, ntm)] = word;
-    }
-    __syncthreads();
-
-    // ---- tensor-core main loop ----
-    float acc[MAX_TPP / 8][4];
-#pragma unroll
-    for (int t = 0; t < MAX_TPP / 8; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
-
+    // first weight groups go out before the staging so HBM latency overlaps it
+    typename WT::Stage st[STAGES];
     if (tile_ok) {
-      constexpr int U = 4;
-      if constexpr (WT::kF16) {
-        for (int kb0 = kb_begin; kb0 < kb_end; kb0 += U) {
-          uint4 q[U];
-          uint32_t s2[U];
-#pragma unroll
-          for (int u = 0; u < U; ++u)
-            if (kb0 + u < kb_end) q[u] = ldg_stream(WT::qptr(p, e, tile, kb0 + u, lane));
-#pragma unroll
-          for (int u = 0; u < U; ++u) {
-            const int kb = kb0 + u;
-            if (kb < kb_end) {
-              const uint32_t* sp = reinterpret_cast<const uint32_t*>(WT::sptr(p, e, tile, kb >> 2, lane));
-              s2[u] = __ldg(sp + (kb & 3));
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < U; ++u) {
-            const int kb = kb0 + u;
-            if (kb < kb_end) {
-              uint32_t a0[4], a1[4];
-              WT::decode(q[u], s2[u], a0, a1);
-#pragma unroll
-              for (int t = 0; t < MAX_TPP / 8; ++t) {
-                if (t < nt_used) {
-                  uint4 b = lds128(xs + ((kb * ntm + t) * 32 + lane) * 4);
-                  mma_f16(acc[t], a0, b.x, b.y);
-                  mma_f16(acc[t], a1, b.z, b.w);
-                }
-              }
-            }
-          }
-        }
-      } else {
-        for (int kb0 = kb_begin; kb0 < kb_end; kb0 += U) {
-          uint4 q0[U], q1[U];
-#pragma unroll
-          for (int u = 0; u < U; ++u)
-            if (kb0 + u < kb_end) {
-              const uint8_t* ptr = WT::qptr(p, e, tile, kb0 + u, lane);
-              q0[u] = ldg_stream(ptr);
-              q1[u] = ldg_stream(ptr + 512);
-            }
-#pragma unroll
-          for (int u = 0; u < U; ++u) {
-            const int kb = kb0 + u;
-            if (kb < kb_end) {
-              uint32_t a0[4] = {q0[u].x, q0[u].y, q0[u].z, q0[u].w};
-              uint32_t a1[4] = {q1[u].x, q1[u].y, q1[u].z, q1[u].w};
-#pragma unroll
-              for (int t = 0; t < MAX_TPP / 8; ++t) {
-                if (t < nt_used) {
-                  uint4 b = lds128(xs + ((kb * ntm + t) * 32 + lane) * 4);
-                  mma_bf16(acc[t], a0, b.x, b.y);
-                  mma_bf16(acc[t], a1, b.z, b.w);
-                }
-              }
-            }
-          }
-        }
-      }
+      WT::load(p, e, tile, kb_begin, kb_end, lane, st[0]);
+      WT::load(p, e, tile, kb_begin + G, kb_end, lane, st[1]);
     }
-
-    // ---- K-split reduction through shared memory ----
-    // C fragment: c0,c1 -> (row g, tokens 2c, 2c+1); c2,c3 -> (row g+8, same tokens)
-    {
-      const int g = lane >> 2, c = lane & 3;
-      float* r = red + ((size_t)ks * ROWT * 16 + rt_local * 16) * p.tpp;
-#pragma unroll
-      for (int t = 0; t < MAX_TPP / 8; ++t) {
-        if (t < ntm) {
-          const int n0 = t * 8 + 2 * c;
-          r[g * p.tpp + n0] = acc[t][0];
-          r[g * p.tpp + n0 + 1] = acc[t][1];
-          r[(g + 8) * p.tpp + n0] = acc[t][2];
-          r[(g + 8) * p.tpp + n0 + 1] = acc[t][3];
-        }
-      }
+    if (threadIdx.x < tpp) spair[threadIdx.x] = threadIdx.x < ntok ? p.perm[base + p0 + threadIdx.x] : -1;
+    for (int n = warp; n < ntok; n += EXP_WARPS) {
+      const int src = p.phase == 0 ? p.perm[base + p0 + n] / p.width : base + p0 + n;
+      stage_row<WT::kF16>(p, n, src, xs, ntm, tscale, lane);
     }
     __syncthreads();
 
-    if (p.phase == 0) {
-      // h[n][col] = silu(gate) * up, col = tile*8 + r; rows 0..7 of a tile are gate, 8..15 up
-      const int cols = ROWT * 8;
-      const int I = p.N >> 1;
-      for (int i = threadIdx.x; i < ntok * cols; i += EXP_THREADS) {
-        const int n = i / cols, cl = i - n * cols;
-        const int rl = cl >> 3, r = cl & 7;
-        const int tl = chunk * ROWT + rl;
-        if (tl >= p.tiles) continue;
-        float gsum = 0.0f, usum = 0.0f;
+    float acc[NTM][4];
 #pragma unroll
-        for (int s = 0; s < KS; ++s) {
-          gsum += red[((size_t)s * ROWT * 16 + rl * 16 + r) * p.tpp + n];
-          usum += red[((size_t)s * ROWT * 16 + rl * 16 + 8 + r) * p.tpp + n];
+    for (int t = 0; t < NTM; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
+    if (tile_ok) {
+      for (int kb0 = kb_begin; kb0 < kb_end; kb0 += STAGES * G) {
+        WT::load(p, e, tile, kb0 + 2 * G, kb_end, lane, st[2]);
+        WT::template compute<NTM>(st[0], kb0, kb_end, xs, ntm, nt_used, lane, acc);
+        WT::load(p, e, tile, kb0 + 3 * G, kb_end, lane, st[0]);
+        WT::template compute<NTM>(st[1], kb0 + G, kb_end, xs, ntm, nt_used, lane, acc);
+        WT::load(p, e, tile, kb0 + 4 * G, kb_end, lane, st[1]);
+        WT::template compute<NTM>(st[2], kb0 + 2 * G, kb_end, xs, ntm, nt_used, lane, acc);
+      }
+    }
+
+    const int g = lane >> 2, c = lane & 3;
+    if constexpr (KS == 1) {
+      // complete sums in registers: c0,c1 -> (row g, tokens 2c, 2c+1); c2,c3 -> (row g+8, same)
+      if (tile_ok) {
+#pragma unroll
+        for (int t = 0; t < NTM; ++t) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int n = t * 8 + 2 * c + j;
+            if (t < nt_used && n < ntok) {
+              const float sc = tscale[n];
+              if (p.phase == 0) {
+                const float gv = acc[t][j] * sc, uv = acc[t][2 + j] * sc;
+                const int I = p.N >> 1;
+                p.out[(int64_t)(base + p0 + n) * I + tile * 8 + g] = gv / (1.0f + __expf(-gv)) * uv;
+              } else {
+                const int pr = spair[n];
+                const float w = p.route_w[pr] * sc;
+                float* o = p.out + (int64_t)pr * p.N + tile * 16;
+                o[g] = acc[t][j] * w;
+                o[g + 8] = acc[t][2 + j] * w;
+              }
+            }
+          }
         }
-        const float sc = tscale[n];
-        gsum *= sc;
-        usum *= sc;
-        const float hval = gsum / (1.0f + __expf(-gsum)) * usum;
-        p.out[(int64_t)(base + p0 + n) * I + tl * 8 + r] = hval;
       }
     } else {
-      const int rows = ROWT * 16;
-      for (int i = threadIdx.x; i < ntok * rows; i += EXP_THREADS) {
-        const int n = i / rows, rl = i - n * rows;
-        const int row = chunk * ROWT * 16 + rl;
-        if (row >= p.N) continue;
-        float sum = 0.0f;
+      float* r = red + ((size_t)ks * ROWT * 16 + rt_local * 16) * tpp;
 #pragma unroll
-        for (int s = 0; s < KS; ++s) sum += red[((size_t)s * ROWT * 16 + rl) * p.tpp + n];
-        const int pr = spair[n];
-        p.out[(int64_t)pr * p.N + row] = sum * tscale[n] * p.route_w[pr];
+      for (int t = 0; t < NTM; ++t) {
+        const int n0 = t * 8 + 2 * c;
+        r[g * tpp + n0] = acc[t][0];
+        r[g * tpp + n0 + 1] = acc[t][1];
+        r[(g + 8) * tpp + n0] = acc[t][2];
+        r[(g + 8) * tpp + n0 + 1] = acc[t][3];
+      }
+      __syncthreads();
+      if (p.phase == 0) {
+        const int cols = ROWT * 8;
+        const int I = p.N >> 1;
+        for (int i = threadIdx.x; i < ntok * cols; i += EXP_THREADS) {
+          const int n = i / cols, cl = i - n * cols;
+          const int rl = cl >> 3, rr = cl & 7;
+          const int tl = chunk * ROWT + rl;
+          if (tl >= p.tiles) continue;
+          float gsum = 0.0f, usum = 0.0f;
+#pragma unroll
+          for (int s = 0; s < KS; ++s) {
+            gsum += red[((size_t)s * ROWT * 16 + rl * 16 + rr) * tpp + n];
+            usum += red[((size_t)s * ROWT * 16 + rl * 16 + 8 + rr) * tpp + n];
+          }
+          const float sc = tscale[n];
+          gsum *= sc;
+          usum *= sc;
+          p.out[(int64_t)(base + p0 + n) * I + tl * 8 + rr] = gsum / (1.0f + __expf(-gsum)) * usum;
+        }
+      } else {
+        const int rows = ROWT * 16;
+        for (int i = threadIdx.x; i < ntok * rows; i += EXP_THREADS) {
+          const int n = i / rows, rl = i - n * rows;
+          const int row = chunk * ROWT * 16 + rl;
+          if (row >= p.N) continue;
+          float sum = 0.0f;
+#pragma unroll
+          for (int s = 0; s < KS; ++s) sum += red[((size_t)s * ROWT * 16 + rl) * tpp + n];
+          const int pr = spair[n];
+          p.out[(int64_t)pr * p.N + row] = sum * tscale[n] * p.route_w[pr];
+        }
       }
     }
     __syncthreads();
@@ -316,53 +354,67 @@ __global__ void combine_kernel(const float* __restrict__ ypair, const uint32_t* 
 
 // ---- host launchers -------------------------------------------------------------------------------
 
-int choose_tpp(int K) {
-  if ((size_t)K * 32 * 2 <= 72 * 1024) return 32;
-  if ((size_t)K * 16 * 2 <= 96 * 1024) return 16;
-  return 8;
+// Tokens per pass: enough n-tiles for the expected busiest expert (mean + 3 sd of a binomial
+// count), within a shared-memory budget.
+int choose_tpp(int K, double mean_tokens_per_expert) {
+  const double m = mean_tokens_per_expert;
+  const double want = m + 3.0 * sqrt(m > 0 ? m : 0) + 1.0;
+  int tpp = want <= 8 ? 8 : want <= 16 ? 16 : want <= 24 ? 24 : 32;
+  while (tpp > 8 && (size_t)K * tpp * 2 > 132 * 1024) tpp -= 8;
+  return tpp;
 }
 
-size_t expert_smem_bytes(int K, int tpp) {
-  return (size_t)K * tpp * 2 + (size_t)EXP_WARPS * 16 * tpp * 4 + MAX_TPP * 4 * 3 + 64;
+size_t expert_smem_bytes(int K, int tpp, int rowt) {
+  const int ks = EXP_WARPS / rowt;
+  return (size_t)K * tpp * 2 + (ks > 1 ? (size_t)EXP_WARPS * 16 * tpp * 4 : 0) + MAX_TPP * 4 * 2 + 64;
 }
 
-template <class WT, int ROWT>
-static moe_status launch_rowt(const ExpertParams& p, int grid, size_t smem, cudaStream_t st) {
+template <class WT, int ROWT, int NTM>
+static moe_status launch3(const ExpertParams& p, int grid, size_t smem, cudaStream_t st) {
   static bool attr[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr[dev & 63]) {
-    MOE_CUDA_TRY(cudaFuncSetAttribute(expert_gemv_kernel<WT, ROWT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      200 * 1024));
+    MOE_CUDA_TRY(cudaFuncSetAttribute(expert_gemv_kernel<WT, ROWT, NTM>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     attr[dev & 63] = true;
   }
-  expert_gemv_kernel<WT, ROWT><<<grid, EXP_THREADS, smem, st>>>(p);
+  expert_gemv_kernel<WT, ROWT, NTM><<<grid, EXP_THREADS, smem, st>>>(p);
   MOE_CUDA_TRY(cudaGetLastError());
   return MOE_OK;
 }
 
-// rowt: row tiles per CTA (1, 2, 4 or 8); est_active: expected active experts (grid upper bound
-// is min(E, n_pairs) experts, CTAs past the real count exit at once).
+template <class WT, int ROWT>
+static moe_status launch2(const ExpertParams& p, int grid, size_t smem, cudaStream_t st) {
+  switch (p.tpp) {
+    case 8: return launch3<WT, ROWT, 1>(p, grid, smem, st);
+    case 16: return launch3<WT, ROWT, 2>(p, grid, smem, st);
+    case 24: return launch3<WT, ROWT, 3>(p, grid, smem, st);
+    default: return launch3<WT, ROWT, 4>(p, grid, smem, st);
+  }
+}
+
+template <class WT>
+static moe_status launch1(const ExpertParams& p, int grid, size_t smem, int rowt, cudaStream_t st) {
+  switch (rowt) {
+    case 1: return launch2<WT, 1>(p, grid, smem, st);
+    case 2: return launch2<WT, 2>(p, grid, smem, st);
+    case 4: return launch2<WT, 4>(p, grid, smem, st);
+    default: return launch2<WT, 8>(p, grid, smem, st);
+  }
+}
+
+// rowt: row tiles per CTA (1, 2, 4 or 8). The grid covers min(E, n_pairs) experts; CTAs past the
+// real count of active experts exit at once.
 moe_status launch_expert_gemv(int wdtype, ExpertParams p, int max_active, int rowt, cudaStream_t st) {
+  if (p.tpp % 8 || p.tpp < 8 || p.tpp > MAX_TPP) return fail(MOE_ERR_INVALID, "expert kernel: bad tokens per pass");
+  if (p.K > 4096) return fail(MOE_ERR_UNSUPPORTED, "decode expert kernel: K > 4096");
   p.units_per_expert = ceil_div(p.tiles, rowt);
   const int grid = max_active * p.units_per_expert;
   if (grid <= 0) return MOE_OK;
-  const size_t smem = expert_smem_bytes(p.K, p.tpp);
-  if (wdtype == MOE_DTYPE_Q8_0) {
-    switch (rowt) {
-      case 1: return launch_rowt<WQ8, 1>(p, grid, smem, st);
-      case 2: return launch_rowt<WQ8, 2>(p, grid, smem, st);
-      case 4: return launch_rowt<WQ8, 4>(p, grid, smem, st);
-      default: return launch_rowt<WQ8, 8>(p, grid, smem, st);
-    }
-  } else if (wdtype == MOE_DTYPE_BF16) {
-    switch (rowt) {
-      case 1: return launch_rowt<WBF16, 1>(p, grid, smem, st);
-      case 2: return launch_rowt<WBF16, 2>(p, grid, smem, st);
-      case 4: return launch_rowt<WBF16, 4>(p, grid, smem, st);
-      default: return launch_rowt<WBF16, 8>(p, grid, smem, st);
-    }
-  }
+  const size_t smem = expert_smem_bytes(p.K, p.tpp, rowt);
+  if (wdtype == MOE_DTYPE_Q8_0) return launch1<WQ8>(p, grid, smem, rowt, st);
+  if (wdtype == MOE_DTYPE_BF16) return launch1<WBF16>(p, grid, smem, rowt, st);
   return fail(MOE_ERR_UNSUPPORTED, "decode expert kernel: weight format not built yet");
 }
 

@@ -314,8 +314,9 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   if (T < 0 || width <= 0) return fail(MOE_ERR_INVALID, "moe_forward: need T >= 0 and width > 0");
   if (T == 0) return MOE_OK;
   if (!x || !ids || !weights || !y) return fail(MOE_ERR_INVALID, "moe_forward: null pointer");
-  if (((uintptr_t)x | (uintptr_t)ids | (uintptr_t)weights) & 3)
-    return fail(MOE_ERR_INVALID, "moe_forward: x, ids and weights must be 4-byte aligned");
+  if ((uintptr_t)x & 15) return fail(MOE_ERR_INVALID, "moe_forward: x must be 16-byte aligned");
+  if (((uintptr_t)ids | (uintptr_t)weights) & 3)
+    return fail(MOE_ERR_INVALID, "moe_forward: ids and weights must be 4-byte aligned");
   if ((uintptr_t)y & 7) return fail(MOE_ERR_INVALID, "moe_forward: y must be 8-byte aligned");
   const int64_t n64 = (int64_t)T * width;
   if (n64 > L->cap_pairs)
@@ -342,7 +343,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   gp.tiles = 2 * I / 16;
   gp.kb_count = H / 32;
   gp.phase = 0;
-  gp.tpp = choose_tpp(H);
+  gp.tpp = choose_tpp(H, n_pairs / (est > 1.0 ? est : 1.0));
   gp.width = width;
   gp.n_pairs = n_pairs;
   gp.x = static_cast<const __nv_bfloat16*>(x);
@@ -364,7 +365,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   dp.tiles = H / 16;
   dp.kb_count = I / 32;
   dp.phase = 1;
-  dp.tpp = choose_tpp(I);
+  dp.tpp = choose_tpp(I, n_pairs / (est > 1.0 ? est : 1.0));
   dp.x = nullptr;
   dp.h_in = L->h;
   dp.route_w = weights;

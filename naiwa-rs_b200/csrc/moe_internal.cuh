@@ -53,8 +53,8 @@ struct ExpertParams {
 moe_status launch_expert_gemv(int wdtype, ExpertParams p, int max_active, int rowt, cudaStream_t st);
 moe_status launch_combine(const float* ypair, const uint32_t* ids, int T, int width, int H, int E, void* y,
                           cudaStream_t st);
-int choose_tpp(int K);
-size_t expert_smem_bytes(int K, int tpp);
+int choose_tpp(int K, double mean_tokens_per_expert);
+size_t expert_smem_bytes(int K, int tpp, int rowt);
 
 int64_t device_q_bytes(int wdtype, int N, int K);
 int64_t device_s_bytes(int wdtype, int N, int K);
