@@ -439,7 +439,11 @@ def main():
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batches", default=None,
+                    help="comma-separated batch sizes replacing the ragged sweep (profiling runs only)")
     args = ap.parse_args()
+    if args.batches:
+        RAGGED[:] = [int(b) for b in args.batches.split(",")]
     if args.impl == "reference":
         run_reference(args)
     else:

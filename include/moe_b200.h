@@ -126,10 +126,13 @@ size_t moe_last_error(char* buf, size_t n);
 
 /* ---- stateless kernels (the layer calls the same code) ----------------------------------- */
 
-/* Router logits + top-k without a layer. w_router: [E, H] bf16; bias: [E] f32 or NULL. */
+/* Router logits + top-k without a layer. w_router: [E, H] bf16; bias: [E] f32 or NULL.
+ * workspace: 16-byte aligned device scratch of moe_route_workspace_bytes(T, E) bytes, zero-filled
+ * before its first use; every call leaves it ready for the next call on the same stream. */
 moe_status moe_route_tokens(const void* x, const void* w_router, const float* bias, int T, int H, int E, int k,
                             int mode, int n_group, int topk_group, float routed_scale, uint32_t* ids,
-                            float* weights, void* stream);
+                            float* weights, void* workspace, size_t workspace_bytes, void* stream);
+size_t moe_route_workspace_bytes(int T, int E);
 
 /* Expert histogram + stable token->expert permutation of n_pairs routed pairs (the grouping the
  * reference does in Gpu::submit, gpu.rs:103-132, and rings::group_rows, rings.rs:68-156).

@@ -24,8 +24,6 @@
 
 namespace moe {
 
-constexpr int EXP_THREADS = 256;
-constexpr int EXP_WARPS = 8;
 constexpr int MAX_TPP = 32;  // tokens per pass (4 n-tiles of 8)
 
 // ---- weight fragment streams ---------------------------------------------------------------------
@@ -51,10 +49,11 @@ struct WQ8 {
                         (lane >> 2) * 16);
     }
   }
-  // exact int8 -> f16 of the lane's 16 quant bytes: a0 (k16 step 0), a1 (step 1)
+  // exact int8 -> f16 of the lane's 16 quant bytes: a0 (k16 step 0), a1 (step 1). The device layout
+  // stores u = q + 128 (the repack flips the sign bit), so 0x64 in the high byte makes 1024 + u.
   __device__ static __forceinline__ void quants(uint4 q, uint32_t (&a0)[4], uint32_t (&a1)[4]) {
     const __half2 bias = __float2half2_rn(1152.0f);
-    const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
       uint32_t* dst = s ? a1 : a0;
@@ -85,13 +84,11 @@ struct WQ8 {
       for (int t = 0; t < NTM; ++t) {
         if (t < nt_used) {
           uint4 b = lds128(xs + ((kb * ntm + t) * 32 + lane) * 4);
-          float tmp[4] = {0.f, 0.f, 0.f, 0.f};
-          mma_f16(tmp, a0, b.x, b.y);
+          float tmp[4];
+          mma_f16_zero(tmp, a0, b.x, b.y);
           mma_f16(tmp, a1, b.z, b.w);
-          acc[t][0] = fmaf(slo, tmp[0], acc[t][0]);
-          acc[t][1] = fmaf(slo, tmp[1], acc[t][1]);
-          acc[t][2] = fmaf(shi, tmp[2], acc[t][2]);
-          acc[t][3] = fmaf(shi, tmp[3], acc[t][3]);
+          ffma2(acc[t][0], acc[t][1], slo, tmp[0], tmp[1]);
+          ffma2(acc[t][2], acc[t][3], shi, tmp[2], tmp[3]);
         }
       }
     }
@@ -197,9 +194,10 @@ __device__ __forceinline__ void stage_row(const ExpertParams& p, int n, int src_
   }
 }
 
-template <class WT, int ROWT, int NTM>
-__global__ void __launch_bounds__(EXP_THREADS, 2) expert_gemv_kernel(ExpertParams p) {
-  constexpr int KS = EXP_WARPS / ROWT;
+template <class WT, int ROWT, int NTM, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(ExpertParams p) {
+  constexpr int KS = WARPS / ROWT;
+  constexpr int THREADS = WARPS * 32;
   constexpr int STAGES = 3;
   constexpr int G = WT::GROUP;
   extern __shared__ __align__(16) unsigned char smem[];
@@ -222,11 +220,10 @@ __global__ void __launch_bounds__(EXP_THREADS, 2) expert_gemv_kernel(ExpertParam
   const int rt_local = warp / KS, ks = warp % KS;
   const int tile = chunk * ROWT + rt_local;
   const bool tile_ok = tile < p.tiles;
-  // K range of this warp, in whole groups so a scale load always covers its group
+  // K range of this warp: whole groups (a scale load always covers its group), balanced to within one
   const int groups = (p.kb_count + G - 1) / G;
-  const int g_per = (groups + KS - 1) / KS;
-  const int kb_begin = min(ks * g_per * G, p.kb_count);
-  const int kb_end = min(kb_begin + g_per * G, p.kb_count);
+  const int kb_begin = min(groups * ks / KS * G, p.kb_count);
+  const int kb_end = min(groups * (ks + 1) / KS * G, p.kb_count);
 
   for (int p0 = 0; p0 < count; p0 += tpp) {
     const int ntok = min(tpp, count - p0);
@@ -238,7 +235,7 @@ __global__ void __launch_bounds__(EXP_THREADS, 2) expert_gemv_kernel(ExpertParam
       WT::load(p, e, tile, kb_begin + G, kb_end, lane, st[1]);
     }
     if (threadIdx.x < tpp) spair[threadIdx.x] = threadIdx.x < ntok ? p.perm[base + p0 + threadIdx.x] : -1;
-    for (int n = warp; n < ntok; n += EXP_WARPS) {
+    for (int n = warp; n < ntok; n += WARPS) {
       const int src = p.phase == 0 ? p.perm[base + p0 + n] / p.width : base + p0 + n;
       stage_row<WT::kF16>(p, n, src, xs, ntm, tscale, lane);
     }
@@ -298,7 +295,7 @@ __global__ void __launch_bounds__(EXP_THREADS, 2) expert_gemv_kernel(ExpertParam
       if (p.phase == 0) {
         const int cols = ROWT * 8;
         const int I = p.N >> 1;
-        for (int i = threadIdx.x; i < ntok * cols; i += EXP_THREADS) {
+        for (int i = threadIdx.x; i < ntok * cols; i += THREADS) {
           const int n = i / cols, cl = i - n * cols;
           const int rl = cl >> 3, rr = cl & 7;
           const int tl = chunk * ROWT + rl;
@@ -316,7 +313,7 @@ __global__ void __launch_bounds__(EXP_THREADS, 2) expert_gemv_kernel(ExpertParam
         }
       } else {
         const int rows = ROWT * 16;
-        for (int i = threadIdx.x; i < ntok * rows; i += EXP_THREADS) {
+        for (int i = threadIdx.x; i < ntok * rows; i += THREADS) {
           const int n = i / rows, rl = i - n * rows;
           const int row = chunk * ROWT * 16 + rl;
           if (row >= p.N) continue;
@@ -364,55 +361,58 @@ int choose_tpp(int K, double mean_tokens_per_expert) {
   return tpp;
 }
 
-size_t expert_smem_bytes(int K, int tpp, int rowt) {
-  const int ks = EXP_WARPS / rowt;
-  return (size_t)K * tpp * 2 + (ks > 1 ? (size_t)EXP_WARPS * 16 * tpp * 4 : 0) + MAX_TPP * 4 * 2 + 64;
+size_t expert_smem_bytes(int K, int tpp, int rowt, int warps) {
+  const int ks = warps / rowt;
+  return (size_t)K * tpp * 2 + (ks > 1 ? (size_t)warps * 16 * tpp * 4 : 0) + MAX_TPP * 4 * 2 + 64;
 }
 
-template <class WT, int ROWT, int NTM>
+template <class WT, int ROWT, int NTM, int WARPS>
 static moe_status launch3(const ExpertParams& p, int grid, size_t smem, cudaStream_t st) {
   static bool attr[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr[dev & 63]) {
-    MOE_CUDA_TRY(cudaFuncSetAttribute(expert_gemv_kernel<WT, ROWT, NTM>,
+    MOE_CUDA_TRY(cudaFuncSetAttribute(expert_gemv_kernel<WT, ROWT, NTM, WARPS>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     attr[dev & 63] = true;
   }
-  expert_gemv_kernel<WT, ROWT, NTM><<<grid, EXP_THREADS, smem, st>>>(p);
+  expert_gemv_kernel<WT, ROWT, NTM, WARPS><<<grid, WARPS * 32, smem, st>>>(p);
   MOE_CUDA_TRY(cudaGetLastError());
   return MOE_OK;
 }
 
-template <class WT, int ROWT>
+template <class WT, int ROWT, int WARPS>
 static moe_status launch2(const ExpertParams& p, int grid, size_t smem, cudaStream_t st) {
   switch (p.tpp) {
-    case 8: return launch3<WT, ROWT, 1>(p, grid, smem, st);
-    case 16: return launch3<WT, ROWT, 2>(p, grid, smem, st);
-    case 24: return launch3<WT, ROWT, 3>(p, grid, smem, st);
-    default: return launch3<WT, ROWT, 4>(p, grid, smem, st);
+    case 8: return launch3<WT, ROWT, 1, WARPS>(p, grid, smem, st);
+    case 16: return launch3<WT, ROWT, 2, WARPS>(p, grid, smem, st);
+    case 24: return launch3<WT, ROWT, 3, WARPS>(p, grid, smem, st);
+    default: return launch3<WT, ROWT, 4, WARPS>(p, grid, smem, st);
   }
 }
 
 template <class WT>
 static moe_status launch1(const ExpertParams& p, int grid, size_t smem, int rowt, cudaStream_t st) {
   switch (rowt) {
-    case 1: return launch2<WT, 1>(p, grid, smem, st);
-    case 2: return launch2<WT, 2>(p, grid, smem, st);
-    case 4: return launch2<WT, 4>(p, grid, smem, st);
-    default: return launch2<WT, 8>(p, grid, smem, st);
+    case 1: return launch2<WT, 1, 8>(p, grid, smem, st);
+    case 2: return launch2<WT, 2, 8>(p, grid, smem, st);
+    case 4: return launch2<WT, 4, 8>(p, grid, smem, st);
+    case 8: return launch2<WT, 8, 8>(p, grid, smem, st);
+    default: return launch2<WT, 16, 16>(p, grid, smem, st);
   }
 }
 
-// rowt: row tiles per CTA (1, 2, 4 or 8). The grid covers min(E, n_pairs) experts; CTAs past the
-// real count of active experts exit at once.
+// rowt: row tiles per CTA (1, 2, 4 or 8 with 8 warps; 16 with 16 warps, one tile per warp). The
+// grid covers min(E, n_pairs) experts; CTAs past the real count of active experts exit at once.
 moe_status launch_expert_gemv(int wdtype, ExpertParams p, int max_active, int rowt, cudaStream_t st) {
   if (p.tpp % 8 || p.tpp < 8 || p.tpp > MAX_TPP) return fail(MOE_ERR_INVALID, "expert kernel: bad tokens per pass");
   if (p.K > 4096) return fail(MOE_ERR_UNSUPPORTED, "decode expert kernel: K > 4096");
+  if (rowt != 1 && rowt != 2 && rowt != 4 && rowt != 8 && rowt != 16)
+    return fail(MOE_ERR_INVALID, "expert kernel: bad row tiles per CTA");
   p.units_per_expert = ceil_div(p.tiles, rowt);
   const int grid = max_active * p.units_per_expert;
   if (grid <= 0) return MOE_OK;
-  const size_t smem = expert_smem_bytes(p.K, p.tpp, rowt);
+  const size_t smem = expert_smem_bytes(p.K, p.tpp, rowt, rowt == 16 ? 16 : 8);
   if (wdtype == MOE_DTYPE_Q8_0) return launch1<WQ8>(p, grid, smem, rowt, st);
   if (wdtype == MOE_DTYPE_BF16) return launch1<WBF16>(p, grid, smem, rowt, st);
   return fail(MOE_ERR_UNSUPPORTED, "decode expert kernel: weight format not built yet");

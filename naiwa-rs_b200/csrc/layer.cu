@@ -65,6 +65,7 @@ struct moe_layer {
   float* router_b = nullptr;
   // scratch
   int cap_pairs = 0;
+  int cap_tokens = 0;
   int32_t* counts = nullptr;
   int32_t* offsets = nullptr;
   int32_t* perm = nullptr;
@@ -75,6 +76,8 @@ struct moe_layer {
   size_t plan_ws_bytes = 0;
   float* h = nullptr;
   float* ypair = nullptr;
+  void* route_ws = nullptr;
+  size_t route_ws_bytes = 0;
   int64_t weight_bytes = 0;
   int64_t scratch_bytes = 0;
 };
@@ -89,10 +92,14 @@ static void free_scratch(moe_layer* L) {
   cudaFree(L->plan_ws);
   cudaFree(L->h);
   cudaFree(L->ypair);
+  cudaFree(L->route_ws);
+  L->route_ws = nullptr;
+  L->route_ws_bytes = 0;
   L->counts = L->offsets = L->perm = L->active = L->n_active = L->err = nullptr;
   L->plan_ws = nullptr;
   L->h = L->ypair = nullptr;
   L->cap_pairs = 0;
+  L->cap_tokens = 0;
   L->scratch_bytes = 0;
 }
 
@@ -110,7 +117,7 @@ static moe_status alloc_scratch(moe_layer* L, int max_tokens) {
   const int64_t cap64 = (int64_t)max_tokens * L->d.top_k;
   if (cap64 > (1 << 28)) return fail(MOE_ERR_INVALID, "max_tokens * top_k too large");
   const int cap = (int)cap64;
-  if (cap <= L->cap_pairs && L->counts) return MOE_OK;
+  if (cap <= L->cap_pairs && max_tokens <= L->cap_tokens && L->counts) return MOE_OK;
   free_scratch(L);
   const int E = L->d.num_experts, H = L->d.hidden, I = L->d.inter;
   int64_t acc = 0;
@@ -125,7 +132,11 @@ static moe_status alloc_scratch(moe_layer* L, int max_tokens) {
   MOE_TRY(dalloc(&L->plan_ws, L->plan_ws_bytes, &acc));
   MOE_TRY(dalloc(&L->h, sizeof(float) * (size_t)cap * I, &acc));
   MOE_TRY(dalloc(&L->ypair, sizeof(float) * (size_t)cap * H, &acc));
+  L->route_ws_bytes = route_workspace_bytes(max_tokens, E);
+  MOE_TRY(dalloc(&L->route_ws, L->route_ws_bytes, &acc));
+  MOE_CUDA_TRY(cudaMemset(L->route_ws, 0, L->route_ws_bytes));  // arrival counters start at zero
   L->cap_pairs = cap;
+  L->cap_tokens = max_tokens;
   L->scratch_bytes = acc;
   return MOE_OK;
 }
@@ -267,16 +278,21 @@ moe_status moe_layer_warmup(moe_layer* L, int max_tokens) {
 moe_status moe_route(moe_layer* L, const void* x, int T, uint32_t* ids, float* weights, void* stream) {
   if (!L) return fail(MOE_ERR_INVALID, "moe_route: null layer");
   if (!L->router_w) return fail(MOE_ERR_INVALID, "moe_route: layer was created without router weights");
+  if (T > L->cap_tokens)
+    return fail(MOE_ERR_INVALID, "moe_route: T exceeds the max_tokens sized at create/warmup");
   DeviceGuard guard(L->dev);
   RouteParams p{static_cast<const __nv_bfloat16*>(x), L->router_w, L->router_b, ids, weights, T, L->d.hidden,
                 L->d.num_experts, L->d.top_k, L->d.router_mode, L->d.n_group, L->d.topk_group,
                 L->d.routed_scale};
-  return route_tokens(p, static_cast<cudaStream_t>(stream));
+  return route_tokens(p, L->route_ws, L->route_ws_bytes, static_cast<cudaStream_t>(stream));
 }
 
-// Row tiles per CTA: the largest of 8/4/2/1 that still gives >= 2 CTAs per SM for the expected
-// number of distinct experts (uniform routing: E (1 - (1 - 1/E)^pairs)).
-static int pick_rowt(int tiles, double est_active, int sms) {
+// Row tiles per CTA for the expected number of distinct experts (uniform routing:
+// E (1 - (1 - 1/E)^pairs)). Large passes (>= 24 tokens, shared memory for one CTA per SM) take
+// 16-warp CTAs with one full-K row tile per warp; otherwise the largest of 8/4/2/1 tiles per 8-warp
+// CTA that still gives >= 2 CTAs per SM (fewer tiles per CTA split K across more warps).
+static int pick_rowt(int tiles, int tpp, double est_active, int sms) {
+  if (tpp >= 24 && tiles >= 16 && est_active * ceil_div(tiles, 16) >= 2.0 * sms) return 16;
   for (int r = 8; r >= 1; r >>= 1) {
     if (r > tiles) continue;
     if (est_active * ceil_div(tiles, r) >= 2.0 * sms) return r;
@@ -352,7 +368,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   gp.perm = L->perm;
   gp.active = L->active;
   gp.n_active = L->n_active;
-  MOE_TRY(launch_expert_gemv(L->d.wdtype, gp, max_active, pick_rowt(gp.tiles, est, L->sms), st));
+  MOE_TRY(launch_expert_gemv(L->d.wdtype, gp, max_active, pick_rowt(gp.tiles, gp.tpp, est, L->sms), st));
   MOE_TRY(mark(events, 2, st));
 
   ExpertParams dp = gp;
@@ -370,7 +386,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   dp.h_in = L->h;
   dp.route_w = weights;
   dp.out = L->ypair;
-  MOE_TRY(launch_expert_gemv(L->d.wdtype, dp, max_active, pick_rowt(dp.tiles, est, L->sms), st));
+  MOE_TRY(launch_expert_gemv(L->d.wdtype, dp, max_active, pick_rowt(dp.tiles, dp.tpp, est, L->sms), st));
   MOE_TRY(mark(events, 3, st));
   MOE_TRY(launch_combine(L->ypair, ids, T, width, H, E, y, st));
   return mark(events, 4, st);
@@ -413,11 +429,13 @@ size_t moe_last_error(char* buf, size_t n) {
 
 moe_status moe_route_tokens(const void* x, const void* w_router, const float* bias, int T, int H, int E, int k,
                             int mode, int n_group, int topk_group, float routed_scale, uint32_t* ids,
-                            float* weights, void* stream) {
+                            float* weights, void* workspace, size_t workspace_bytes, void* stream) {
   RouteParams p{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w_router), bias, ids,
                 weights, T, H, E, k, mode, n_group, topk_group, routed_scale};
-  return route_tokens(p, static_cast<cudaStream_t>(stream));
+  return route_tokens(p, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
+
+size_t moe_route_workspace_bytes(int T, int E) { return route_workspace_bytes(T, E); }
 
 moe_status moe_plan_pairs(const uint32_t* ids, int n_pairs, int E, int32_t* counts, int32_t* offsets,
                           int32_t* perm, int32_t* active, int32_t* n_active, void* workspace,

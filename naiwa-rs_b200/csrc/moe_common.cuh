@@ -73,10 +73,11 @@ __device__ __forceinline__ uint32_t total_key_u(float f) {
   return (uint32_t)b ^ 0x80000000u;
 }
 
-// Streaming 16-byte load that does not allocate in L1 (weights are read once per launch).
+// Streaming 16-byte load that does not allocate in L1 (weights are read once per launch). The
+// data is read-only for the kernel's lifetime, so the asm is not volatile and may be scheduled freely.
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
   return v;
@@ -84,30 +85,48 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
 
 __device__ __forceinline__ uint4 ldg_nc(const void* p) {
   uint4 v;
-  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
   return v;
 }
 
-__device__ __forceinline__ uint4 lds128(const void* p) {
-  uint4 v;
-  uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
-  return v;
-}
+// 16-byte shared load as a plain C++ access, so the compiler keeps it ordered against barriers.
+__device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
 // D = A(16x16, row) * B(16x8, col) + C, f32 accumulate (warp-level tensor-core MMA).
 __device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// D = A * B (no accumulator input): the first MMA of a block-scaled partial sum.
+__device__ __forceinline__ void mma_f16_zero(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm(
+      "{.reg .f32 z; mov.f32 z, 0f00000000;\n"
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {z,z,z,z};}"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// (d0, d1) += s * (t0, t1) as one packed f32x2 fused multiply-add (sm_100).
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float s, float t0, float t1) {
+  asm(
+      "{.reg .b64 t, c, s2;\n"
+      "mov.b64 t, {%2, %3};\n"
+      "mov.b64 c, {%0, %1};\n"
+      "mov.b64 s2, {%4, %4};\n"
+      "fma.rn.f32x2 c, s2, t, c;\n"
+      "mov.b64 {%0, %1}, c;}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(t0), "f"(t1), "f"(s));
+}
+
 __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

@@ -13,7 +13,8 @@ struct RouteParams {
   int T, H, E, k, mode, n_group, topk_group;
   float routed_scale;
 };
-moe_status route_tokens(const RouteParams& p, cudaStream_t st);
+moe_status route_tokens(const RouteParams& p, void* ws, size_t ws_bytes, cudaStream_t st);
+size_t route_workspace_bytes(int T, int E);
 
 struct PlanOut {
   int32_t* counts;    // [E]
@@ -54,7 +55,7 @@ moe_status launch_expert_gemv(int wdtype, ExpertParams p, int max_active, int ro
 moe_status launch_combine(const float* ypair, const uint32_t* ids, int T, int width, int H, int E, void* y,
                           cudaStream_t st);
 int choose_tpp(int K, double mean_tokens_per_expert);
-size_t expert_smem_bytes(int K, int tpp, int rowt);
+size_t expert_smem_bytes(int K, int tpp, int rowt, int warps);
 
 int64_t device_q_bytes(int wdtype, int N, int K);
 int64_t device_s_bytes(int wdtype, int N, int K);

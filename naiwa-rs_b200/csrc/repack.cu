@@ -6,7 +6,8 @@
 // are its m16n8k16 A-operand values for the block's two k16 steps:
 //   byte/element j of a k16 step -> (row g + 8*((j>>1)&1), column (j>=4 ? 8 : 0) + 2c + (j&1)),
 //   g = l/4, c = l%4.
-// Q8_0 scales go to a separate array: per tile and group of 4 blocks, 8 x 4 pairs {d(row g),
+// Q8_0 quants are stored biased (u = q + 128, the sign bit flipped) so the kernel's int8 -> f16
+// conversion needs no XOR. Q8_0 scales go to a separate array: per tile and group of 4 blocks, 8 x 4 pairs {d(row g),
 // d(row g+8)} (128 B), so one 16-byte load gives a lane its two rows' scales for 4 blocks.
 // Gate and up are merged: tile t holds gate rows 8t..8t+7 then up rows 8t..8t+7, which puts a
 // gate value and its up partner in the same thread after the MMA (SwiGLU in registers).
@@ -55,7 +56,7 @@ __global__ void repack_q8_kernel(RepackSrc s, int E, int tiles, uint8_t* __restr
     int r, kk;
     frag_pos(lane, j & 7, &r, &kk);
     const int k = (j >> 3) * 16 + kk;
-    out[j] = src_row(s, e, tile, r, row_bytes)[kb * 34 + 2 + k];
+    out[j] = src_row(s, e, tile, r, row_bytes)[kb * 34 + 2 + k] ^ 0x80;  // stored as u = q + 128
   }
   uint4 v;
   memcpy(&v, out, 16);

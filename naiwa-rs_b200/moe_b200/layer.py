@@ -188,6 +188,8 @@ class RoutedExperts:
             raise MoeError(_lib.MOE_ERR_INVALID, "forward: xs must be a CUDA bf16 tensor")
         x2 = x2.contiguous()
         T = x2.shape[0]
+        if T == 0:
+            return (out if out is not None else torch.empty_like(x2)).reshape(shape)
         ids = topk_ids.reshape(T, -1)
         if ids.dtype not in (torch.int32, torch.uint32) or not ids.is_cuda:
             ids = ids.to(device=x2.device, dtype=torch.int32)
@@ -233,8 +235,10 @@ def route_tokens(x, w_router, k: int, mode: int, bias=None, n_group: int = 1, to
     E = w_router.shape[0]
     ids = torch.empty((T, k), dtype=torch.int32, device=x.device)
     w = torch.empty((T, k), dtype=torch.float32, device=x.device)
+    ws_bytes = int(lib().moe_route_workspace_bytes(T, E))
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=x.device)
     check(lib().moe_route_tokens(_ptr(x.contiguous()), _ptr(w_router.contiguous()), _ptr(bias), T, H, E, k, mode,
-                                 n_group, topk_group, float(routed_scale), _ptr(ids), _ptr(w),
+                                 n_group, topk_group, float(routed_scale), _ptr(ids), _ptr(w), _ptr(ws), ws_bytes,
                                  ctypes.c_void_p(_stream(stream))))
     return ids, w
 

@@ -64,8 +64,8 @@ def test_host_side_validation_needs_no_gpu():
     d = _lib.LayerDesc(num_experts=8, top_k=2, hidden=64, inter=32, wdtype=9, max_tokens=4)
     assert L.moe_layer_create(ctypes.byref(d), ctypes.byref(out)) == _lib.MOE_ERR_UNSUPPORTED
     # router: k > E and hidden not a multiple of 8 are rejected before any launch
-    assert L.moe_route_tokens(None, None, None, 1, 64, 8, 9, 1, 1, 1, 1.0, None, None, None) == _lib.MOE_ERR_INVALID
-    assert L.moe_route_tokens(None, None, None, 1, 60, 8, 2, 1, 1, 1, 1.0, None, None, None) == _lib.MOE_ERR_INVALID
+    assert L.moe_route_tokens(None, None, None, 1, 64, 8, 9, 1, 1, 1, 1.0, None, None, None, 0, None) == _lib.MOE_ERR_INVALID
+    assert L.moe_route_tokens(None, None, None, 1, 60, 8, 2, 1, 1, 1, 1.0, None, None, None, 0, None) == _lib.MOE_ERR_INVALID
     assert L.moe_plan_pairs(None, 4, 0, None, None, None, None, None, None, 0, None, None) == _lib.MOE_ERR_INVALID
     assert L.moe_forward(None, None, 1, None, None, 1, None, None) == _lib.MOE_ERR_INVALID
     assert L.moe_layer_device_bytes(None) == 0
@@ -78,3 +78,4 @@ def test_plan_workspace_sizes():
     L = _lib.lib()
     assert L.moe_plan_workspace_bytes(2048, 128) == 0  # single-CTA plan
     assert L.moe_plan_workspace_bytes(65536, 256) == 64 * 256 * 4
+    assert L.moe_route_workspace_bytes(1, 128) == 512 + 4
