@@ -144,6 +144,23 @@ moe_status moe_plan_pairs(const uint32_t* ids, int n_pairs, int E, int32_t* coun
                           size_t workspace_bytes, int32_t* error_word, void* stream);
 size_t moe_plan_workspace_bytes(int n_pairs, int E);
 
+/* Router logits + top-k for callers that cannot allocate device memory. No counterpart in the
+ * reference: its router runs inside the model it links against. Some callers of this library have
+ * no allocator to give moe_route_tokens its workspace: a host binding that owns no CUDA allocator
+ * and only forwards pointers it was handed, code running while a stream capture is active (a
+ * cudaMalloc there breaks the capture), or an embedding that fixes the library's device memory up
+ * front. This call runs the same router kernel with its workspace in a file-scope device array of
+ * MOE_ROUTE_NOALLOC_MAX_BYTES, which every GPU that loads the library holds until the process exits.
+ * It never allocates or frees. Calls needing more than the array (moe_route_workspace_bytes(T, E)
+ * above the maximum) fail with MOE_ERR_INVALID. The first call on a device looks up the array's
+ * device address; make that first call before any stream capture. All calls on a device share the
+ * array: calls that overlap on the GPU (different streams without ordering) race and give wrong
+ * results. Arguments and results are those of moe_route_tokens without the workspace. */
+#define MOE_ROUTE_NOALLOC_MAX_BYTES (1u << 20)
+moe_status moe_route_tokens_noalloc(const void* x, const void* w_router, const float* bias, int T, int H, int E,
+                                    int k, int mode, int n_group, int topk_group, float routed_scale, uint32_t* ids,
+                                    float* weights, void* stream);
+
 /* Library version string. */
 const char* moe_version(void);
 

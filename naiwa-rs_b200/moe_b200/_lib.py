@@ -83,6 +83,7 @@ def lib():
             "moe_last_error": (ctypes.c_size_t, [ctypes.c_char_p, ctypes.c_size_t]),
             "moe_route_tokens": (i, [P, P, P, i, i, i, i, i, i, i, f, P, P, P, ctypes.c_size_t, P]),
             "moe_route_workspace_bytes": (ctypes.c_size_t, [i, i]),
+            "moe_route_tokens_noalloc": (i, [P, P, P, i, i, i, i, i, i, i, f, P, P, P]),
             "moe_plan_pairs": (i, [P, i, i, P, P, P, P, P, P, ctypes.c_size_t, P, P]),
             "moe_plan_workspace_bytes": (ctypes.c_size_t, [i, i]),
             "moe_version": (ctypes.c_char_p, []),
