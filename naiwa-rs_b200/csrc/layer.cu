@@ -78,6 +78,18 @@ struct moe_layer {
   float* ypair = nullptr;
   void* route_ws = nullptr;
   size_t route_ws_bytes = 0;
+  // tensor-core path (Q4_K / FP8): tile-major weights, f16 staging, TMA maps
+  bool tc = false;
+  float* gu_scale = nullptr;
+  float* dn_scale = nullptr;
+  void* x16 = nullptr;
+  float* xscale = nullptr;
+  void* h16 = nullptr;
+  float* hscale = nullptr;
+  int32_t* tile_list = nullptr;
+  int32_t* n_tiles = nullptr;
+  alignas(128) unsigned char tmap_x[128];
+  alignas(128) unsigned char tmap_h[128];
   int64_t weight_bytes = 0;
   int64_t scratch_bytes = 0;
 };
@@ -95,6 +107,15 @@ static void free_scratch(moe_layer* L) {
   cudaFree(L->route_ws);
   L->route_ws = nullptr;
   L->route_ws_bytes = 0;
+  cudaFree(L->x16);
+  cudaFree(L->xscale);
+  cudaFree(L->h16);
+  cudaFree(L->hscale);
+  cudaFree(L->tile_list);
+  cudaFree(L->n_tiles);
+  L->x16 = L->h16 = nullptr;
+  L->xscale = L->hscale = nullptr;
+  L->tile_list = L->n_tiles = nullptr;
   L->counts = L->offsets = L->perm = L->active = L->n_active = L->err = nullptr;
   L->plan_ws = nullptr;
   L->h = L->ypair = nullptr;
@@ -135,6 +156,16 @@ static moe_status alloc_scratch(moe_layer* L, int max_tokens) {
   L->route_ws_bytes = route_workspace_bytes(max_tokens, E);
   MOE_TRY(dalloc(&L->route_ws, L->route_ws_bytes, &acc));
   MOE_CUDA_TRY(cudaMemset(L->route_ws, 0, L->route_ws_bytes));  // arrival counters start at zero
+  if (L->tc) {
+    MOE_TRY(dalloc(&L->x16, (size_t)cap * H * 2, &acc));
+    MOE_TRY(dalloc(&L->xscale, sizeof(float) * cap, &acc));
+    MOE_TRY(dalloc(&L->h16, (size_t)cap * I * 2, &acc));
+    MOE_TRY(dalloc(&L->hscale, sizeof(float) * cap, &acc));
+    MOE_TRY(dalloc(&L->tile_list, sizeof(int32_t) * ((size_t)cap / TC_BN + E + 1), &acc));
+    MOE_TRY(dalloc(&L->n_tiles, sizeof(int32_t), &acc));
+    MOE_TRY(make_row_tmap(L->tmap_x, L->x16, cap, H));
+    MOE_TRY(make_row_tmap(L->tmap_h, L->h16, cap, I));
+  }
   L->cap_pairs = cap;
   L->cap_tokens = max_tokens;
   L->scratch_bytes = acc;
@@ -148,6 +179,9 @@ static void free_weights(moe_layer* L) {
   cudaFree(L->dn_s);
   cudaFree(L->router_w);
   cudaFree(L->router_b);
+  cudaFree(L->gu_scale);
+  cudaFree(L->dn_scale);
+  L->gu_scale = L->dn_scale = nullptr;
   L->gu_q = L->gu_s = L->dn_q = L->dn_s = nullptr;
   L->router_w = nullptr;
   L->router_b = nullptr;
@@ -189,8 +223,14 @@ static moe_status validate_desc(const moe_layer_desc* d) {
   if (d->hidden <= 0 || d->inter <= 0) return fail(MOE_ERR_INVALID, "hidden and inter must be positive");
   if (d->hidden % 32 || d->inter % 32)
     return fail(MOE_ERR_INVALID, "hidden and inter must be multiples of 32 (one Q8_0 block / two k16 MMA steps)");
-  if (d->wdtype != MOE_DTYPE_BF16 && d->wdtype != MOE_DTYPE_Q8_0)
-    return fail(MOE_ERR_UNSUPPORTED, "weight format not built for the decode path yet");
+  if (d->wdtype == MOE_DTYPE_Q4_K && (d->hidden % 256 || d->inter % 256))
+    return fail(MOE_ERR_INVALID, "Q4_K needs hidden and inter multiples of 256 (one super-block)");
+  if (d->wdtype == MOE_DTYPE_FP8_E4M3_B128 && (d->hidden % 128 || d->inter % 128))
+    return fail(MOE_ERR_INVALID, "FP8 128x128-block weights need hidden and inter multiples of 128");
+  if (d->wdtype == MOE_DTYPE_FP8_E4M3_B128 && (!d->gate_scale || !d->up_scale || !d->down_scale))
+    return fail(MOE_ERR_INVALID, "FP8 weights need gate_scale, up_scale and down_scale");
+  if (d->wdtype < MOE_DTYPE_BF16 || d->wdtype > MOE_DTYPE_FP8_E4M3_B128)
+    return fail(MOE_ERR_UNSUPPORTED, "unknown weight format");
   if (!d->gate || !d->up || !d->down) return fail(MOE_ERR_INVALID, "null expert stack");
   if (d->max_tokens <= 0) return fail(MOE_ERR_INVALID, "max_tokens must be positive");
   return MOE_OK;
@@ -216,10 +256,11 @@ moe_status moe_layer_create(const moe_layer_desc* desc, moe_layer** out) {
     delete L;
     return st;
   };
-  L->gu_q_stride = device_q_bytes(w, 2 * I, H);
-  L->gu_s_stride = device_s_bytes(w, 2 * I, H);
-  L->dn_q_stride = device_q_bytes(w, H, I);
-  L->dn_s_stride = device_s_bytes(w, H, I);
+  L->tc = (w == MOE_DTYPE_Q4_K || w == MOE_DTYPE_FP8_E4M3_B128);
+  L->gu_q_stride = L->tc ? tc_weight_bytes(w, 2 * I, H) : device_q_bytes(w, 2 * I, H);
+  L->gu_s_stride = L->tc ? 0 : device_s_bytes(w, 2 * I, H);
+  L->dn_q_stride = L->tc ? tc_weight_bytes(w, H, I) : device_q_bytes(w, H, I);
+  L->dn_s_stride = L->tc ? 0 : device_s_bytes(w, H, I);
   int64_t acct = 0;
   moe_status st;
   if ((st = dalloc(&L->gu_q, (size_t)(L->gu_q_stride * E), &acct)) != MOE_OK) return cleanup(st);
@@ -233,12 +274,32 @@ moe_status moe_layer_create(const moe_layer_desc* desc, moe_layer** out) {
     st = stage_source(desc->gate, gb, on_dev, &g, &og);
     if (st == MOE_OK) st = stage_source(desc->up, gb, on_dev, &u, &ou);
     if (st == MOE_OK) st = stage_source(desc->down, gb, on_dev, &dn, &od);
-    if (st == MOE_OK) st = repack_projection(w, g, u, E, I, H, L->gu_q, L->gu_s, 0);
-    if (st == MOE_OK) st = repack_projection(w, dn, nullptr, E, H, I, L->dn_q, L->dn_s, 0);
+    uint8_t *gs = nullptr, *us = nullptr, *ds = nullptr;
+    bool ogs = false, ous = false, ods = false;
+    if (L->tc) {
+      if (st == MOE_OK && w == MOE_DTYPE_FP8_E4M3_B128) {
+        const int64_t gsb = (int64_t)E * (I / 128) * (H / 128) * 4;
+        st = stage_source(desc->gate_scale, gsb, on_dev, &gs, &ogs);
+        if (st == MOE_OK) st = stage_source(desc->up_scale, gsb, on_dev, &us, &ous);
+        if (st == MOE_OK) st = stage_source(desc->down_scale, gsb, on_dev, &ds, &ods);
+        if (st == MOE_OK) st = dalloc(&L->gu_scale, sizeof(float) * tc_scale_count(w, 2 * I, H) * E, &acct);
+        if (st == MOE_OK) st = dalloc(&L->dn_scale, sizeof(float) * tc_scale_count(w, H, I) * E, &acct);
+      }
+      if (st == MOE_OK)
+        st = tc_repack(w, g, u, (const float*)gs, (const float*)us, E, I, H, L->gu_q, L->gu_scale, 0);
+      if (st == MOE_OK)
+        st = tc_repack(w, dn, nullptr, (const float*)ds, (const float*)ds, E, H, I, L->dn_q, L->dn_scale, 0);
+    } else {
+      if (st == MOE_OK) st = repack_projection(w, g, u, E, I, H, L->gu_q, L->gu_s, 0);
+      if (st == MOE_OK) st = repack_projection(w, dn, nullptr, E, H, I, L->dn_q, L->dn_s, 0);
+    }
     cudaError_t se = cudaDeviceSynchronize();
     if (og) cudaFree(g);
     if (ou) cudaFree(u);
     if (od) cudaFree(dn);
+    if (ogs) cudaFree(gs);
+    if (ous) cudaFree(us);
+    if (ods) cudaFree(ds);
     if (st != MOE_OK) return cleanup(st);
     if (se != cudaSuccess) return cleanup(cuda_fail(se, "repack"));
   }
@@ -348,6 +409,46 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   MOE_TRY(mark(events, 1, st));
   const int max_active = n_pairs < E ? n_pairs : E;
   const double est = (double)E * (1.0 - std::pow(1.0 - 1.0 / E, (double)n_pairs));
+  if (L->tc) {
+    const int w = L->d.wdtype;
+    MOE_TRY(tc_tile_list(L->counts, L->active, L->n_active, L->tile_list, L->n_tiles, st));
+    MOE_TRY(tc_gather(x, nullptr, H, width, L->perm, n_pairs, L->x16, L->xscale, st));
+    TcArgs ga{};
+    ga.w = L->gu_q;
+    ga.wscale = L->gu_scale;
+    ga.w_stride = L->gu_q_stride;
+    ga.N_rows = 2 * I;
+    ga.K = H;
+    ga.phase = 0;
+    ga.tile_list = L->tile_list;
+    ga.n_tiles = L->n_tiles;
+    ga.offsets = L->offsets;
+    ga.active = L->active;
+    ga.perm = L->perm;
+    ga.tscale = L->xscale;
+    ga.route_w = weights;
+    ga.out = L->h;
+    ga.err = L->err;
+    ga.tmap = L->tmap_x;
+    ga.max_tiles = (n_pairs + TC_BN - 1) / TC_BN + max_active;
+    MOE_TRY(tc_gemm(w, ga, st));
+    MOE_TRY(mark(events, 2, st));
+    MOE_TRY(tc_gather(nullptr, L->h, I, width, L->perm, n_pairs, L->h16, L->hscale, st));
+    TcArgs da = ga;
+    da.w = L->dn_q;
+    da.wscale = L->dn_scale;
+    da.w_stride = L->dn_q_stride;
+    da.N_rows = H;
+    da.K = I;
+    da.phase = 1;
+    da.tscale = L->hscale;
+    da.out = L->ypair;
+    da.tmap = L->tmap_h;
+    MOE_TRY(tc_gemm(w, da, st));
+    MOE_TRY(mark(events, 3, st));
+    MOE_TRY(launch_combine(L->ypair, ids, T, width, H, E, y, st));
+    return mark(events, 4, st);
+  }
 
   ExpertParams gp{};
   gp.wq = L->gu_q;

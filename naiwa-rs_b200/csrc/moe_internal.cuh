@@ -62,4 +62,30 @@ int64_t device_s_bytes(int wdtype, int N, int K);
 moe_status repack_projection(int wdtype, const uint8_t* a, const uint8_t* b, int E, int N_src, int K, uint8_t* dq,
                              uint8_t* ds, cudaStream_t st);
 
+// tensor-core (tcgen05) grouped GEMM path for Q4_K and FP8 layers
+struct TcArgs {
+  const uint8_t* w;
+  const float* wscale;
+  int64_t w_stride;
+  int N_rows, K, phase;
+  const int32_t *tile_list, *n_tiles, *offsets, *active, *perm;
+  const float *tscale, *route_w;
+  float* out;
+  int32_t* err;
+  const void* tmap;
+  int max_tiles;  // grid bound on (expert, token-tile) entries
+};
+constexpr int TC_BN = 128;  // tokens per tensor-core tile
+moe_status make_row_tmap(void* map_out, const void* base, int64_t rows, int cols);
+size_t tensor_map_bytes();
+int64_t tc_weight_bytes(int wdtype, int N, int K);
+int64_t tc_scale_count(int wdtype, int N, int K);
+moe_status tc_repack(int wdtype, const uint8_t* a, const uint8_t* b, const float* sa, const float* sb, int E, int N_src,
+                     int K, uint8_t* dst, float* dscale, cudaStream_t st);
+moe_status tc_gather(const void* x_bf16, const float* x_f32, int K, int width, const int32_t* perm, int n_pairs,
+                     void* out_f16, float* scale, cudaStream_t st);
+moe_status tc_tile_list(const int32_t* counts, const int32_t* active, const int32_t* n_active, int32_t* list,
+                        int32_t* n_list, cudaStream_t st);
+moe_status tc_gemm(int wdtype, const TcArgs& a, cudaStream_t st);
+
 }  // namespace moe
