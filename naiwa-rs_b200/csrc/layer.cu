@@ -379,9 +379,15 @@ moe_status moe_forward_marked(moe_layer* L, const void* x, int T, const uint32_t
 
 }  // extern "C"
 
+// Stage marker: under stream capture the event becomes an external event-record node of the graph;
+// outside capture it is a plain record.
 static moe_status mark(void* const* events, int i, cudaStream_t st) {
   if (!events) return MOE_OK;
-  MOE_CUDA_TRY(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[i]), st, cudaEventRecordExternal));
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  MOE_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
+  cudaEvent_t ev = static_cast<cudaEvent_t>(events[i]);
+  if (cs == cudaStreamCaptureStatusActive) MOE_CUDA_TRY(cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal));
+  else MOE_CUDA_TRY(cudaEventRecord(ev, st));
   return MOE_OK;
 }
 
