@@ -21,9 +21,12 @@
 // stops issuing work, waits (bounded) for its own MMAs, frees its TMEM and returns.
 //
 // Weight layouts in HBM (tile-major, built by the repack kernels below):
-//   FP8:  per (expert, 128-row tile, 128-column chunk) 16 KB of e4m3, row-major inside; the
+//   FP8:  per (expert, 128-row tile, 128-column chunk) 16 KB of e4m3, rows of 128 B with 16-byte
+//         chunk j of row r stored at j ^ (r % 8); the
 //         128x128 block scale of that chunk in a separate f32 array.
-//   Q4_K: per (expert, 128-row tile, 256-column super-block) the tile's 128 GGML blocks (144 B each).
+//   Q4_K: per (expert, 128-row tile, 256-column super-block) the 128 rows' quant bytes (16 KB, same
+//         chunk swizzle) and
+//         their per-sub-block f16 pairs {d*sc, -dmin*m} (4 KB), precomputed at repack.
 // Gate/up tiles hold, per 32-row group, 16 gate rows then the 16 up rows of the same columns, so
 // one warp holds a gate value and its up partner after tcgen05.ld (SwiGLU by one shuffle).
 #include <cuda.h>
@@ -36,11 +39,17 @@ namespace tc {
 constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int BK = 128;
-constexpr int THREADS = 256;
+constexpr int DQ_WARPS = 16;                       // dequantise (and run the epilogue)
+constexpr int DQ_THREADS = DQ_WARPS * 32;
+constexpr int MMA_WARP = DQ_WARPS;                  // issues the tensor-core MMAs
+constexpr int LOAD_WARP = DQ_WARPS + 1;             // issues the weight-unit and token-tile copies
+constexpr int THREADS = DQ_THREADS + 64;
 constexpr int A_BYTES = BM * BK * 2;  // one stage of f16 weights
 constexpr int B_BYTES = BN * BK * 2;  // one stage of f16 tokens
-constexpr int STAGES = 2;
-constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + 1024 /* alignment */ + 256 /* barriers */;
+constexpr int STAGES = 2;             // dequantised weight stages
+constexpr int BSTAGES = 3;            // token-tile stages, loaded two chunks ahead
+constexpr int Q4K_UNIT = BM * 128 + BM * 32;
+constexpr int TMA_ROWS = 32;  // token rows per TMA box  // Q4_K unit: quants + per-sub-block scale pairs
 constexpr uint32_t WAIT_POLLS = 1u << 22;             // backstop on try_wait polls
 constexpr uint64_t WAIT_NS = 200ull * 1000ull * 1000ull;  // a wait longer than 200 ms is declared stuck
 
@@ -159,25 +168,32 @@ struct GemmParams {
   int32_t* err;
 };
 
+// Weight formats. Weights stream through a shared-memory ring in "units" (one contiguous 1-D bulk
+// copy each); each dequant thread then reads the 32 weights it owns of a 128-column chunk.
 struct FP8W {
-  // thread (row r, half q) -> 64 weights of K-chunk kc: 4 x 16 B
+  static constexpr int UNIT_BYTES = BM * BK;  // one 128-column chunk of the tile: 16 KB
+  static constexpr int CHUNKS_PER_UNIT = 1;
+  static constexpr int RING = 3;
   struct Raw {
-    uint4 q[4];
+    uint4 q[2];
     float s;
   };
-  __device__ static __forceinline__ void load(const GemmParams& p, int e, int tile, int kc, int r, int q, Raw& raw) {
-    const int kchunks = p.K / BK;
-    const uint8_t* base = p.w + (int64_t)e * p.w_stride + ((int64_t)tile * kchunks + kc) * (BM * BK) + r * BK + q * 64;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) raw.q[i] = ldg_stream(base + i * 16);
-    // merged gate/up tiles carry two scales per chunk: rows 16..31 of each 32-row group are up rows
-    raw.s = __ldg(p.wscale + (((int64_t)e * p.tiles + tile) * kchunks + kc) * 2 + ((r & 31) >> 4));
+  __device__ static __forceinline__ const uint8_t* unit_src(const GemmParams& p, int e, int tile, int u) {
+    return p.w + (int64_t)e * p.w_stride + ((int64_t)tile * (p.K / BK) + u) * UNIT_BYTES;
   }
-  // 64 f16 values as 8 chunks of 16 bytes
-  __device__ static __forceinline__ void dequant(const Raw& raw, uint4 (&out)[8]) {
+  // thread (row r, quarter qq): 32 e4m3 bytes of chunk kc
+  __device__ static __forceinline__ void read(const GemmParams& p, const unsigned char* unit, int e, int tile, int kc,
+                                              int r, int qq, Raw& raw) {
+    const unsigned char* row = unit + r * BK;
+    raw.q[0] = *reinterpret_cast<const uint4*>(row + (((2 * qq) ^ (r & 7)) << 4));
+    raw.q[1] = *reinterpret_cast<const uint4*>(row + (((2 * qq + 1) ^ (r & 7)) << 4));
+    // merged gate/up tiles carry two scales per chunk: rows 16..31 of each 32-row group are up rows
+    raw.s = __ldg(p.wscale + (((int64_t)e * p.tiles + tile) * (p.K / BK) + kc) * 2 + ((r & 31) >> 4));
+  }
+  __device__ static __forceinline__ void dequant(const Raw& raw, int, int, uint4 (&out)[4]) {
     const __half2 s2 = __float2half2_rn(raw.s);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 2; ++i) {
       const uint32_t w[4] = {raw.q[i].x, raw.q[i].y, raw.q[i].z, raw.q[i].w};
       uint32_t h[8];
 #pragma unroll
@@ -195,98 +211,112 @@ struct FP8W {
       out[2 * i + 1] = make_uint4(h[4], h[5], h[6], h[7]);
     }
   }
+  // 16-byte chunk index (within the 64-column atom row) of out[j]: 32 bytes -> chunks 4 (qq%2) + j
+  __device__ static __forceinline__ int chunk_of(int qq, int j) { return (qq & 1) * 4 + j; }
 };
 
 struct Q4KW {
+  static constexpr int UNIT_BYTES = Q4K_UNIT;  // one 256-column super-block of the tile: 20 KB
+  static constexpr int CHUNKS_PER_UNIT = 2;
+  static constexpr int RING = 3;
   struct Raw {
-    uint4 hdr;   // d, dmin, scales[12]
-    uint4 q[2];  // 32 bytes of nibbles
+    uint4 q;     // 16 quant bytes: low nibbles of sub-block 2c, high nibbles of 2c + 1
+    uint2 s;     // {d*sc, -dmin*m} f16 pairs of sub-blocks 2c and 2c + 1
   };
-  __device__ static __forceinline__ void load(const GemmParams& p, int e, int tile, int kc, int r, int q, Raw& raw) {
-    const int sbs = p.K / 256;
-    const int sb = kc >> 1;                    // super-block of this 128-column chunk
-    const int c = ((kc & 1) << 1) | q;         // 64-column quarter of the super-block
-    const uint8_t* blk = p.w + (int64_t)e * p.w_stride + ((int64_t)tile * sbs + sb) * (BM * 144) + r * 144;
-    raw.hdr = ldg_nc(blk);
-    raw.q[0] = ldg_stream(blk + 16 + c * 32);
-    raw.q[1] = ldg_stream(blk + 16 + c * 32 + 16);
+  __device__ static __forceinline__ const uint8_t* unit_src(const GemmParams& p, int e, int tile, int u) {
+    return p.w + (int64_t)e * p.w_stride + ((int64_t)tile * (p.K / 256) + u) * UNIT_BYTES;
   }
-  __device__ static __forceinline__ void dequant_c(const Raw& raw, int c, uint4 (&out)[8]) {
-    const uint32_t hw[4] = {raw.hdr.x, raw.hdr.y, raw.hdr.z, raw.hdr.w};
-    const __half2 dd = *reinterpret_cast<const __half2*>(&hw[0]);
-    const float d = __low2float(dd), dmin = __high2float(dd);
-    const uint8_t* sc = reinterpret_cast<const uint8_t*>(&hw[1]);
-    float dl[2], ml[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int j = 2 * c + h;
-      int s, m;
-      if (j < 4) {
-        s = sc[j] & 63;
-        m = sc[j + 4] & 63;
-      } else {
-        s = (sc[j + 4] & 0xf) | ((sc[j - 4] >> 6) << 4);
-        m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
-      }
-      dl[h] = d * (float)s;
-      ml[h] = dmin * (float)m;
-    }
+  // thread (row r, quarter qq) of chunk kc: 64-column quarter c = 2 (kc % 2) + qq / 2 of the
+  // super-block, quant bytes 32 c + 16 (qq % 2) .. +15
+  __device__ static __forceinline__ void read(const GemmParams&, const unsigned char* unit, int, int, int kc, int r,
+                                              int qq, Raw& raw) {
+    const int c = ((kc & 1) << 1) | (qq >> 1);
+    raw.q = *reinterpret_cast<const uint4*>(unit + r * 128 + (((2 * c + (qq & 1)) ^ (r & 7)) << 4));
+    raw.s = *reinterpret_cast<const uint2*>(unit + BM * 128 + r * 32 + c * 8);
+  }
+  // out[0..1]: the 16 low-nibble weights (columns 16 (qq%2) .. +15 of the atom row),
+  // out[2..3]: the 16 high-nibble weights (columns 32 + 16 (qq%2) .. +15)
+  __device__ static __forceinline__ void dequant(const Raw& raw, int, int, uint4 (&out)[4]) {
     const __half2 bias = __float2half2_rn(1024.0f);
-    const uint32_t w[8] = {raw.q[0].x, raw.q[0].y, raw.q[0].z, raw.q[0].w, raw.q[1].x, raw.q[1].y, raw.q[1].z, raw.q[1].w};
+    const __half2 p0 = *reinterpret_cast<const __half2*>(&raw.s.x), p1 = *reinterpret_cast<const __half2*>(&raw.s.y);
+    const __half2 d0 = __low2half2(p0), m0 = __high2half2(p0), d1 = __low2half2(p1), m1 = __high2half2(p1);
+    const uint32_t w[4] = {raw.q.x, raw.q.y, raw.q.z, raw.q.w};
+    uint32_t lo[8], hi[8];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {  // h = 0: low nibbles (sub-block 2c), 1: high nibbles (2c + 1)
-      const __half2 d2 = __float2half2_rn(dl[h]);
-      const __half2 m2 = __float2half2_rn(-ml[h]);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {  // 8 bytes -> 8 weights per output chunk
-        uint32_t o[4];
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          const uint32_t word = w[2 * i + t];
-          const uint32_t nib = h ? (word >> 4) & 0x0f0f0f0fu : word & 0x0f0f0f0fu;
-          uint32_t lo = __byte_perm(nib, 0x64646464u, 0x4140);  // 1024 + q
-          uint32_t hi = __byte_perm(nib, 0x64646464u, 0x4342);
-          __half2 a = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&lo), bias), d2, m2);
-          __half2 b = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&hi), bias), d2, m2);
-          o[2 * t] = *reinterpret_cast<uint32_t*>(&a);
-          o[2 * t + 1] = *reinterpret_cast<uint32_t*>(&b);
-        }
-        out[4 * h + i] = make_uint4(o[0], o[1], o[2], o[3]);
-      }
+    for (int t = 0; t < 4; ++t) {
+      const uint32_t nl = w[t] & 0x0f0f0f0fu, nh = (w[t] >> 4) & 0x0f0f0f0fu;
+      uint32_t a0 = __byte_perm(nl, 0x64646464u, 0x4140), a1 = __byte_perm(nl, 0x64646464u, 0x4342);
+      uint32_t b0 = __byte_perm(nh, 0x64646464u, 0x4140), b1 = __byte_perm(nh, 0x64646464u, 0x4342);
+      __half2 x0 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&a0), bias), d0, m0);
+      __half2 x1 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&a1), bias), d0, m0);
+      __half2 y0 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&b0), bias), d1, m1);
+      __half2 y1 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&b1), bias), d1, m1);
+      lo[2 * t] = *reinterpret_cast<uint32_t*>(&x0);
+      lo[2 * t + 1] = *reinterpret_cast<uint32_t*>(&x1);
+      hi[2 * t] = *reinterpret_cast<uint32_t*>(&y0);
+      hi[2 * t + 1] = *reinterpret_cast<uint32_t*>(&y1);
     }
+    out[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    out[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+    out[2] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    out[3] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
   }
+  // 16-byte chunk index (within the 64-column atom row) of out[j]
+  __device__ static __forceinline__ int chunk_of(int qq, int j) { return (j >> 1) * 4 + (qq & 1) * 2 + (j & 1); }
 };
 
-template <class W>
-__device__ __forceinline__ void dequant_any(const typename W::Raw& raw, int c, uint4 (&out)[8]);
-template <>
-__device__ __forceinline__ void dequant_any<FP8W>(const FP8W::Raw& raw, int, uint4 (&out)[8]) {
-  FP8W::dequant(raw, out);
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
-template <>
-__device__ __forceinline__ void dequant_any<Q4KW>(const Q4KW::Raw& raw, int c, uint4 (&out)[8]) {
-  Q4KW::dequant_c(raw, c, out);
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+template <class W>
+constexpr int gemm_smem_bytes() {
+  return W::RING * W::UNIT_BYTES + STAGES * A_BYTES + BSTAGES * B_BYTES + 1024 + 256;
 }
 
 // ---- the GEMM ------------------------------------------------------------------------------------
+//
+// Warp roles, all hand-offs through mbarriers (no CTA-wide barrier inside the loop):
+//   * warps 0..15 dequantise: chunk kc waits for its weight unit in the ring and for the A stage
+//     (kc % 2) to be free (MMAs of chunk kc - 2 done), writes the stage, fences the generic-to-async
+//     proxy, and each warp's lane 0 arrives on a_full[kc % 2]; after the last chunk of a unit they
+//     arrive on raw_free[slot];
+//   * warp 16 (one lane) waits for a_full and b_full of each chunk, issues its 8 MMAs and commits
+//     them to mma_done[kc % 3], which frees the A and the B stage;
+//   * warp 17 (one lane) keeps the weight ring RING units ahead (1-D bulk copies, each after the
+//     slot's raw_free) and the token tiles three chunks ahead (2-D TMA, each after the MMAs that read
+//     the stage).
+// Any wait that runs past its limit sets s_abort; every role stops at its next check, the CTA waits
+// (bounded) for what it issued, frees its TMEM and returns.
 
 template <class W>
 __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, const __grid_constant__ CUtensorMap tmap) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   unsigned char* sA = smem;                                // [STAGES][A_BYTES]
-  unsigned char* sB = smem + STAGES * A_BYTES;             // [STAGES][B_BYTES]
-  uint64_t* bar_full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);  // TMA landed, per stage
-  uint64_t* bar_mma = bar_full + STAGES;                   // MMAs of the stage done, per stage
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + STAGES);
-  __shared__ int s_abort;
-  __shared__ int s_last_tma, s_last_mma;  // last chunk whose TMA was issued / whose MMAs were committed
+  unsigned char* sB = smem + STAGES * A_BYTES;             // [BSTAGES][B_BYTES]
+  unsigned char* sR = sB + BSTAGES * B_BYTES;              // [RING][UNIT_BYTES] raw weights
+  uint64_t* bar_raw = reinterpret_cast<uint64_t*>(sR + W::RING * W::UNIT_BYTES);  // weight unit landed
+  uint64_t* bar_rawfree = bar_raw + W::RING;               // weight unit fully read
+  uint64_t* bar_bfull = bar_rawfree + W::RING;             // token tile landed
+  uint64_t* bar_afull = bar_bfull + BSTAGES;               // dequantised stage written
+  uint64_t* bar_mma = bar_afull + STAGES;                  // MMAs of chunk c done (slot c % 3)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + BSTAGES);
+  __shared__ volatile int s_abort;
+  __shared__ int s_last_mma, s_last_tma, s_last_raw;  // last chunk/unit committed or issued
 
   const int tiles = p.tiles;
   const int ti = blockIdx.x / tiles;
   const int tile = blockIdx.x % tiles;
   if (ti >= *p.n_tiles) return;
-  // after any CTA of this launch (or an earlier one) gave up on a wait, the rest do no work
+  // after any CTA gave up on a wait, the rest of the launch does no work
   if (p.err && *reinterpret_cast<volatile int32_t*>(p.err) == (int32_t)MOE_ERR_TIMEOUT) return;
   const int entry = p.tile_list[ti];
   const int a_idx = entry >> 16, ntile = entry & 0xffff;
@@ -298,16 +328,23 @@ __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, c
   const int nmma = (nval + 15) & ~15;  // M = 128 needs N % 16 == 0
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kchunks = p.K / BK;
+  const int units = kchunks / W::CHUNKS_PER_UNIT;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&bar_full[s], 1);
+    for (int s = 0; s < W::RING; ++s) {
+      mbar_init(&bar_raw[s], 1);
+      mbar_init(&bar_rawfree[s], DQ_WARPS);
+    }
+    for (int s = 0; s < BSTAGES; ++s) {
+      mbar_init(&bar_bfull[s], 1);
       mbar_init(&bar_mma[s], 1);
     }
+    for (int s = 0; s < STAGES; ++s) mbar_init(&bar_afull[s], DQ_WARPS);  // one arrival per dequant warp
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     s_abort = 0;
-    s_last_tma = -1;
     s_last_mma = -1;
+    s_last_tma = -1;
+    s_last_raw = -1;
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -319,69 +356,119 @@ __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, c
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // thread -> (row, 64-column half) of the weight tile for the dequant
-  const int drow = threadIdx.x >> 1, dq = threadIdx.x & 1;
-  typename W::Raw raw;
-  W::load(p, e, tile, 0, drow, dq, raw);
-  const uint32_t idesc = idesc_f16(nmma);
-  bool ok = true;
-
-  for (int kc = 0; kc < kchunks; ++kc) {
-    const int s = kc & 1;
-    if (kc >= STAGES) {  // the MMAs that read this stage two steps ago must be done
-      if (!mbar_wait(&bar_mma[s], ((kc >> 1) - 1) & 1)) ok = false;
+  if (warp == LOAD_WARP) {
+    // ---------------- producer: weight units and token tiles ----------------
+    if (lane == 0) {
+      const int boxes = (nmma + TMA_ROWS - 1) / TMA_ROWS;  // only the tile's own token rows
+      auto issue_unit = [&](int u) {
+        const int slot = u % W::RING;
+        mbar_expect_tx(&bar_raw[slot], W::UNIT_BYTES);
+        bulk_load(sR + slot * W::UNIT_BYTES, W::unit_src(p, e, tile, u), W::UNIT_BYTES, &bar_raw[slot]);
+        s_last_raw = u;
+      };
+      auto issue_tokens = [&](int c) {
+        const int b = c % BSTAGES;
+        mbar_expect_tx(&bar_bfull[b], 2 * boxes * TMA_ROWS * 128);
+        for (int h = 0; h < 2; ++h)
+          for (int j = 0; j < boxes; ++j)
+            tma_load_2d(sB + b * B_BYTES + h * (BN * 128) + j * (TMA_ROWS * 128), &tmap, c * BK + 64 * h,
+                        base + n0 + j * TMA_ROWS, &bar_bfull[b]);
+        s_last_tma = c;
+      };
+      for (int u = 0; u < W::RING && u < units; ++u) issue_unit(u);
+      for (int c = 0; c < BSTAGES && c < kchunks; ++c) issue_tokens(c);
+      int next_u = W::RING, next_c = BSTAGES;
+      while (!s_abort && (next_u < units || next_c < kchunks)) {
+        // the next copy whose slot frees first in chunk order: unit next_u needs the unit
+        // next_u - RING read (chunk (next_u - RING + 1) * CPU - 1); tile next_c needs MMA(next_c - 3)
+        const int cu = next_u < units ? (next_u - W::RING + 1) * W::CHUNKS_PER_UNIT - 1 : 1 << 30;
+        const int cc = next_c < kchunks ? next_c - BSTAGES : 1 << 30;
+        if (cu <= cc) {
+          const int old = next_u - W::RING;
+          if (!mbar_wait(&bar_rawfree[old % W::RING], (old / W::RING) & 1)) { s_abort = 1; break; }
+          issue_unit(next_u++);
+        } else {
+          const int old = next_c - BSTAGES;
+          if (!mbar_wait(&bar_mma[old % BSTAGES], (old / BSTAGES) & 1)) { s_abort = 1; break; }
+          issue_tokens(next_c++);
+        }
+      }
     }
-    if (!ok) s_abort = 1;
-    __syncthreads();
-    if (s_abort) break;
-    if (threadIdx.x == 0) {
-      mbar_expect_tx(&bar_full[s], 2 * BN * 128);
-      tma_load_2d(sB + s * B_BYTES, &tmap, kc * BK, base + n0, &bar_full[s]);
-      tma_load_2d(sB + s * B_BYTES + BN * 128, &tmap, kc * BK + 64, base + n0, &bar_full[s]);
-      s_last_tma = kc;
-    }
-    // dequantise this thread's 64 weights into the stage, prefetch the next chunk's bytes
-    uint4 vals[8];
-    dequant_any<W>(raw, ((kc & 1) << 1) | dq, vals);
-    if (kc + 1 < kchunks) W::load(p, e, tile, kc + 1, drow, dq, raw);
-    unsigned char* atom = sA + s * A_BYTES + dq * (BM * 128);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(atom + sw128(drow, j)) = vals[j];
-    fence_proxy_async();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      if (!mbar_wait(&bar_full[s], (kc >> 1) & 1)) {
-        s_abort = 1;
-      } else {
+    __syncwarp();
+  } else if (warp == MMA_WARP) {
+    // ---------------- MMA issue ----------------
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(nmma);
+      const uint64_t adesc0 = smem_desc(smem_u32(sA)), bdesc0 = smem_desc(smem_u32(sB));
+      for (int kc = 0; kc < kchunks && !s_abort; ++kc) {
+        const int sa = kc & 1, b = kc % BSTAGES;
+        if (!mbar_wait(&bar_afull[sa], (kc >> 1) & 1) || !mbar_wait(&bar_bfull[b], (kc / BSTAGES) & 1)) {
+          s_abort = 1;
+          break;
+        }
         tc_fence_after();
-        const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * B_BYTES);
+        const uint32_t aoff = (uint32_t)(sa * A_BYTES) >> 4, boff = (uint32_t)(b * B_BYTES) >> 4;
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k) {
-          const uint32_t off = (k >> 2) * (BM * 128) + (k & 3) * 32;
-          const uint32_t offb = (k >> 2) * (BN * 128) + (k & 3) * 32;
-          umma_f16(tmem, smem_desc(a0 + off), smem_desc(b0 + offb), idesc, (kc > 0 || k > 0) ? 1u : 0u);
+          const uint32_t ka = ((k >> 2) * (BM * 128) + (k & 3) * 32) >> 4;
+          const uint32_t kb = ((k >> 2) * (BN * 128) + (k & 3) * 32) >> 4;
+          umma_f16(tmem, adesc0 + aoff + ka, bdesc0 + boff + kb, idesc, (kc > 0 || k > 0) ? 1u : 0u);
         }
-        umma_commit(&bar_mma[s]);
+        umma_commit(&bar_mma[b]);
         s_last_mma = kc;
       }
     }
+    __syncwarp();
+  } else {
+    // ---------------- dequant warps ----------------
+    // (row, quarter): a warp covers 32 consecutive rows of one quarter, so each 8-lane phase of a
+    // 16-byte store writes 8 rows of one 8-row group: distinct swizzled bank groups, no conflicts
+    const int drow = threadIdx.x & (BM - 1), dq = threadIdx.x >> 7;
+    const uint32_t row_off = (uint32_t)((drow >> 3) * 1024 + (drow & 7) * 128 + (dq >> 1) * (BM * 128));
+    const int r7 = drow & 7;
+    for (int kc = 0; kc < kchunks; ++kc) {
+      const int u = kc / W::CHUNKS_PER_UNIT, slot = u % W::RING;
+      bool ok = mbar_wait(&bar_raw[slot], (u / W::RING) & 1);
+      if (ok && kc >= STAGES) ok = mbar_wait(&bar_mma[(kc - 2) % BSTAGES], ((kc - 2) / BSTAGES) & 1);
+      if (!ok) s_abort = 1;
+      if (s_abort) break;
+      typename W::Raw raw;
+      W::read(p, sR + slot * W::UNIT_BYTES, e, tile, kc, drow, dq, raw);
+      if ((kc + 1) % W::CHUNKS_PER_UNIT == 0) {  // last read of this unit: hand the slot back
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_rawfree[slot]);
+      }
+      uint4 vals[4];
+      W::dequant(raw, kc, dq, vals);
+      unsigned char* stage = sA + (kc & 1) * A_BYTES + row_off;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(stage + ((W::chunk_of(dq, j) ^ r7) << 4)) = vals[j];
+      fence_proxy_async();  // each writer orders its stores before the tensor core's reads
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_afull[kc & 1]);
+    }
   }
   __syncthreads();
-  // Wait (bounded) for this CTA's own work in flight: the last committed MMAs (which imply all
-  // earlier ones) and, after an abort, the last issued TMA, before reading or freeing anything.
-  bool have = !s_abort;
-  if (s_last_mma >= 0 && !mbar_wait(&bar_mma[s_last_mma & 1], (s_last_mma >> 1) & 1)) have = false;
-  if (s_abort && s_last_tma > s_last_mma) (void)mbar_wait(&bar_full[s_last_tma & 1], (s_last_tma >> 1) & 1);
-  if (s_last_mma != kchunks - 1) have = false;
+
+  // Wait (bounded) for this CTA's work in flight before reading or freeing anything: the last committed
+  // MMAs (which imply all earlier ones), and after an abort the outstanding token tiles and weight units.
+  bool have = !s_abort && s_last_mma == kchunks - 1;
+  if (s_last_mma >= 0 && !mbar_wait(&bar_mma[s_last_mma % BSTAGES], (s_last_mma / BSTAGES) & 1)) have = false;
+  if (s_abort && threadIdx.x == 0) {
+    for (int c = max(0, s_last_tma - BSTAGES + 1); c <= s_last_tma; ++c)
+      (void)mbar_wait(&bar_bfull[c % BSTAGES], (c / BSTAGES) & 1);
+    for (int u = max(0, s_last_raw - W::RING + 1); u <= s_last_raw; ++u)
+      (void)mbar_wait(&bar_raw[u % W::RING], (u / W::RING) & 1);
+  }
   if (!have && threadIdx.x == 0 && p.err) atomicExch(p.err, (int)MOE_ERR_TIMEOUT);
   tc_fence_after();
 
-  if (have) {
-    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (one weight row per thread) and the
-    // token columns [64 (w / 4), +64) in steps of 16
-    const int quad = warp & 3, chalf = warp >> 2;
+  if (have && warp < DQ_WARPS) {
+    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (one weight row per thread) and the token
+    // columns [32 (w / 4), +32) in steps of 16
+    const int quad = warp & 3, cq = warp >> 2;
     const int row = quad * 32 + lane;  // weight row within the tile
-    for (int c0 = chalf * 64; c0 < chalf * 64 + 64; c0 += 16) {
+    for (int c0 = cq * 32; c0 < cq * 32 + 32; c0 += 16) {
       if (c0 >= nmma) break;
       float v[16];
       tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
@@ -393,9 +480,9 @@ __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, c
           const int n = c0 + i;
           if (lane < 16 && n < nval) {
             const float sc = p.tscale[base + n0 + n];
-            const float g = v[i] * sc, u = up * sc;
+            const float g = v[i] * sc, uu = up * sc;
             const int col = tile * 64 + quad * 16 + lane;
-            p.out[(int64_t)(base + n0 + n) * (p.N_rows >> 1) + col] = g / (1.0f + __expf(-g)) * u;
+            p.out[(int64_t)(base + n0 + n) * (p.N_rows >> 1) + col] = g / (1.0f + __expf(-g)) * uu;
           }
         }
       } else {
@@ -519,7 +606,8 @@ __global__ void repack_fp8_kernel(const uint8_t* __restrict__ a, const uint8_t* 
   if (merged) gu_src(tile, r, &which, &srow);
   const uint8_t* src = (which ? b : a) + ((int64_t)e * N_src + srow) * K + kc * BK;
   uint8_t* d = dst + (((int64_t)e * tiles + tile) * kch + kc) * (BM * BK) + r * BK;
-  for (int j = 0; j < BK; j += 16) *reinterpret_cast<uint4*>(d + j) = *reinterpret_cast<const uint4*>(src + j);
+  for (int j = 0; j < BK / 16; ++j)  // 16-byte chunk j of the row at j ^ (r % 8): conflict-free ring reads
+    *reinterpret_cast<uint4*>(d + ((j ^ (r & 7)) << 4)) = *reinterpret_cast<const uint4*>(src + j * 16);
   // per (tile, chunk) two scales {rows of group half 0, rows of group half 1}: a merged tile holds gate
   // rows 64t..64t+63 and up rows 64t..64t+63, each inside one 128-row scale block of its projection;
   // an unmerged 128-row tile is one scale block, stored twice
@@ -531,6 +619,9 @@ __global__ void repack_fp8_kernel(const uint8_t* __restrict__ a, const uint8_t* 
 }
 
 // Q4_K: one thread per (e, tile, super-block, row): 144 bytes (9 x 16)
+// Q4_K: one thread per (e, tile, super-block, row). Unit layout per (e, tile, super-block):
+// [128 rows][128 B] quants, then [128 rows][8 sub-blocks] f16 pairs {d*sc, -dmin*m} (the values the
+// GGML formula multiplies and adds, rounded once to f16 exactly as the in-kernel dequant rounds them).
 __global__ void repack_q4k_kernel(const uint8_t* __restrict__ a, const uint8_t* __restrict__ b, int E, int N_src,
                                   int K, uint8_t* __restrict__ dst) {
   const bool merged = b != nullptr;
@@ -548,8 +639,28 @@ __global__ void repack_q4k_kernel(const uint8_t* __restrict__ a, const uint8_t* 
   int which = 0, srow = tile * BM + r;
   if (merged) gu_src(tile, r, &which, &srow);
   const uint8_t* src = (which ? b : a) + (((int64_t)e * N_src + srow) * sbs + sb) * 144;
-  uint8_t* d = dst + (((int64_t)e * tiles + tile) * sbs + sb) * (BM * 144) + r * 144;
-  for (int j = 0; j < 144; j += 16) *reinterpret_cast<uint4*>(d + j) = *reinterpret_cast<const uint4*>(src + j);
+  uint8_t* unit = dst + (((int64_t)e * tiles + tile) * sbs + sb) * Q4K_UNIT;
+  for (int j = 0; j < 8; ++j)  // 16-byte chunk j of the row at j ^ (r % 8): conflict-free ring reads
+    *reinterpret_cast<uint4*>(unit + r * 128 + ((j ^ (r & 7)) << 4)) = *reinterpret_cast<const uint4*>(src + 16 + j * 16);
+  const float d = __half2float(*reinterpret_cast<const __half*>(src));
+  const float dmin = __half2float(*reinterpret_cast<const __half*>(src + 2));
+  const uint8_t* sc = src + 4;
+  uint32_t pairs[8];
+  for (int j = 0; j < 8; ++j) {
+    int sv, mv;
+    if (j < 4) {
+      sv = sc[j] & 63;
+      mv = sc[j + 4] & 63;
+    } else {
+      sv = (sc[j + 4] & 0xf) | ((sc[j - 4] >> 6) << 4);
+      mv = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    }
+    __half2 h2 = __floats2half2_rn(d * (float)sv, -(dmin * (float)mv));
+    pairs[j] = *reinterpret_cast<uint32_t*>(&h2);
+  }
+  uint4* sdst = reinterpret_cast<uint4*>(unit + BM * 128 + r * 32);
+  sdst[0] = make_uint4(pairs[0], pairs[1], pairs[2], pairs[3]);
+  sdst[1] = make_uint4(pairs[4], pairs[5], pairs[6], pairs[7]);
 }
 
 }  // namespace tc
@@ -572,7 +683,7 @@ static PFN_encodeTiled get_encode() {
   return fn;
 }
 
-// 2-D map over an f16 [rows, cols] row-major buffer, box 64 columns x 128 rows, SWIZZLE_128B.
+// 2-D map over an f16 [rows, cols] row-major buffer, box 64 columns x 32 rows, SWIZZLE_128B.
 moe_status make_row_tmap(void* map_out, const void* base, int64_t rows, int cols) {
   PFN_encodeTiled enc = get_encode();
   if (!enc) return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -580,7 +691,7 @@ moe_status make_row_tmap(void* map_out, const void* base, int64_t rows, int cols
   CUtensorMap* m = static_cast<CUtensorMap*>(map_out);
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)tc::BN};
+  cuuint32_t box[2] = {64, (cuuint32_t)tc::TMA_ROWS};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -593,7 +704,7 @@ size_t tensor_map_bytes() { return sizeof(CUtensorMap); }
 
 int64_t tc_weight_bytes(int wdtype, int N, int K) {
   if (wdtype == MOE_DTYPE_FP8_E4M3_B128) return (int64_t)N * K;
-  if (wdtype == MOE_DTYPE_Q4_K) return (int64_t)N * (K / 256) * 144;
+  if (wdtype == MOE_DTYPE_Q4_K) return (int64_t)(N / tc::BM) * (K / 256) * tc::Q4K_UNIT;
   return 0;
 }
 int64_t tc_scale_count(int wdtype, int N, int K) {
@@ -644,7 +755,7 @@ static moe_status launch_tc(const TcArgs& a, cudaStream_t st) {
   cudaGetDevice(&dev);
   if (!attr[dev & 63]) {
     MOE_CUDA_TRY(cudaFuncSetAttribute(tc::expert_gemm_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      tc::SMEM_BYTES));
+                                      tc::gemm_smem_bytes<W>()));
     attr[dev & 63] = true;
   }
   tc::GemmParams p;
@@ -666,7 +777,7 @@ static moe_status launch_tc(const TcArgs& a, cudaStream_t st) {
   p.err = a.err;
   const int grid = a.max_tiles * p.tiles;
   if (grid <= 0) return MOE_OK;
-  tc::expert_gemm_kernel<W><<<grid, tc::THREADS, tc::SMEM_BYTES, st>>>(p, *static_cast<const CUtensorMap*>(a.tmap));
+  tc::expert_gemm_kernel<W><<<grid, tc::THREADS, tc::gemm_smem_bytes<W>(), st>>>(p, *static_cast<const CUtensorMap*>(a.tmap));
   MOE_CUDA_TRY(cudaGetLastError());
   return MOE_OK;
 }
