@@ -4,19 +4,20 @@
 // PrefillStream::dispatch (src/moe/prefill_stream.rs:1178-1216) and forward_batched (:2080-2102),
 // with the expert math of run_expert (src/moe/stages/gpu.rs:162-167).
 //
-// One CTA computes one (expert, 128-row weight tile, <=128-token tile) block of
+// A work item is one (expert, 128-row weight tile, <=128-token tile) block of
 //   gate/up:  H[tok, n] = SwiGLU over the tile's 64 gate and 64 up rows of X_e W^T
 //   down:     Ypair[pair, n] = w_pair * (h_e W^T)[tok, n]
-// as D[128 x N] (TMEM, f32) = A[128 x K] (weights, shared memory) * B[K x N] (tokens, shared memory)
-// with tcgen05.mma kind::f16 issued by one thread. Per 128-column K stage:
-//   * the token tile arrives by two 2-D TMA loads (64 columns each, SWIZZLE_128B) from the
-//     gathered, f16-converted activations, completing on an mbarrier;
-//   * every thread dequantises 64 weights of one row (Q4_K: nibble -> f16 by the 0x6400 exponent
-//     trick, then d*sc*q - dmin*m in f16; FP8 e4m3: cvt to f16 times the 128x128 block scale) and
-//     writes them in the same SWIZZLE_128B K-major layout;
-//   * one thread issues 8 MMAs (K = 16 each) and commits them to the stage's mbarrier, which gates
-//     the reuse of that stage two steps later. Two stages keep dequant/TMA of stage k+1 under the
-//     MMAs of stage k.
+// computed as D[128 x N] (TMEM, f32) = A[128 x K] (weights, TMEM) * B[K x N] (tokens, shared memory)
+// with tcgen05.mma kind::f16. The kernel is persistent (one CTA per SM walking the items) and
+// warp-specialised. Per 128-column K chunk:
+//   * the token tile arrives by 2-D TMA loads (64 columns x 32 rows per box, SWIZZLE_128B) from the
+//     gathered, f16-converted activations;
+//   * the weight tile streams into a shared-memory ring by 1-D bulk copies; 16 warps dequantise it
+//     (Q4_K: nibble -> f16 by the 0x6400 exponent trick, then d*sc*q - dmin*m in f16; FP8 e4m3: cvt
+//     to f16 times the 128x128 block scale) and write the f16 operand straight into tensor memory
+//     with tcgen05.st, so the dequantised weights never touch shared memory;
+//   * one thread issues 8 MMAs (K = 16 each).
+// Two accumulators let the epilogue of one item overlap the main loop of the next.
 // Every wait is bounded: a wait that runs out sets MOE_ERR_TIMEOUT in the error word, the CTA
 // stops issuing work, waits (bounded) for its own MMAs, frees its TMEM and returns.
 //
@@ -39,20 +40,27 @@ namespace tc {
 constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int BK = 128;
-constexpr int DQ_WARPS = 16;                       // dequantise (and run the epilogue)
-constexpr int DQ_THREADS = DQ_WARPS * 32;
-constexpr int MMA_WARP = DQ_WARPS;                  // issues the tensor-core MMAs
-constexpr int LOAD_WARP = DQ_WARPS + 1;             // issues the weight-unit and token-tile copies
-constexpr int THREADS = DQ_THREADS + 64;
-constexpr int A_BYTES = BM * BK * 2;  // one stage of f16 weights
+constexpr int DQ_WARPS = 16;     // warps 0..15 dequantise
+constexpr int MMA_WARP = 16;     // issues the tensor-core MMAs
+constexpr int WLOAD_WARP = 17;   // weight units -> shared-memory ring
+constexpr int TLOAD_WARP = 18;   // token tiles -> B stages
+constexpr int EPI_WARP0 = 20;    // warps 20..23: epilogue, tensor-memory lane quarter = warp % 4
+constexpr int EPI_WARPS = 4;
+constexpr int THREADS = (EPI_WARP0 + EPI_WARPS) * 32;
 constexpr int B_BYTES = BN * BK * 2;  // one stage of f16 tokens
-constexpr int STAGES = 2;             // dequantised weight stages
-constexpr int BSTAGES = 3;            // token-tile stages, loaded two chunks ahead
+constexpr int ASTAGES = 4;            // dequantised weight stages (tensor memory)
+constexpr int BSTAGES = 4;            // token-tile stages (shared memory)
+// Tensor memory: two f32 accumulators at columns [0, BN) and [BN, 2 BN) (lane = weight row), used
+// by alternate work items; stage s of the dequantised f16 weights at columns A_COL0 + 64 s .. +63
+// (lane = weight row, two K values per 32-bit column), the operand layout tcgen05.mma reads for A
+// from tensor memory.
+constexpr int A_COL0 = 2 * BN;
+constexpr int A_COLS = BK / 2;
+constexpr int TMEM_COLS = 512;
+static_assert(A_COL0 + ASTAGES * A_COLS <= TMEM_COLS, "tensor memory budget");
+static_assert(EPI_WARP0 % 4 == 0, "epilogue warp w reads tensor-memory lane quarter w % 4");
 constexpr int Q4K_UNIT = BM * 128 + BM * 32;
 constexpr int TMA_ROWS = 32;  // token rows per TMA box  // Q4_K unit: quants + per-sub-block scale pairs
-constexpr uint32_t WAIT_POLLS = 1u << 22;             // backstop on try_wait polls
-constexpr uint64_t WAIT_NS = 200ull * 1000ull * 1000ull;  // a wait longer than 200 ms is declared stuck
-
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -63,27 +71,32 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
+constexpr uint32_t WAIT_POLLS = 1u << 22;               // backstop on try_wait polls
+constexpr long long WAIT_CYCLES = 400ll * 1000ll * 1000ll;  // ~200 ms of SM clock: a longer wait is declared stuck
+
+// Bounded parity wait: true when the phase completed; false after WAIT_CYCLES SM clocks (or
+// WAIT_POLLS polls), or as soon as another role of the CTA gave up (*abort set; nullptr: no such
+// check). The clock is read only once the first poll failed: the common, already-completed case
+// costs one try_wait.
+__device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{.reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;}"
+      : "=r"(done)
+      : "r"(a), "r"(parity)
+      : "memory");
+  return done != 0;
 }
 
-// Bounded parity wait: true when the phase completed, false after 200 ms (or WAIT_POLLS polls).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   const uint32_t a = smem_u32(bar);
-  const uint64_t t0 = globaltimer_ns();
+  if (mbar_try(a, parity)) return true;
+  const long long t0 = clock64();
   for (uint32_t i = 0; i < WAIT_POLLS; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{.reg .pred p;\n"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        "selp.u32 %0, 1, 0, p;}"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if ((i & 63) == 63 && globaltimer_ns() - t0 > WAIT_NS) return false;
+    if (mbar_try(a, parity)) return true;
+    if ((i & 63) == 63 && ((abort && *abort) || clock64() - t0 > WAIT_CYCLES)) return false;
   }
   return false;
 }
@@ -96,7 +109,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -117,14 +129,22 @@ __device__ __forceinline__ uint32_t idesc_f16(int n) {
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
+// A from tensor memory (columns of 2 x f16 per lane), B from shared memory.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
   asm volatile(
       "{.reg .pred p;\n"
       "setp.ne.b32 p, %4, 0;\n"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// Four 32-bit columns per lane of this warp's 32-lane quarter.
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint4& v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -144,8 +164,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Byte offset of the 16-byte chunk j (8 elements) of row r in a SWIZZLE_128B K-major atom.
-__device__ __forceinline__ uint32_t sw128(int r, int j) { return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4)); }
 
 // ---- weight formats -----------------------------------------------------------------------------
 
@@ -173,7 +191,7 @@ struct GemmParams {
 struct FP8W {
   static constexpr int UNIT_BYTES = BM * BK;  // one 128-column chunk of the tile: 16 KB
   static constexpr int CHUNKS_PER_UNIT = 1;
-  static constexpr int RING = 3;
+  static constexpr int RING = 4;
   struct Raw {
     uint4 q[2];
     float s;
@@ -218,7 +236,7 @@ struct FP8W {
 struct Q4KW {
   static constexpr int UNIT_BYTES = Q4K_UNIT;  // one 256-column super-block of the tile: 20 KB
   static constexpr int CHUNKS_PER_UNIT = 2;
-  static constexpr int RING = 3;
+  static constexpr int RING = 4;
   struct Raw {
     uint4 q;     // 16 quant bytes: low nibbles of sub-block 2c, high nibbles of 2c + 1
     uint2 s;     // {d*sc, -dmin*m} f16 pairs of sub-blocks 2c and 2c + 1
@@ -278,119 +296,149 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 
 template <class W>
 constexpr int gemm_smem_bytes() {
-  return W::RING * W::UNIT_BYTES + STAGES * A_BYTES + BSTAGES * B_BYTES + 1024 + 256;
+  return W::RING * W::UNIT_BYTES + BSTAGES * B_BYTES + 1024 + 512;
 }
 
 // ---- the GEMM ------------------------------------------------------------------------------------
 //
-// Warp roles, all hand-offs through mbarriers (no CTA-wide barrier inside the loop):
-//   * warps 0..15 dequantise: chunk kc waits for its weight unit in the ring and for the A stage
-//     (kc % 2) to be free (MMAs of chunk kc - 2 done), writes the stage, fences the generic-to-async
-//     proxy, and each warp's lane 0 arrives on a_full[kc % 2]; after the last chunk of a unit they
-//     arrive on raw_free[slot];
-//   * warp 16 (one lane) waits for a_full and b_full of each chunk, issues its 8 MMAs and commits
-//     them to mma_done[kc % 3], which frees the A and the B stage;
-//   * warp 17 (one lane) keeps the weight ring RING units ahead (1-D bulk copies, each after the
-//     slot's raw_free) and the token tiles three chunks ahead (2-D TMA, each after the MMAs that read
-//     the stage).
-// Any wait that runs past its limit sets s_abort; every role stops at its next check, the CTA waits
-// (bounded) for what it issued, frees its TMEM and returns.
+// Persistent: one CTA per SM walks the work items w = blockIdx.x, blockIdx.x + gridDim.x, ... of
+// the launch, item w = (token tile w / tiles, weight tile w % tiles), so CTAs running side by side
+// share a token tile in L2 and stream different weight tiles. Every item costs about the same
+// (a 128 x N x 16 MMA takes the same issue slot for any N <= 64, and the dequant work does not
+// depend on N), so the static schedule balances. Warp roles, all hand-offs through mbarriers and
+// all rings continuing across item boundaries:
+//   * warps 0..15 dequantise chunk q (a global chunk counter) from the weight ring into tensor-memory
+//     stage q % ASTAGES once the MMAs of chunk q - ASTAGES released it (a_free), and arrive a_full;
+//     after the last chunk of a weight unit they arrive raw_free for its ring slot;
+//   * warp 16 (one lane) issues the 8 MMAs of each chunk into the item's accumulator (two
+//     accumulators alternate between items), commits them to a_free and b_free, and after the last
+//     chunk commits acc_full; it waits acc_free before reusing an accumulator;
+//   * warp 17 (one lane) streams weight units into the ring (1-D bulk copies, each after raw_free);
+//   * warp 18 (one lane) streams token tiles into the B stages (2-D TMA, each after b_free);
+//   * warps 20..23 run the epilogue of item j while the next item computes: tensor-memory lane
+//     quarter w % 4, per-column scales and destinations loaded before acc_full completes.
+// A wait that runs past its limit (or sees another role give up) sets s_abort; every role stops at
+// its next wait, the MMA warp drains its MMAs, the CTA waits (bounded) for the copies it issued,
+// frees its tensor memory and returns.
+
+struct Item {
+  int e, base, n0, nval, nmma, tile;
+};
+
+__device__ __forceinline__ Item decode_item(const GemmParams& p, int w) {
+  Item it;
+  const int ti = w / p.tiles;
+  it.tile = w % p.tiles;
+  const int entry = __ldg(p.tile_list + ti);
+  it.e = __ldg(p.active + (entry >> 16));
+  it.base = __ldg(p.offsets + it.e);
+  const int count = __ldg(p.offsets + it.e + 1) - it.base;
+  it.n0 = (entry & 0xffff) * BN;
+  it.nval = min(BN, count - it.n0);
+  it.nmma = (it.nval + 15) & ~15;  // M = 128 needs N % 16 == 0
+  return it;
+}
 
 template <class W>
 __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, const __grid_constant__ CUtensorMap tmap) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  unsigned char* sA = smem;                                // [STAGES][A_BYTES]
-  unsigned char* sB = smem + STAGES * A_BYTES;             // [BSTAGES][B_BYTES]
+  unsigned char* sB = smem;                                // [BSTAGES][B_BYTES]
   unsigned char* sR = sB + BSTAGES * B_BYTES;              // [RING][UNIT_BYTES] raw weights
-  uint64_t* bar_raw = reinterpret_cast<uint64_t*>(sR + W::RING * W::UNIT_BYTES);  // weight unit landed
-  uint64_t* bar_rawfree = bar_raw + W::RING;               // weight unit fully read
-  uint64_t* bar_bfull = bar_rawfree + W::RING;             // token tile landed
-  uint64_t* bar_afull = bar_bfull + BSTAGES;               // dequantised stage written
-  uint64_t* bar_mma = bar_afull + STAGES;                  // MMAs of chunk c done (slot c % 3)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + BSTAGES);
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(sR + W::RING * W::UNIT_BYTES);
+  uint64_t* raw_free = raw_full + W::RING;
+  uint64_t* b_full = raw_free + W::RING;
+  uint64_t* b_free = b_full + BSTAGES;
+  uint64_t* a_full = b_free + BSTAGES;
+  uint64_t* a_free = a_full + ASTAGES;
+  uint64_t* acc_full = a_free + ASTAGES;
+  uint64_t* acc_free = acc_full + 2;
+  uint64_t* mma_done = acc_free + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   __shared__ volatile int s_abort;
-  __shared__ int s_last_mma, s_last_tma, s_last_raw;  // last chunk/unit committed or issued
+  __shared__ int s_units_issued, s_tiles_issued;
 
-  const int tiles = p.tiles;
-  const int ti = blockIdx.x / tiles;
-  const int tile = blockIdx.x % tiles;
-  if (ti >= *p.n_tiles) return;
   // after any CTA gave up on a wait, the rest of the launch does no work
   if (p.err && *reinterpret_cast<volatile int32_t*>(p.err) == (int32_t)MOE_ERR_TIMEOUT) return;
-  const int entry = p.tile_list[ti];
-  const int a_idx = entry >> 16, ntile = entry & 0xffff;
-  const int e = p.active[a_idx];
-  const int base = p.offsets[e];
-  const int count = p.offsets[e + 1] - base;
-  const int n0 = ntile * BN;
-  const int nval = min(BN, count - n0);
-  const int nmma = (nval + 15) & ~15;  // M = 128 needs N % 16 == 0
+  const int n_items = *p.n_tiles * p.tiles;
+  if ((int)blockIdx.x >= n_items) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kchunks = p.K / BK;
   const int units = kchunks / W::CHUNKS_PER_UNIT;
+  const int G = gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < W::RING; ++s) {
-      mbar_init(&bar_raw[s], 1);
-      mbar_init(&bar_rawfree[s], DQ_WARPS);
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_free[s], DQ_WARPS);
     }
     for (int s = 0; s < BSTAGES; ++s) {
-      mbar_init(&bar_bfull[s], 1);
-      mbar_init(&bar_mma[s], 1);
+      mbar_init(&b_full[s], 1);
+      mbar_init(&b_free[s], 1);
     }
-    for (int s = 0; s < STAGES; ++s) mbar_init(&bar_afull[s], DQ_WARPS);  // one arrival per dequant warp
+    for (int s = 0; s < ASTAGES; ++s) {
+      mbar_init(&a_full[s], DQ_WARPS);  // one arrival per dequant warp
+      mbar_init(&a_free[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&acc_full[s], 1);
+      mbar_init(&acc_free[s], EPI_WARPS);
+    }
+    mbar_init(mma_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     s_abort = 0;
-    s_last_mma = -1;
-    s_last_tma = -1;
-    s_last_raw = -1;
+    s_units_issued = 0;
+    s_tiles_issued = 0;
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(BN));
+                 "r"(TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  volatile int* abort = &s_abort;
 
-  if (warp == LOAD_WARP) {
-    // ---------------- producer: weight units and token tiles ----------------
+  if (warp == WLOAD_WARP) {
+    // ---------------- weight units -> ring ----------------
     if (lane == 0) {
-      const int boxes = (nmma + TMA_ROWS - 1) / TMA_ROWS;  // only the tile's own token rows
-      auto issue_unit = [&](int u) {
-        const int slot = u % W::RING;
-        mbar_expect_tx(&bar_raw[slot], W::UNIT_BYTES);
-        bulk_load(sR + slot * W::UNIT_BYTES, W::unit_src(p, e, tile, u), W::UNIT_BYTES, &bar_raw[slot]);
-        s_last_raw = u;
-      };
-      auto issue_tokens = [&](int c) {
-        const int b = c % BSTAGES;
-        mbar_expect_tx(&bar_bfull[b], 2 * boxes * TMA_ROWS * 128);
-        for (int h = 0; h < 2; ++h)
-          for (int j = 0; j < boxes; ++j)
-            tma_load_2d(sB + b * B_BYTES + h * (BN * 128) + j * (TMA_ROWS * 128), &tmap, c * BK + 64 * h,
-                        base + n0 + j * TMA_ROWS, &bar_bfull[b]);
-        s_last_tma = c;
-      };
-      for (int u = 0; u < W::RING && u < units; ++u) issue_unit(u);
-      for (int c = 0; c < BSTAGES && c < kchunks; ++c) issue_tokens(c);
-      int next_u = W::RING, next_c = BSTAGES;
-      while (!s_abort && (next_u < units || next_c < kchunks)) {
-        // the next copy whose slot frees first in chunk order: unit next_u needs the unit
-        // next_u - RING read (chunk (next_u - RING + 1) * CPU - 1); tile next_c needs MMA(next_c - 3)
-        const int cu = next_u < units ? (next_u - W::RING + 1) * W::CHUNKS_PER_UNIT - 1 : 1 << 30;
-        const int cc = next_c < kchunks ? next_c - BSTAGES : 1 << 30;
-        if (cu <= cc) {
-          const int old = next_u - W::RING;
-          if (!mbar_wait(&bar_rawfree[old % W::RING], (old / W::RING) & 1)) { s_abort = 1; break; }
-          issue_unit(next_u++);
-        } else {
-          const int old = next_c - BSTAGES;
-          if (!mbar_wait(&bar_mma[old % BSTAGES], (old / BSTAGES) & 1)) { s_abort = 1; break; }
-          issue_tokens(next_c++);
+      int g = 0;
+      for (int w = blockIdx.x; w < n_items && !*abort; w += G) {
+        const Item it = decode_item(p, w);
+        for (int u = 0; u < units; ++u, ++g) {
+          const int slot = g % W::RING;
+          if (g >= W::RING && !mbar_wait(&raw_free[slot], ((g / W::RING) - 1) & 1, abort)) {
+            s_abort = 1;
+            break;
+          }
+          mbar_expect_tx(&raw_full[slot], W::UNIT_BYTES);
+          bulk_load(sR + slot * W::UNIT_BYTES, W::unit_src(p, it.e, it.tile, u), W::UNIT_BYTES, &raw_full[slot]);
+          s_units_issued = g + 1;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == TLOAD_WARP) {
+    // ---------------- token tiles -> B stages ----------------
+    if (lane == 0) {
+      int q = 0;
+      for (int w = blockIdx.x; w < n_items && !*abort; w += G) {
+        const Item it = decode_item(p, w);
+        const int boxes = (it.nmma + TMA_ROWS - 1) / TMA_ROWS;  // only the tile's own token rows
+        for (int kc = 0; kc < kchunks; ++kc, ++q) {
+          const int b = q % BSTAGES;
+          if (q >= BSTAGES && !mbar_wait(&b_free[b], ((q / BSTAGES) - 1) & 1, abort)) {
+            s_abort = 1;
+            break;
+          }
+          mbar_expect_tx(&b_full[b], 2 * boxes * TMA_ROWS * 128);
+          for (int h = 0; h < 2; ++h)
+            for (int j = 0; j < boxes; ++j)
+              tma_load_2d(sB + b * B_BYTES + h * (BN * 128) + j * (TMA_ROWS * 128), &tmap, kc * BK + 64 * h,
+                          it.base + it.n0 + j * TMA_ROWS, &b_full[b]);
+          s_tiles_issued = q + 1;
         }
       }
     }
@@ -398,108 +446,162 @@ __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, c
   } else if (warp == MMA_WARP) {
     // ---------------- MMA issue ----------------
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(nmma);
-      const uint64_t adesc0 = smem_desc(smem_u32(sA)), bdesc0 = smem_desc(smem_u32(sB));
-      for (int kc = 0; kc < kchunks && !s_abort; ++kc) {
-        const int sa = kc & 1, b = kc % BSTAGES;
-        if (!mbar_wait(&bar_afull[sa], (kc >> 1) & 1) || !mbar_wait(&bar_bfull[b], (kc / BSTAGES) & 1)) {
+      const uint64_t bdesc0 = smem_desc(smem_u32(sB));
+      int q = 0, j = 0;
+      for (int w = blockIdx.x; w < n_items && !*abort; w += G, ++j) {
+        const Item it = decode_item(p, w);
+        const int acc = j & 1;
+        if (j >= 2 && !mbar_wait(&acc_free[acc], ((j >> 1) - 1) & 1, abort)) {
           s_abort = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t aoff = (uint32_t)(sa * A_BYTES) >> 4, boff = (uint32_t)(b * B_BYTES) >> 4;
+        const uint32_t idesc = idesc_f16(it.nmma);
+        const uint32_t dcol = tmem + (uint32_t)(acc * BN);
+        for (int kc = 0; kc < kchunks; ++kc, ++q) {
+          const int sa = q % ASTAGES, b = q % BSTAGES;
+          if (!mbar_wait(&a_full[sa], (q / ASTAGES) & 1, abort) || !mbar_wait(&b_full[b], (q / BSTAGES) & 1, abort)) {
+            s_abort = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t acol = tmem + (uint32_t)(A_COL0 + sa * A_COLS);
+          const uint64_t bd = bdesc0 + ((uint32_t)(b * B_BYTES) >> 4);
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k) {
-          const uint32_t ka = ((k >> 2) * (BM * 128) + (k & 3) * 32) >> 4;
-          const uint32_t kb = ((k >> 2) * (BN * 128) + (k & 3) * 32) >> 4;
-          umma_f16(tmem, adesc0 + aoff + ka, bdesc0 + boff + kb, idesc, (kc > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16_ts(dcol, acol + (uint32_t)(k * 8), bd + (uint32_t)(((k >> 2) * (BN * 128) + (k & 3) * 32) >> 4),
+                        idesc, (kc > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&a_free[sa]);
+          umma_commit(&b_free[b]);
         }
-        umma_commit(&bar_mma[b]);
-        s_last_mma = kc;
+        if (*abort) break;
+        umma_commit(&acc_full[acc]);
       }
+      // drain: every MMA this thread issued has completed once mma_done flips
+      umma_commit(mma_done);
+      if (!mbar_wait(mma_done, 0, nullptr)) s_abort = 1;
     }
     __syncwarp();
-  } else {
-    // ---------------- dequant warps ----------------
-    // (row, quarter): a warp covers 32 consecutive rows of one quarter, so each 8-lane phase of a
-    // 16-byte store writes 8 rows of one 8-row group: distinct swizzled bank groups, no conflicts
-    const int drow = threadIdx.x & (BM - 1), dq = threadIdx.x >> 7;
-    const uint32_t row_off = (uint32_t)((drow >> 3) * 1024 + (drow & 7) * 128 + (dq >> 1) * (BM * 128));
-    const int r7 = drow & 7;
-    for (int kc = 0; kc < kchunks; ++kc) {
-      const int u = kc / W::CHUNKS_PER_UNIT, slot = u % W::RING;
-      bool ok = mbar_wait(&bar_raw[slot], (u / W::RING) & 1);
-      if (ok && kc >= STAGES) ok = mbar_wait(&bar_mma[(kc - 2) % BSTAGES], ((kc - 2) / BSTAGES) & 1);
-      if (!ok) s_abort = 1;
-      if (s_abort) break;
-      typename W::Raw raw;
-      W::read(p, sR + slot * W::UNIT_BYTES, e, tile, kc, drow, dq, raw);
-      if ((kc + 1) % W::CHUNKS_PER_UNIT == 0) {  // last read of this unit: hand the slot back
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bar_rawfree[slot]);
-      }
-      uint4 vals[4];
-      W::dequant(raw, kc, dq, vals);
-      unsigned char* stage = sA + (kc & 1) * A_BYTES + row_off;
+  } else if (warp >= EPI_WARP0) {
+    // ---------------- epilogue ----------------
+    const int quad = warp & 3;  // tensor-memory lanes 32 quad .. +31
+    int j = 0;
+    for (int w = blockIdx.x; w < n_items; w += G, ++j) {
+      const Item it = decode_item(p, w);
+      const int acc = j & 1;
+      // per-column scale (and, for the down projection, destination pair), columns lane + 32 t
+      float csc[4];
+      int cpr[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(stage + ((W::chunk_of(dq, j) ^ r7) << 4)) = vals[j];
-      fence_proxy_async();  // each writer orders its stores before the tensor core's reads
+      for (int t = 0; t < 4; ++t) {
+        const int n = lane + 32 * t;
+        csc[t] = 0.0f;
+        cpr[t] = 0;
+        if (n < it.nval) {
+          const int idx = it.base + it.n0 + n;
+          csc[t] = __ldg(p.tscale + idx);
+          if (p.phase == 1) {
+            cpr[t] = __ldg(p.perm + idx);
+            csc[t] *= __ldg(p.route_w + cpr[t]);
+          }
+        }
+      }
+      const bool ok = __all_sync(FULL, mbar_wait(&acc_full[acc], (j >> 1) & 1, abort));
+      if (!ok) {
+        if (lane == 0) s_abort = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tbase = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll
+      for (int cb = 0; cb < BN / 16; ++cb) {
+        const int c0 = cb * 16;
+        if (c0 >= it.nmma) break;
+        float v[16];
+        tmem_ld16(tbase + (uint32_t)c0, v);
+        if (p.phase == 0) {
+          // lanes 0..15: gate rows, lanes 16..31: the matching up rows
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = c0 + i;
+            const float sc = __shfl_sync(FULL, csc[n >> 5], n & 31);
+            const float up = __shfl_down_sync(FULL, v[i], 16);
+            if (lane < 16 && n < it.nval) {
+              const float g = v[i] * sc, uu = up * sc;
+              const int col = it.tile * 64 + quad * 16 + lane;
+              p.out[(int64_t)(it.base + it.n0 + n) * (p.N_rows >> 1) + col] = g / (1.0f + __expf(-g)) * uu;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = c0 + i;
+            const float sc = __shfl_sync(FULL, csc[n >> 5], n & 31);
+            const int pr = __shfl_sync(FULL, cpr[n >> 5], n & 31);
+            if (n < it.nval) p.out[(int64_t)pr * p.N_rows + it.tile * BM + quad * 32 + lane] = v[i] * sc;
+          }
+        }
+      }
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar_afull[kc & 1]);
+      if (lane == 0) mbar_arrive(&acc_free[acc]);
     }
+  } else if (warp < DQ_WARPS) {
+    // ---------------- dequant ----------------
+    // warp w owns tensor-memory lanes 32 (w % 4) .. +31 (its weight rows, one per thread) and the
+    // 32-column quarter w / 4 of each chunk
+    const int drow = threadIdx.x & (BM - 1), dq = threadIdx.x >> 7;
+    const uint32_t lane_base = tmem + ((uint32_t)(drow & ~31) << 16) + (uint32_t)(A_COL0 + (dq >> 1) * 32);
+    int q = 0, g = 0;
+    bool stop = false;
+    for (int w = blockIdx.x; w < n_items && !stop; w += G) {
+      const Item it = decode_item(p, w);
+      for (int kc = 0; kc < kchunks; ++kc, ++q) {
+        const int gu = g + kc / W::CHUNKS_PER_UNIT, slot = gu % W::RING;
+        const bool ok_raw = mbar_wait(&raw_full[slot], (gu / W::RING) & 1, abort);
+        // the tcgen05 stores below are warp-collective: every lane takes the same branch
+        stop = __any_sync(FULL, !ok_raw);
+        if (stop) break;
+        typename W::Raw raw;
+        W::read(p, sR + slot * W::UNIT_BYTES, it.e, it.tile, kc, drow, dq, raw);
+        if ((kc + 1) % W::CHUNKS_PER_UNIT == 0) {  // last read of this unit: hand the slot back
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&raw_free[slot]);
+        }
+        uint4 vals[4];
+        W::dequant(raw, kc, dq, vals);
+        const int sa = q % ASTAGES;
+        const bool ok_a = q < ASTAGES || mbar_wait(&a_free[sa], ((q / ASTAGES) - 1) & 1, abort);
+        stop = __any_sync(FULL, !ok_a);
+        if (stop) break;
+        tc_fence_after();  // order the stores after the MMAs that read this stage
+        const uint32_t stage = lane_base + (uint32_t)(sa * A_COLS);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) tmem_st4(stage + (uint32_t)(W::chunk_of(dq, jj) * 4), vals[jj]);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[sa]);
+      }
+      g += units;
+    }
+    if (stop && lane == 0) s_abort = 1;
   }
   __syncthreads();
 
-  // Wait (bounded) for this CTA's work in flight before reading or freeing anything: the last committed
-  // MMAs (which imply all earlier ones), and after an abort the outstanding token tiles and weight units.
-  bool have = !s_abort && s_last_mma == kchunks - 1;
-  if (s_last_mma >= 0 && !mbar_wait(&bar_mma[s_last_mma % BSTAGES], (s_last_mma / BSTAGES) & 1)) have = false;
-  if (s_abort && threadIdx.x == 0) {
-    for (int c = max(0, s_last_tma - BSTAGES + 1); c <= s_last_tma; ++c)
-      (void)mbar_wait(&bar_bfull[c % BSTAGES], (c / BSTAGES) & 1);
-    for (int u = max(0, s_last_raw - W::RING + 1); u <= s_last_raw; ++u)
-      (void)mbar_wait(&bar_raw[u % W::RING], (u / W::RING) & 1);
-  }
-  if (!have && threadIdx.x == 0 && p.err) atomicExch(p.err, (int)MOE_ERR_TIMEOUT);
-  tc_fence_after();
-
-  if (have && warp < DQ_WARPS) {
-    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (one weight row per thread) and the token
-    // columns [32 (w / 4), +32) in steps of 16
-    const int quad = warp & 3, cq = warp >> 2;
-    const int row = quad * 32 + lane;  // weight row within the tile
-    for (int c0 = cq * 32; c0 < cq * 32 + 32; c0 += 16) {
-      if (c0 >= nmma) break;
-      float v[16];
-      tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
-      if (p.phase == 0) {
-        // lanes 0..15: gate rows, lanes 16..31: the matching up rows
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float up = __shfl_down_sync(FULL, v[i], 16);
-          const int n = c0 + i;
-          if (lane < 16 && n < nval) {
-            const float sc = p.tscale[base + n0 + n];
-            const float g = v[i] * sc, uu = up * sc;
-            const int col = tile * 64 + quad * 16 + lane;
-            p.out[(int64_t)(base + n0 + n) * (p.N_rows >> 1) + col] = g / (1.0f + __expf(-g)) * uu;
-          }
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int n = c0 + i;
-          if (n < nval) {
-            const int pr = p.perm[base + n0 + n];
-            p.out[(int64_t)pr * p.N_rows + tile * BM + row] = v[i] * p.tscale[base + n0 + n] * p.route_w[pr];
-          }
-        }
-      }
-    }
+  // After an abort, wait (bounded) for the copies still in flight: the last RING weight units and the
+  // last BSTAGES token tiles issued (earlier ones were consumed, so their phases completed).
+  const bool failed = s_abort != 0;
+  if (failed && threadIdx.x == 0) {
+    for (int u = max(0, s_units_issued - W::RING); u < s_units_issued; ++u)
+      (void)mbar_wait(&raw_full[u % W::RING], (u / W::RING) & 1, nullptr);
+    for (int c = max(0, s_tiles_issued - BSTAGES); c < s_tiles_issued; ++c)
+      (void)mbar_wait(&b_full[c % BSTAGES], (c / BSTAGES) & 1, nullptr);
+    if (p.err) atomicExch(p.err, (int)MOE_ERR_TIMEOUT);
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
 }
 
 // ---- helpers around the GEMM ----------------------------------------------------------------------
@@ -775,7 +877,10 @@ static moe_status launch_tc(const TcArgs& a, cudaStream_t st) {
   p.route_w = a.route_w;
   p.out = a.out;
   p.err = a.err;
-  const int grid = a.max_tiles * p.tiles;
+  static int sms[64] = {};
+  if (!sms[dev & 63]) MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev));
+  // persistent: one CTA per SM (or per work item when there are fewer)
+  const int grid = (int)std::min<int64_t>((int64_t)a.max_tiles * p.tiles, sms[dev & 63]);
   if (grid <= 0) return MOE_OK;
   tc::expert_gemm_kernel<W><<<grid, tc::THREADS, tc::gemm_smem_bytes<W>(), st>>>(p, *static_cast<const CUtensorMap*>(a.tmap));
   MOE_CUDA_TRY(cudaGetLastError());
