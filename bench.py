@@ -481,7 +481,7 @@ def run_prefill(args):
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         step()
-    with torch.cuda.stream(stream):
+    with torch.cuda.stream(stream), ClockSampler(local) as clk:
         for _ in range(args.warmup):
             graph.replay()
         torch.cuda.synchronize()
@@ -490,9 +490,41 @@ def run_prefill(args):
         for _ in range(args.steps):
             graph.replay()
         e1.record(stream)
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     tokens = prompt * L
+    del graph
+
+    # end to end through the public API with host buffers: every layer-chunk copies its pinned
+    # activations, routing ids and weights in and its output back, inside the timed region
+    hx = [x.cpu().pin_memory() for x in xs]
+    hid = [t.cpu().pin_memory() for t in ids]
+    hw = [t.cpu().pin_memory() for t in wts]
+    hy = [torch.empty_like(x, device="cpu").pin_memory() for x in xs]
+    dx, did, dw, dy = torch.empty_like(xs[0]), torch.empty_like(ids[0]), torch.empty_like(wts[0]), torch.empty_like(xs[0])
+
+    def e2e_step():
+        for layer in layers:
+            for c in range(nch):
+                dx.copy_(hx[c], non_blocking=True)
+                did.copy_(hid[c], non_blocking=True)
+                dw.copy_(hw[c], non_blocking=True)
+                layer.forward(dx, dw, did, out=dy)
+                hy[c].copy_(dy, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1) / args.steps
+    h2d = L * nch * (xs[0].numel() * 2 + ids[0].numel() * 4 + wts[0].numel() * 4)
+    d2h = L * nch * xs[0].numel() * 2
     # stage-marked pass: gate/up and down kernel times
     evs = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(5)] for _ in range(L * nch)]
     arrs = []
@@ -529,7 +561,7 @@ def run_prefill(args):
         "metric": "MoE-layer tokens/s per B200 (prefill, Qwen3-30B-A3B-shaped Q4_K layer, 512-token chunks)",
         "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "q4_k weights dequantised to f16 in shared memory, tcgen05 f16 MMA, f32 accumulate",
+        "dtype": "q4_k weights dequantised to f16 in tensor memory, tcgen05 f16 MMA, f32 accumulate",
         "data": "synthetic: seeded N(0,0.02) Q4_K experts, N(0,1) bf16 activations, Zipf(1.1) routing",
         "config": {"workload": "BASELINE config 3: 4096-token prompt in 512-token chunks through "
                                f"{L} distinct Q4_K layers (E128 k8 H2048 I768); routing ids drawn Zipf(1.1)",
@@ -540,6 +572,11 @@ def run_prefill(args):
                      "peak_source": kind, "hbm_gbs": round(gbs, 1), "hbm_frac": round(gbs / hpeak, 4),
                      "traffic": None},
         "stage_ms_per_step": {"gate_up": round(gu, 3), "down": round(dn, 3)},
+        "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        # plan, tile list, token gather, gate/up GEMM, h gather, down GEMM, combine per layer-chunk
+        "gpu_launches": 7 * L * nch * args.steps,
+        "clocks": clk.summary(),
     }), flush=True)
     for layer in layers:
         layer.close()

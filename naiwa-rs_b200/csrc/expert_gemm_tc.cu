@@ -32,6 +32,9 @@
 // one warp holds a gate value and its up partner after tcgen05.ld (SwiGLU by one shuffle).
 #include <cuda.h>
 
+#include <cstdlib>
+#include <string>
+
 #include "moe_internal.cuh"
 
 namespace moe {
@@ -40,25 +43,43 @@ namespace tc {
 constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int BK = 128;
-constexpr int DQ_WARPS = 16;     // warps 0..15 dequantise
-constexpr int MMA_WARP = 16;     // issues the tensor-core MMAs
-constexpr int WLOAD_WARP = 17;   // weight units -> shared-memory ring
-constexpr int TLOAD_WARP = 18;   // token tiles -> B stages
-constexpr int EPI_WARP0 = 20;    // warps 20..23: epilogue, tensor-memory lane quarter = warp % 4
-constexpr int EPI_WARPS = 4;
-constexpr int THREADS = (EPI_WARP0 + EPI_WARPS) * 32;
 constexpr int B_BYTES = BN * BK * 2;  // one stage of f16 tokens
-constexpr int ASTAGES = 4;            // dequantised weight stages (tensor memory)
-constexpr int BSTAGES = 4;            // token-tile stages (shared memory)
-// Tensor memory: two f32 accumulators at columns [0, BN) and [BN, 2 BN) (lane = weight row), used
-// by alternate work items; stage s of the dequantised f16 weights at columns A_COL0 + 64 s .. +63
-// (lane = weight row, two K values per 32-bit column), the operand layout tcgen05.mma reads for A
-// from tensor memory.
-constexpr int A_COL0 = 2 * BN;
-constexpr int A_COLS = BK / 2;
-constexpr int TMEM_COLS = 512;
-static_assert(A_COL0 + ASTAGES * A_COLS <= TMEM_COLS, "tensor memory budget");
-static_assert(EPI_WARP0 % 4 == 0, "epilogue warp w reads tensor-memory lane quarter w % 4");
+constexpr int A_COLS = BK / 2;        // tensor-memory columns of one dequantised weight stage
+constexpr int EPI_WARPS = 4;
+
+// Kernel shapes. Warps 0 .. DQW-1 dequantise, DQW issues MMAs, DQW+1 streams weight units, DQW+2
+// streams token tiles, DQW+4 .. DQW+7 run the epilogue (tensor-memory lane quarter = warp % 4).
+// Tensor memory: NACC f32 accumulators at columns [a BN, (a + 1) BN) (lane = weight row), used by
+// successive work items in turn; stage s of the dequantised f16 weights at columns
+// A_COL0 + 64 s .. +63 (lane = weight row, two K values per 32-bit column), the operand layout
+// tcgen05.mma reads for A from tensor memory. One commit per chunk frees its weight stage and its
+// token stage together, so both rings have STG stages.
+//   Wide:  one CTA per SM, 16 dequant warps, 4 stages, 2 accumulators (epilogue of one item
+//          overlaps the main loop of the next), 512 columns.
+//   Pair:  two CTAs per SM, 8 dequant warps each, 2 stages, 1 accumulator, 256 columns: two MMA
+//          issuers and two dequant pipelines per SM, each CTA's epilogue overlapping the other's
+//          main loop.
+template <int DQW_, int STG_, int NACC_, int RING_, int CTAS_>
+struct GemmShape {
+  static constexpr int DQW = DQW_;
+  static constexpr int QPW = 16 / DQW_;  // 32-column quarters of a chunk each dequant thread covers
+  static constexpr int STG = STG_;
+  static constexpr int NACC = NACC_;
+  static constexpr int RING = RING_;
+  static constexpr int CTAS_PER_SM = CTAS_;
+  static constexpr int MMA_WARP = DQW_;
+  static constexpr int WLOAD_WARP = DQW_ + 1;
+  static constexpr int TLOAD_WARP = DQW_ + 2;
+  static constexpr int EPI_WARP0 = DQW_ + 4;
+  static constexpr int THREADS = (DQW_ + 4 + EPI_WARPS) * 32;
+  static constexpr int A_COL0 = NACC_ * BN;
+  static constexpr int TMEM_COLS = (A_COL0 + STG_ * A_COLS) <= 256 ? 256 : 512;
+  static_assert(A_COL0 + STG_ * A_COLS <= TMEM_COLS, "tensor memory budget");
+  static_assert(TMEM_COLS * CTAS_ <= 512, "co-resident CTAs must fit tensor memory together");
+  static_assert(DQW_ % 4 == 0 && 16 % DQW_ == 0, "dequant warps cover whole lane quarters");
+};
+using WideShape = GemmShape<16, 4, 2, 4, 1>;
+using PairShape = GemmShape<8, 2, 1, 2, 2>;
 constexpr int Q4K_UNIT = BM * 128 + BM * 32;
 constexpr int TMA_ROWS = 32;  // token rows per TMA box  // Q4_K unit: quants + per-sub-block scale pairs
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -191,7 +212,6 @@ struct GemmParams {
 struct FP8W {
   static constexpr int UNIT_BYTES = BM * BK;  // one 128-column chunk of the tile: 16 KB
   static constexpr int CHUNKS_PER_UNIT = 1;
-  static constexpr int RING = 4;
   struct Raw {
     uint4 q[2];
     float s;
@@ -236,7 +256,6 @@ struct FP8W {
 struct Q4KW {
   static constexpr int UNIT_BYTES = Q4K_UNIT;  // one 256-column super-block of the tile: 20 KB
   static constexpr int CHUNKS_PER_UNIT = 2;
-  static constexpr int RING = 4;
   struct Raw {
     uint4 q;     // 16 quant bytes: low nibbles of sub-block 2c, high nibbles of 2c + 1
     uint2 s;     // {d*sc, -dmin*m} f16 pairs of sub-blocks 2c and 2c + 1
@@ -294,9 +313,9 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-template <class W>
+template <class W, class C>
 constexpr int gemm_smem_bytes() {
-  return W::RING * W::UNIT_BYTES + BSTAGES * B_BYTES + 1024 + 512;
+  return C::RING * W::UNIT_BYTES + C::STG * B_BYTES + 1024 + 512;
 }
 
 // ---- the GEMM ------------------------------------------------------------------------------------
@@ -308,13 +327,13 @@ constexpr int gemm_smem_bytes() {
 // depend on N), so the static schedule balances. Warp roles, all hand-offs through mbarriers and
 // all rings continuing across item boundaries:
 //   * warps 0..15 dequantise chunk q (a global chunk counter) from the weight ring into tensor-memory
-//     stage q % ASTAGES once the MMAs of chunk q - ASTAGES released it (a_free), and arrive a_full;
+//     stage q % ASTAGES once the MMAs of chunk q - ASTAGES released it (stage_free), and arrive a_full;
 //     after the last chunk of a weight unit they arrive raw_free for its ring slot;
 //   * warp 16 (one lane) issues the 8 MMAs of each chunk into the item's accumulator (two
-//     accumulators alternate between items), commits them to a_free and b_free, and after the last
+//     accumulators alternate between items), commits them to stage_free, and after the last
 //     chunk commits acc_full; it waits acc_free before reusing an accumulator;
 //   * warp 17 (one lane) streams weight units into the ring (1-D bulk copies, each after raw_free);
-//   * warp 18 (one lane) streams token tiles into the B stages (2-D TMA, each after b_free);
+//   * warp 18 (one lane) streams token tiles into the B stages (2-D TMA, each after stage_free);
 //   * warps 20..23 run the epilogue of item j while the next item computes: tensor-memory lane
 //     quarter w % 4, per-column scales and destinations loaded before acc_full completes.
 // A wait that runs past its limit (or sees another role give up) sets s_abort; every role stops at
@@ -339,21 +358,21 @@ __device__ __forceinline__ Item decode_item(const GemmParams& p, int w) {
   return it;
 }
 
-template <class W>
-__global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, const __grid_constant__ CUtensorMap tmap) {
+template <class W, class C>
+__global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
+    expert_gemm_kernel(GemmParams p, const __grid_constant__ CUtensorMap tmap) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  unsigned char* sB = smem;                                // [BSTAGES][B_BYTES]
-  unsigned char* sR = sB + BSTAGES * B_BYTES;              // [RING][UNIT_BYTES] raw weights
-  uint64_t* raw_full = reinterpret_cast<uint64_t*>(sR + W::RING * W::UNIT_BYTES);
-  uint64_t* raw_free = raw_full + W::RING;
-  uint64_t* b_full = raw_free + W::RING;
-  uint64_t* b_free = b_full + BSTAGES;
-  uint64_t* a_full = b_free + BSTAGES;
-  uint64_t* a_free = a_full + ASTAGES;
-  uint64_t* acc_full = a_free + ASTAGES;
-  uint64_t* acc_free = acc_full + 2;
-  uint64_t* mma_done = acc_free + 2;
+  unsigned char* sB = smem;                                // [C::STG][B_BYTES]
+  unsigned char* sR = sB + C::STG * B_BYTES;              // [RING][UNIT_BYTES] raw weights
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(sR + C::RING * W::UNIT_BYTES);
+  uint64_t* raw_free = raw_full + C::RING;
+  uint64_t* b_full = raw_free + C::RING;
+  uint64_t* a_full = b_full + C::STG;
+  uint64_t* stage_free = a_full + C::STG;  // MMAs of the stage's chunk done: weights and tokens reusable
+  uint64_t* acc_full = stage_free + C::STG;
+  uint64_t* acc_free = acc_full + C::NACC;
+  uint64_t* mma_done = acc_free + C::NACC;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   __shared__ volatile int s_abort;
   __shared__ int s_units_issued, s_tiles_issued;
@@ -368,19 +387,18 @@ __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, c
   const int G = gridDim.x;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < W::RING; ++s) {
+    for (int s = 0; s < C::RING; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_free[s], DQ_WARPS);
+      mbar_init(&raw_free[s], C::DQW);
     }
-    for (int s = 0; s < BSTAGES; ++s) {
+    for (int s = 0; s < C::STG; ++s) {
       mbar_init(&b_full[s], 1);
-      mbar_init(&b_free[s], 1);
     }
-    for (int s = 0; s < ASTAGES; ++s) {
-      mbar_init(&a_full[s], DQ_WARPS);  // one arrival per dequant warp
-      mbar_init(&a_free[s], 1);
+    for (int s = 0; s < C::STG; ++s) {
+      mbar_init(&a_full[s], C::DQW);  // one arrival per dequant warp
+      mbar_init(&stage_free[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < C::NACC; ++s) {
       mbar_init(&acc_full[s], 1);
       mbar_init(&acc_free[s], EPI_WARPS);
     }
@@ -392,7 +410,7 @@ __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, c
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS));
+                 "r"(C::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -401,15 +419,15 @@ __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, c
   const uint32_t tmem = *tmem_slot;
   volatile int* abort = &s_abort;
 
-  if (warp == WLOAD_WARP) {
+  if (warp == C::WLOAD_WARP) {
     // ---------------- weight units -> ring ----------------
     if (lane == 0) {
       int g = 0;
       for (int w = blockIdx.x; w < n_items && !*abort; w += G) {
         const Item it = decode_item(p, w);
         for (int u = 0; u < units; ++u, ++g) {
-          const int slot = g % W::RING;
-          if (g >= W::RING && !mbar_wait(&raw_free[slot], ((g / W::RING) - 1) & 1, abort)) {
+          const int slot = g % C::RING;
+          if (g >= C::RING && !mbar_wait(&raw_free[slot], ((g / C::RING) - 1) & 1, abort)) {
             s_abort = 1;
             break;
           }
@@ -420,7 +438,7 @@ __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, c
       }
     }
     __syncwarp();
-  } else if (warp == TLOAD_WARP) {
+  } else if (warp == C::TLOAD_WARP) {
     // ---------------- token tiles -> B stages ----------------
     if (lane == 0) {
       int q = 0;
@@ -428,8 +446,8 @@ __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, c
         const Item it = decode_item(p, w);
         const int boxes = (it.nmma + TMA_ROWS - 1) / TMA_ROWS;  // only the tile's own token rows
         for (int kc = 0; kc < kchunks; ++kc, ++q) {
-          const int b = q % BSTAGES;
-          if (q >= BSTAGES && !mbar_wait(&b_free[b], ((q / BSTAGES) - 1) & 1, abort)) {
+          const int b = q % C::STG;
+          if (q >= C::STG && !mbar_wait(&stage_free[b], ((q / C::STG) - 1) & 1, abort)) {
             s_abort = 1;
             break;
           }
@@ -443,15 +461,15 @@ __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, c
       }
     }
     __syncwarp();
-  } else if (warp == MMA_WARP) {
+  } else if (warp == C::MMA_WARP) {
     // ---------------- MMA issue ----------------
     if (lane == 0) {
       const uint64_t bdesc0 = smem_desc(smem_u32(sB));
       int q = 0, j = 0;
       for (int w = blockIdx.x; w < n_items && !*abort; w += G, ++j) {
         const Item it = decode_item(p, w);
-        const int acc = j & 1;
-        if (j >= 2 && !mbar_wait(&acc_free[acc], ((j >> 1) - 1) & 1, abort)) {
+        const int acc = j % C::NACC;
+        if (j >= C::NACC && !mbar_wait(&acc_free[acc], ((j / C::NACC) - 1) & 1, abort)) {
           s_abort = 1;
           break;
         }
@@ -459,20 +477,19 @@ __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, c
         const uint32_t idesc = idesc_f16(it.nmma);
         const uint32_t dcol = tmem + (uint32_t)(acc * BN);
         for (int kc = 0; kc < kchunks; ++kc, ++q) {
-          const int sa = q % ASTAGES, b = q % BSTAGES;
-          if (!mbar_wait(&a_full[sa], (q / ASTAGES) & 1, abort) || !mbar_wait(&b_full[b], (q / BSTAGES) & 1, abort)) {
+          const int sa = q % C::STG, b = q % C::STG;
+          if (!mbar_wait(&a_full[sa], (q / C::STG) & 1, abort) || !mbar_wait(&b_full[b], (q / C::STG) & 1, abort)) {
             s_abort = 1;
             break;
           }
           tc_fence_after();
-          const uint32_t acol = tmem + (uint32_t)(A_COL0 + sa * A_COLS);
+          const uint32_t acol = tmem + (uint32_t)(C::A_COL0 + sa * A_COLS);
           const uint64_t bd = bdesc0 + ((uint32_t)(b * B_BYTES) >> 4);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
             umma_f16_ts(dcol, acol + (uint32_t)(k * 8), bd + (uint32_t)(((k >> 2) * (BN * 128) + (k & 3) * 32) >> 4),
                         idesc, (kc > 0 || k > 0) ? 1u : 0u);
-          umma_commit(&a_free[sa]);
-          umma_commit(&b_free[b]);
+          umma_commit(&stage_free[sa]);
         }
         if (*abort) break;
         umma_commit(&acc_full[acc]);
@@ -482,13 +499,13 @@ __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, c
       if (!mbar_wait(mma_done, 0, nullptr)) s_abort = 1;
     }
     __syncwarp();
-  } else if (warp >= EPI_WARP0) {
+  } else if (warp >= C::EPI_WARP0) {
     // ---------------- epilogue ----------------
     const int quad = warp & 3;  // tensor-memory lanes 32 quad .. +31
     int j = 0;
     for (int w = blockIdx.x; w < n_items; w += G, ++j) {
       const Item it = decode_item(p, w);
-      const int acc = j & 1;
+      const int acc = j % C::NACC;
       // per-column scale (and, for the down projection, destination pair), columns lane + 32 t
       float csc[4];
       int cpr[4];
@@ -506,7 +523,7 @@ __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, c
           }
         }
       }
-      const bool ok = __all_sync(FULL, mbar_wait(&acc_full[acc], (j >> 1) & 1, abort));
+      const bool ok = __all_sync(FULL, mbar_wait(&acc_full[acc], (j / C::NACC) & 1, abort));
       if (!ok) {
         if (lane == 0) s_abort = 1;
         break;
@@ -546,38 +563,45 @@ __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, c
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_free[acc]);
     }
-  } else if (warp < DQ_WARPS) {
+  } else if (warp < C::DQW) {
     // ---------------- dequant ----------------
     // warp w owns tensor-memory lanes 32 (w % 4) .. +31 (its weight rows, one per thread) and the
-    // 32-column quarter w / 4 of each chunk
-    const int drow = threadIdx.x & (BM - 1), dq = threadIdx.x >> 7;
-    const uint32_t lane_base = tmem + ((uint32_t)(drow & ~31) << 16) + (uint32_t)(A_COL0 + (dq >> 1) * 32);
+    // QPW 32-column quarters QPW (w / 4) .. of each chunk
+    const int drow = threadIdx.x & (BM - 1), dq0 = (warp >> 2) * C::QPW;
+    const uint32_t lane_base = tmem + ((uint32_t)(drow & ~31) << 16) + (uint32_t)C::A_COL0;
     int q = 0, g = 0;
     bool stop = false;
     for (int w = blockIdx.x; w < n_items && !stop; w += G) {
       const Item it = decode_item(p, w);
       for (int kc = 0; kc < kchunks; ++kc, ++q) {
-        const int gu = g + kc / W::CHUNKS_PER_UNIT, slot = gu % W::RING;
-        const bool ok_raw = mbar_wait(&raw_full[slot], (gu / W::RING) & 1, abort);
+        const int gu = g + kc / W::CHUNKS_PER_UNIT, slot = gu % C::RING;
+        const bool ok_raw = mbar_wait(&raw_full[slot], (gu / C::RING) & 1, abort);
         // the tcgen05 stores below are warp-collective: every lane takes the same branch
         stop = __any_sync(FULL, !ok_raw);
         if (stop) break;
-        typename W::Raw raw;
-        W::read(p, sR + slot * W::UNIT_BYTES, it.e, it.tile, kc, drow, dq, raw);
+        typename W::Raw raw[C::QPW];
+#pragma unroll
+        for (int d = 0; d < C::QPW; ++d) W::read(p, sR + slot * W::UNIT_BYTES, it.e, it.tile, kc, drow, dq0 + d, raw[d]);
         if ((kc + 1) % W::CHUNKS_PER_UNIT == 0) {  // last read of this unit: hand the slot back
           __syncwarp();
           if (lane == 0) mbar_arrive(&raw_free[slot]);
         }
-        uint4 vals[4];
-        W::dequant(raw, kc, dq, vals);
-        const int sa = q % ASTAGES;
-        const bool ok_a = q < ASTAGES || mbar_wait(&a_free[sa], ((q / ASTAGES) - 1) & 1, abort);
+        uint4 vals[C::QPW][4];
+#pragma unroll
+        for (int d = 0; d < C::QPW; ++d) W::dequant(raw[d], kc, dq0 + d, vals[d]);
+        const int sa = q % C::STG;
+        const bool ok_a = q < C::STG || mbar_wait(&stage_free[sa], ((q / C::STG) - 1) & 1, abort);
         stop = __any_sync(FULL, !ok_a);
         if (stop) break;
         tc_fence_after();  // order the stores after the MMAs that read this stage
         const uint32_t stage = lane_base + (uint32_t)(sa * A_COLS);
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) tmem_st4(stage + (uint32_t)(W::chunk_of(dq, jj) * 4), vals[jj]);
+        for (int d = 0; d < C::QPW; ++d) {
+          const int dq = dq0 + d;
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj)
+            tmem_st4(stage + (uint32_t)((dq >> 1) * 32 + W::chunk_of(dq, jj) * 4), vals[d][jj]);
+        }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
         __syncwarp();
@@ -590,35 +614,58 @@ __global__ void __launch_bounds__(THREADS, 1) expert_gemm_kernel(GemmParams p, c
   __syncthreads();
 
   // After an abort, wait (bounded) for the copies still in flight: the last RING weight units and the
-  // last BSTAGES token tiles issued (earlier ones were consumed, so their phases completed).
+  // last C::STG token tiles issued (earlier ones were consumed, so their phases completed).
   const bool failed = s_abort != 0;
   if (failed && threadIdx.x == 0) {
-    for (int u = max(0, s_units_issued - W::RING); u < s_units_issued; ++u)
-      (void)mbar_wait(&raw_full[u % W::RING], (u / W::RING) & 1, nullptr);
-    for (int c = max(0, s_tiles_issued - BSTAGES); c < s_tiles_issued; ++c)
-      (void)mbar_wait(&b_full[c % BSTAGES], (c / BSTAGES) & 1, nullptr);
+    for (int u = max(0, s_units_issued - C::RING); u < s_units_issued; ++u)
+      (void)mbar_wait(&raw_full[u % C::RING], (u / C::RING) & 1, nullptr);
+    for (int c = max(0, s_tiles_issued - C::STG); c < s_tiles_issued; ++c)
+      (void)mbar_wait(&b_full[c % C::STG], (c / C::STG) & 1, nullptr);
     if (p.err) atomicExch(p.err, (int)MOE_ERR_TIMEOUT);
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
 }
 
 // ---- helpers around the GEMM ----------------------------------------------------------------------
 
 // (a_idx, 128-token tile) entries of the active experts, in order; one CTA.
-__global__ void tile_list_kernel(const int32_t* __restrict__ counts, const int32_t* __restrict__ active,
-                                 const int32_t* __restrict__ n_active, int32_t* __restrict__ list,
-                                 int32_t* __restrict__ n_list) {
-  if (threadIdx.x == 0) {
-    int t = 0;
-    const int na = *n_active;
-    for (int a = 0; a < na; ++a) {
-      const int nt = (counts[active[a]] + BN - 1) / BN;
-      for (int j = 0; j < nt; ++j) list[t++] = (a << 16) | j;
+constexpr int TL_THREADS = 256;
+
+// (a_idx << 16 | token tile) entries of the active experts, in active order. One CTA: each pass of
+// TL_THREADS active experts computes its tile counts, scans them across the block and writes its
+// entries; loads are independent per thread (a serial walk costs two dependent loads per expert).
+__global__ void __launch_bounds__(TL_THREADS) tile_list_kernel(const int32_t* __restrict__ counts,
+                                                               const int32_t* __restrict__ active,
+                                                               const int32_t* __restrict__ n_active,
+                                                               int32_t* __restrict__ list, int32_t* __restrict__ n_list) {
+  __shared__ int s_warp[TL_THREADS / 32];
+  __shared__ int s_base;
+  const int na = *n_active;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) s_base = 0;
+  __syncthreads();
+  for (int a0 = 0; a0 < na; a0 += TL_THREADS) {
+    const int a = a0 + threadIdx.x;
+    const int nt = a < na ? (__ldg(counts + __ldg(active + a)) + BN - 1) / BN : 0;
+    int incl = nt;  // inclusive scan within the warp, then across warps
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(FULL, incl, o);
+      if (lane >= o) incl += v;
     }
-    *n_list = t;
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    int before = s_base;
+    for (int w = 0; w < warp; ++w) before += s_warp[w];
+    const int start = before + incl - nt;
+    for (int j = 0; j < nt; ++j) list[start + j] = (a << 16) | j;
+    __syncthreads();
+    if (threadIdx.x == TL_THREADS - 1) s_base = start + nt;
+    __syncthreads();
   }
+  if (threadIdx.x == 0) *n_list = s_base;
 }
 
 // Sorted, f16 copy of the tokens (one warp per sorted pair): each row scaled by a power of two so
@@ -843,21 +890,21 @@ moe_status tc_gather(const void* x_bf16, const float* x_f32, int K, int width, c
 
 moe_status tc_tile_list(const int32_t* counts, const int32_t* active, const int32_t* n_active, int32_t* list,
                         int32_t* n_list, cudaStream_t st) {
-  tc::tile_list_kernel<<<1, 32, 0, st>>>(counts, active, n_active, list, n_list);
+  tc::tile_list_kernel<<<1, tc::TL_THREADS, 0, st>>>(counts, active, n_active, list, n_list);
   MOE_CUDA_TRY(cudaGetLastError());
   return MOE_OK;
 }
 
 
 
-template <class W>
+template <class W, class C>
 static moe_status launch_tc(const TcArgs& a, cudaStream_t st) {
   static bool attr[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr[dev & 63]) {
-    MOE_CUDA_TRY(cudaFuncSetAttribute(tc::expert_gemm_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      tc::gemm_smem_bytes<W>()));
+    MOE_CUDA_TRY(cudaFuncSetAttribute(tc::expert_gemm_kernel<W, C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      tc::gemm_smem_bytes<W, C>()));
     attr[dev & 63] = true;
   }
   tc::GemmParams p;
@@ -879,18 +926,25 @@ static moe_status launch_tc(const TcArgs& a, cudaStream_t st) {
   p.err = a.err;
   static int sms[64] = {};
   if (!sms[dev & 63]) MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev));
-  // persistent: one CTA per SM (or per work item when there are fewer)
-  const int grid = (int)std::min<int64_t>((int64_t)a.max_tiles * p.tiles, sms[dev & 63]);
+  // persistent: CTAS_PER_SM CTAs per SM (or one per work item when there are fewer)
+  const int grid = (int)std::min<int64_t>((int64_t)a.max_tiles * p.tiles, (int64_t)sms[dev & 63] * C::CTAS_PER_SM);
   if (grid <= 0) return MOE_OK;
-  tc::expert_gemm_kernel<W><<<grid, tc::THREADS, tc::gemm_smem_bytes<W>(), st>>>(p, *static_cast<const CUtensorMap*>(a.tmap));
+  tc::expert_gemm_kernel<W, C><<<grid, C::THREADS, tc::gemm_smem_bytes<W, C>(), st>>>(p, *static_cast<const CUtensorMap*>(a.tmap));
   MOE_CUDA_TRY(cudaGetLastError());
   return MOE_OK;
 }
 
 moe_status tc_gemm(int wdtype, const TcArgs& a, cudaStream_t st) {
   if (a.K % tc::BK || a.N_rows % tc::BM) return fail(MOE_ERR_INVALID, "tensor-core path: K % 128 or rows % 128");
-  if (wdtype == MOE_DTYPE_FP8_E4M3_B128) return launch_tc<tc::FP8W>(a, st);
-  if (wdtype == MOE_DTYPE_Q4_K) return launch_tc<tc::Q4KW>(a, st);
+  // MOE_TC_SHAPE=wide selects one 16-warp CTA per SM instead of two 8-warp CTAs (tuning knob)
+  static const bool wide = [] {
+    const char* v = std::getenv("MOE_TC_SHAPE");
+    return v && std::string(v) == "wide";
+  }();
+  if (wdtype == MOE_DTYPE_FP8_E4M3_B128)
+    return wide ? launch_tc<tc::FP8W, tc::WideShape>(a, st) : launch_tc<tc::FP8W, tc::PairShape>(a, st);
+  if (wdtype == MOE_DTYPE_Q4_K)
+    return wide ? launch_tc<tc::Q4KW, tc::WideShape>(a, st) : launch_tc<tc::Q4KW, tc::PairShape>(a, st);
   return fail(MOE_ERR_UNSUPPORTED, "tensor-core path: weight format not built");
 }
 
