@@ -54,6 +54,10 @@ typedef enum {
   MOE_ROUTER_SIGMOID_GROUP = 2   /* sigmoid scores + bias, group-limited top-k (DeepSeek-V3) */
 } moe_router_mode;
 
+/* Routed-id sentinel: an empty top-k slot. moe_forward and moe_plan_pairs skip it without error
+ * (the reference pads with weight 0 and a real id, gpu.rs:100-131; the sentinel also skips the work). */
+#define MOE_ID_NONE 0xFFFFFFFFu
+
 typedef struct moe_layer moe_layer;
 
 typedef struct {
@@ -98,8 +102,9 @@ moe_status moe_route(moe_layer* layer, const void* x, int T, uint32_t* ids, floa
 /* Replaces RoutedExperts::forward(xs, topk_weights, topk_ids) (cached_layer.rs:524-664,
  * expert.rs:59-117): y[t] = sum_j weights[t,j] * down(silu(gate x_t) * up x_t) of expert ids[t,j].
  * x, y: [T, H] bf16 device; ids [T, width] u32; weights [T, width] f32. `width` may differ from
- * top_k (weight-0 padded rows, gpu.rs:100-131). Ids >= num_experts fail with MOE_ERR_BAD_IDS
- * (reported by the next call that synchronises; checked on device, no host read). */
+ * top_k (weight-0 padded rows, gpu.rs:100-131). An id of MOE_ID_NONE marks an empty slot that is
+ * skipped (no expert runs for it); other ids >= num_experts fail with MOE_ERR_BAD_IDS (reported by
+ * the next call that synchronises; checked on device, no host read). */
 moe_status moe_forward(moe_layer* layer, const void* x, int T, const uint32_t* ids, const float* weights,
                        int width, void* y, void* stream);
 
@@ -160,6 +165,35 @@ size_t moe_plan_workspace_bytes(int n_pairs, int E);
 moe_status moe_route_tokens_noalloc(const void* x, const void* w_router, const float* bias, int T, int H, int E,
                                     int k, int mode, int n_group, int topk_group, float routed_scale, uint32_t* ids,
                                     float* weights, void* stream);
+
+/* ---- expert parallelism (one process per GPU, experts sharded by rank) ---------------------
+ * No counterpart in the reference, which runs one GPU plus CPU offload. Rank r owns the experts
+ * [r * experts_per_rank, (r + 1) * experts_per_rank). Each rank routes its own T tokens; a token is
+ * sent once to every rank that owns at least one of its experts (with group-limited routing and one
+ * group per rank, at most topk_group ranks), carrying its k (id, weight) slots with the ids local to
+ * the destination and the other slots set to MOE_ID_NONE / 0. The receiving rank runs moe_forward on
+ * the rows it received; the per-rank outputs travel back and moe_ep_combine sums them per token. */
+
+/* Dispatch plan. ids, weights: [T, k] (global expert ids; MOE_ID_NONE slots are ignored; other ids
+ * >= experts_per_rank * world latch MOE_ERR_BAD_IDS in error_word and are ignored). Outputs (int32
+ * unless noted, device): rank_counts [world] rows per destination; n_send [1] their sum;
+ * token_rows [T, world] the send row of (token, rank) or -1; send rows ordered by rank, then token:
+ * send_token [cap], send_ids [cap, k] u32, send_weights [cap, k] f32, cap = T * min(world, k).
+ * One CTA; world <= 64. */
+moe_status moe_ep_dispatch_plan(const uint32_t* ids, const float* weights, int T, int k, int experts_per_rank,
+                                int world, int32_t* rank_counts, int32_t* n_send, int32_t* token_rows,
+                                int32_t* send_token, uint32_t* send_ids, float* send_weights, int32_t* error_word,
+                                void* stream);
+
+/* send_x[row] = x[send_token[row]] for row < *n_send. x [T, H] bf16, send_x [cap, H] bf16. */
+moe_status moe_ep_pack_rows(const void* x, int T, int H, const int32_t* send_token, const int32_t* n_send, int cap,
+                            void* send_x, void* stream);
+
+/* y[t] = y_add[t] + sum over ranks r (in rank order) of y_back[token_rows[t, r]] (rows < 0 skipped),
+ * accumulated in f32 and rounded once to bf16. y_back [*, H] bf16 in send-row order; y_add [T, H]
+ * bf16 or NULL (e.g. the shared expert's output); y [T, H] bf16. */
+moe_status moe_ep_combine(const void* y_back, const int32_t* token_rows, int T, int world, int H, const void* y_add,
+                          void* y, void* stream);
 
 /* Library version string. */
 const char* moe_version(void);

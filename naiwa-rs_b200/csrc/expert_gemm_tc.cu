@@ -669,13 +669,17 @@ __global__ void __launch_bounds__(TL_THREADS) tile_list_kernel(const int32_t* __
 }
 
 // Sorted, f16 copy of the tokens (one warp per sorted pair): each row scaled by a power of two so
-// its max magnitude lies in [2^13, 2^14) (exact for bf16 inputs), the scale kept per row.
+// its max magnitude lies in [2^13, 2^14) (exact for bf16 inputs), the scale kept per row. Only the
+// first *n_valid sorted positions exist (the plan drops empty MOE_ID_NONE slots and bad ids), so
+// warps past it return; a perm entry outside [0, n_pairs) is skipped as well.
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ xf, int K, int width,
-                                   const int32_t* __restrict__ perm, int n_pairs, __half* __restrict__ out,
-                                   float* __restrict__ scale) {
+                                   const int32_t* __restrict__ perm, int n_pairs, const int32_t* __restrict__ n_valid,
+                                   __half* __restrict__ out, float* __restrict__ scale) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= n_pairs) return;
-  const int src = x ? perm[warp] / width : warp;
+  if (warp >= n_pairs || warp >= *n_valid) return;
+  const int pair = x ? perm[warp] : warp;
+  if (pair < 0 || pair >= n_pairs) return;
+  const int src = x ? pair / width : warp;
   float m = 0.0f;
   for (int c = lane; c < K / 8; c += 32) {
     if (x) {
@@ -878,12 +882,13 @@ moe_status tc_repack(int wdtype, const uint8_t* a, const uint8_t* b, const float
 }
 
 moe_status tc_gather(const void* x_bf16, const float* x_f32, int K, int width, const int32_t* perm, int n_pairs,
+                     const int32_t* n_valid,
                      void* out_f16, float* scale, cudaStream_t st) {
   if (n_pairs <= 0) return MOE_OK;
   const int threads = 256;
   const int blocks = (int)(((int64_t)n_pairs * 32 + threads - 1) / threads);
   tc::gather_rows_kernel<<<blocks, threads, 0, st>>>(static_cast<const __nv_bfloat16*>(x_bf16), x_f32, K, width, perm,
-                                                     n_pairs, static_cast<__half*>(out_f16), scale);
+                                                     n_pairs, n_valid, static_cast<__half*>(out_f16), scale);
   MOE_CUDA_TRY(cudaGetLastError());
   return MOE_OK;
 }

@@ -418,7 +418,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   if (L->tc) {
     const int w = L->d.wdtype;
     MOE_TRY(tc_tile_list(L->counts, L->active, L->n_active, L->tile_list, L->n_tiles, st));
-    MOE_TRY(tc_gather(x, nullptr, H, width, L->perm, n_pairs, L->x16, L->xscale, st));
+    MOE_TRY(tc_gather(x, nullptr, H, width, L->perm, n_pairs, L->offsets + E, L->x16, L->xscale, st));
     TcArgs ga{};
     ga.w = L->gu_q;
     ga.wscale = L->gu_scale;
@@ -439,7 +439,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
     ga.max_tiles = (n_pairs + TC_BN - 1) / TC_BN + max_active;
     MOE_TRY(tc_gemm(w, ga, st));
     MOE_TRY(mark(events, 2, st));
-    MOE_TRY(tc_gather(nullptr, L->h, I, width, L->perm, n_pairs, L->h16, L->hscale, st));
+    MOE_TRY(tc_gather(nullptr, L->h, I, width, L->perm, n_pairs, L->offsets + E, L->h16, L->hscale, st));
     TcArgs da = ga;
     da.w = L->dn_q;
     da.wscale = L->dn_scale;

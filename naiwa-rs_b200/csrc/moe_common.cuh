@@ -149,4 +149,33 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Exclusive scan of v over the block (blockDim.x == 1024), returns the prefix, *total the sum.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(FULL, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int s = warp_sums[lane];
+    int z = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(FULL, z, o);
+      if (lane >= o) z += y;
+    }
+    warp_sums[lane] = z - s;  // exclusive warp base
+    if (lane == 31) warp_sums[32] = z;
+  }
+  __syncthreads();
+  int r = x - v + warp_sums[warp];
+  *total = warp_sums[32];
+  __syncthreads();
+  return r;
+}
+
 }  // namespace moe

@@ -21,35 +21,6 @@ constexpr int PLAN_CHUNK = PLAN_THREADS;
 constexpr int PLAN_MAX_E = 1024;
 constexpr int PLAN_SINGLE_MAX = 8 * PLAN_CHUNK;
 
-// Exclusive scan of v over the block (blockDim.x == 1024), returns the prefix, *total the sum.
-__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    int y = __shfl_up_sync(FULL, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) warp_sums[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    int s = warp_sums[lane];
-    int z = s;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      int y = __shfl_up_sync(FULL, z, o);
-      if (lane >= o) z += y;
-    }
-    warp_sums[lane] = z - s;  // exclusive warp base
-    if (lane == 31) warp_sums[32] = z;
-  }
-  __syncthreads();
-  int r = x - v + warp_sums[warp];
-  *total = warp_sums[32];
-  __syncthreads();
-  return r;
-}
-
 // Ranks the pairs of one chunk [c0, c0 + 1024) stably and scatters them to perm.
 // base[e]: first free position of expert e before this chunk (advanced by the chunk's counts).
 // whist: [PLAN_WARPS][E] shared scratch.
@@ -98,7 +69,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_single_kernel(const uint32_
   for (int p = threadIdx.x; p < n_pairs; p += PLAN_THREADS) {
     uint32_t id = ids[p];
     if (id < (uint32_t)E) atomicAdd(&cnt[id], 1);
-    else bad = 1;
+    else if (id != MOE_ID_NONE) bad = 1;  // the sentinel is an empty slot
   }
   if (bad && o.err) atomicExch(o.err, (int)MOE_ERR_BAD_IDS);
   __syncthreads();
@@ -129,7 +100,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_hist_kernel(const uint32_t*
   if (p < n_pairs) {
     uint32_t id = ids[p];
     if (id < (uint32_t)E) atomicAdd(&psm[id], 1);
-    else if (err) atomicExch(err, (int)MOE_ERR_BAD_IDS);
+    else if (id != MOE_ID_NONE && err) atomicExch(err, (int)MOE_ERR_BAD_IDS);
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += PLAN_THREADS) chunk_counts[(size_t)blockIdx.x * E + e] = psm[e];

@@ -59,6 +59,8 @@ class LayerDesc(ctypes.Structure):
     ]
 
 
+MOE_ID_NONE = 0xFFFFFFFF  # empty top-k slot: skipped by the plan (include/moe_b200.h)
+
 LIB_PATH = _build.LIB
 _lib = None
 
@@ -86,6 +88,9 @@ def lib():
             "moe_route_tokens_noalloc": (i, [P, P, P, i, i, i, i, i, i, i, f, P, P, P]),
             "moe_plan_pairs": (i, [P, i, i, P, P, P, P, P, P, ctypes.c_size_t, P, P]),
             "moe_plan_workspace_bytes": (ctypes.c_size_t, [i, i]),
+            "moe_ep_dispatch_plan": (i, [P, P, i, i, i, i, P, P, P, P, P, P, P, P]),
+            "moe_ep_pack_rows": (i, [P, i, i, P, P, i, P, P]),
+            "moe_ep_combine": (i, [P, P, i, i, i, P, P, P]),
             "moe_version": (ctypes.c_char_p, []),
         }
         for name, (res, args) in sigs.items():

@@ -522,12 +522,14 @@ int orc_route(const float* logits, const float* bias, int T, int E, int k, int m
 
 /* Stable counting sort of the routed pairs by expert. The reference groups pairs per bank in
  * pair order (gpu.rs:103-132) and per row in input order (rings.rs:146-156); a stable sort keeps
- * exactly that order inside each expert. Returns -1 on an id >= E (route.rs:52-68). */
+ * exactly that order inside each expert. Ids equal to 0xFFFFFFFF (the library's MOE_ID_NONE, an
+ * empty slot) are skipped; returns -1 on any other id >= E (route.rs:52-68). */
 int orc_permute(const uint32_t* ids, int n_pairs, int E, int32_t* counts, int32_t* offsets, int32_t* perm,
                 int32_t* active, int32_t* n_active) {
   if (E <= 0 || n_pairs < 0) return -1;
   for (int e = 0; e < E; ++e) counts[e] = 0;
   for (int p = 0; p < n_pairs; ++p) {
+    if (ids[p] == 0xFFFFFFFFu) continue;
     if (ids[p] >= (uint32_t)E) return -1;
     counts[ids[p]]++;
   }
@@ -536,6 +538,7 @@ int orc_permute(const uint32_t* ids, int n_pairs, int E, int32_t* counts, int32_
   int32_t* fill = calloc((size_t)E, sizeof(int32_t));
   for (int p = 0; p < n_pairs; ++p) {
     uint32_t e = ids[p];
+    if (e == 0xFFFFFFFFu) continue;
     perm[offsets[e] + fill[e]++] = p;
   }
   free(fill);

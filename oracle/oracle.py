@@ -250,7 +250,7 @@ def permute(ids: np.ndarray, E: int):
     rc = lib().orc_permute(_p(a), n, E, _p(counts), _p(offsets), _p(perm), _p(active), _p(na))
     if rc != 0:
         raise ValueError("orc_permute: id >= E")
-    return counts, offsets, perm[:n], active[: int(na[0])]
+    return counts, offsets, perm[: int(offsets[E])], active[: int(na[0])]
 
 
 def moe_forward_f32(x, ids, w, gate, up, down):
@@ -279,4 +279,53 @@ def fused_moe_decode_q8_0(gate_q, up_q, down_q, x, ids, w, E, H, I, threads):
                                          threads, _p(y))
     if rc != 0:
         raise ValueError("fused decode: bad arguments")
+    return y
+
+
+# ---- expert parallelism (no reference counterpart: the reference runs on one GPU) -----------------
+
+ID_NONE = 0xFFFFFFFF
+
+
+def ep_dispatch_plan(ids: np.ndarray, w: np.ndarray, experts_per_rank: int, world: int):
+    """Restatement of the library's expert-parallel dispatch plan: every token is sent once to each
+    rank owning one of its experts; rows ordered by rank, then token; slot j keeps its position
+    (local id and weight where the expert lives on that rank, ID_NONE / 0 elsewhere).
+    Returns rank_counts [world], token_rows [T, world] (-1: no row), send_token, send_ids, send_w."""
+    ids = np.asarray(ids, dtype=np.uint32)
+    w = np.asarray(w, dtype=np.float32)
+    T, k = ids.shape
+    limit = experts_per_rank * world
+    valid = (ids != ID_NONE) & (ids < limit)
+    dest = np.where(valid, ids.astype(np.int64) // max(experts_per_rank, 1), -1)
+    has = np.zeros((T, world), dtype=bool)
+    for j in range(k):
+        m = dest[:, j] >= 0
+        has[np.nonzero(m)[0], dest[m, j]] = True
+    rank_counts = has.sum(0).astype(np.int32)
+    starts = np.concatenate([[0], np.cumsum(rank_counts)[:-1]]).astype(np.int64)
+    token_rows = np.full((T, world), -1, dtype=np.int32)
+    n = int(rank_counts.sum())
+    send_token = np.zeros(n, dtype=np.int32)
+    send_ids = np.full((n, k), ID_NONE, dtype=np.uint32)
+    send_w = np.zeros((n, k), dtype=np.float32)
+    for r in range(world):
+        toks = np.nonzero(has[:, r])[0]
+        rows = starts[r] + np.arange(toks.size)
+        token_rows[toks, r] = rows
+        send_token[rows] = toks
+        mine = dest[toks] == r
+        send_ids[rows] = np.where(mine, ids[toks].astype(np.int64) - r * experts_per_rank, ID_NONE).astype(np.uint32)
+        send_w[rows] = np.where(mine, w[toks], 0.0)
+    return rank_counts, token_rows, send_token, send_ids, send_w
+
+
+def ep_combine(y_back: np.ndarray, token_rows: np.ndarray, y_add=None) -> np.ndarray:
+    """y[t] = y_add[t] + sum over ranks (in order) of y_back[token_rows[t, r]], f32."""
+    T, world = token_rows.shape
+    H = y_back.shape[1]
+    y = np.zeros((T, H), dtype=np.float32) if y_add is None else np.asarray(y_add, dtype=np.float32).copy()
+    for r in range(world):
+        m = token_rows[:, r] >= 0
+        y[m] += np.asarray(y_back, dtype=np.float32)[token_rows[m, r]]
     return y
