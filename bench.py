@@ -582,6 +582,141 @@ def run_prefill(args):
         layer.close()
 
 
+# ---- expert-parallel workload: FP8 E256 top-8 group-limited, experts sharded by rank
+
+EP_E, EP_K, EP_H, EP_I, EP_T = 256, 8, 7168, 2048, 8192
+EP_FLOPS_PER_STEP = (EP_T * EP_K + EP_T) * 2 * (3 * EP_H * EP_I)  # routed pairs + one shared expert per token
+
+
+def run_ep(args):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import moe_b200 as M
+    from moe_b200 import synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    assert EP_E % world == 0 and EP_T % world == 0
+    epr, T = EP_E // world, EP_T // world
+    prov = M.RoutedExpertsProvider()
+    (g, u, d), (gs, us, ds) = synth.expert_stacks(epr, EP_H, EP_I, M.DTYPE_FP8_E4M3_B128, 0.02, seed=5000 + rank,
+                                                  device=dev, with_scales=True)
+    cfg = M.MoeConfig(num_experts=epr, num_experts_per_tok=EP_K, hidden_size=EP_H, moe_intermediate_size=EP_I)
+    local_layer = prov.build(M.ExpertLoadContext(layer=0, device=local, config=cfg, wdtype=M.DTYPE_FP8_E4M3_B128,
+                                                 gate=g, up=u, down=d, gate_scale=gs, up_scale=us, down_scale=ds,
+                                                 max_tokens=T * world))
+    del g, u, d, gs, us, ds
+    (g, u, d), (gs, us, ds) = synth.expert_stacks(1, EP_H, EP_I, M.DTYPE_FP8_E4M3_B128, 0.02, seed=4999, device=dev,
+                                                  with_scales=True)
+    scfg = M.MoeConfig(num_experts=1, num_experts_per_tok=1, hidden_size=EP_H, moe_intermediate_size=EP_I)
+    shared = prov.build(M.ExpertLoadContext(layer=0, device=local, config=scfg, wdtype=M.DTYPE_FP8_E4M3_B128,
+                                            gate=g, up=u, down=d, gate_scale=gs, up_scale=us, down_scale=ds,
+                                            max_tokens=T))
+    del g, u, d, gs, us, ds
+    torch.cuda.empty_cache()
+    w_router = synth.router_weight(EP_E, EP_H, 0.02, seed=77, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(900 + rank)
+    bias = (torch.randn(EP_E, generator=gen, device=dev) * 0.01).float()
+    x = torch.randn((T, EP_H), generator=gen, device=dev).to(torch.bfloat16)
+    layer = M.ExpertParallelMoE(local_layer, rank, world, epr, shared=shared)
+
+    def step(xin):
+        ids, w = M.route_tokens(xin, w_router, EP_K, M.ROUTER_SIGMOID_GROUP, bias=bias, n_group=8, topk_group=4,
+                                routed_scale=2.5)
+        return layer.forward(xin, w, ids)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world > 1:
+            t = torch.tensor([v], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+        return v
+
+    for _ in range(max(3, args.warmup)):
+        step(x)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            step(x)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    send_counts, recv_counts = layer.last_counts
+    rows_out = sum(send_counts) - send_counts[rank]
+    # end to end: this rank's activations copied in from pinned host memory and the output read back
+    hx = x.cpu().pin_memory()
+    hy = torch.empty_like(hx).pin_memory()
+    dx = torch.empty_like(x)
+    for _ in range(2):
+        dx.copy_(hx, non_blocking=True)
+        hy.copy_(step(dx), non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        dx.copy_(hx, non_blocking=True)
+        hy.copy_(step(dx), non_blocking=True)
+    f1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps)
+    local_layer.check()
+    shared.check()
+    try:
+        peaks_j = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        tpeak, kind = float(peaks_j["bf16_tflops"]), "measured"
+    except Exception:
+        tpeak, kind = 1590.0, "fallback"
+    tflops = EP_FLOPS_PER_STEP / (ms / 1e3) / 1e12
+    if rank == 0:
+        print(json.dumps({
+            "metric": "MoE-layer tokens/s (expert parallel, DeepSeek-V3-shaped FP8 layer, 8192 tokens per step)",
+            "value": EP_T / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "fp8 e4m3 (128x128 block scales) weights dequantised to f16 in tensor memory, tcgen05 f16 MMA",
+            "data": "synthetic: seeded N(0,0.02) FP8 experts and router, N(0,1) bf16 activations",
+            "config": {"workload": "BASELINE config 5: E256 (+1 shared) top-8 sigmoid group-limited (8 groups, "
+                                   "top-4), H7168 I2048 FP8; 8192 tokens per step split over the ranks",
+                       "experts_per_rank": epr, "tokens_per_rank": T, "parallelism": f"ep{world}",
+                       "l2": "inputs larger than L2 (11.3 GB of FP8 experts over the ranks)"},
+            "roofline": {"kernel": "whole step (route, dispatch, NCCL all-to-all, grouped GEMM, return, combine)",
+                         "bound": "tensor", "achieved": round(tflops, 1), "peak": tpeak * world,
+                         "unit": "TFLOP/s", "frac": round(tflops / (tpeak * world), 4), "peak_source": kind,
+                         "traffic": None, "rows_sent_off_rank_rank0": rows_out},
+            "e2e": {"value": EP_T / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": EP_T * EP_H * 2,
+                    "d2h_bytes_per_step": EP_T * EP_H * 2},
+            # route, dispatch plan, pack, shared-expert forward (7), local forward (7), combine
+            "gpu_launches": 17 * args.steps,
+            "clocks": clk.summary(),
+        }), flush=True)
+    local_layer.close()
+    shared.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -591,8 +726,8 @@ def main():
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
-                    help="decode: BASELINE config 2 (the headline); prefill: config 3")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep"],
+                    help="decode: BASELINE config 2 (the headline); prefill: config 3; ep: config 5")
     ap.add_argument("--batches", default=None,
                     help="comma-separated batch sizes replacing the ragged sweep (profiling runs only)")
     args = ap.parse_args()
@@ -602,6 +737,8 @@ def main():
         run_reference(args)
     elif args.workload == "prefill":
         run_prefill(args)
+    elif args.workload == "ep":
+        run_ep(args)
     else:
         run_ours(args)
 

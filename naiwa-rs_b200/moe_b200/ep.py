@@ -81,11 +81,21 @@ def ep_combine(y_back, token_rows, T: int, y_add=None, stream=None):
 
 # ---- exchange (torch.distributed) ---------------------------------------------------------------
 
+def _single(group) -> bool:
+    import torch.distributed as dist
+
+    return not dist.is_initialized() or dist.get_world_size(group) == 1
+
+
 def exchange_counts(rank_counts, group=None):
-    """All-to-all of the per-destination row counts; returns (send_counts, recv_counts) as lists."""
+    """All-to-all of the per-destination row counts; returns (send_counts, recv_counts) as lists.
+    A single rank (no process group) exchanges with itself."""
     torch = _torch()
     import torch.distributed as dist
 
+    if _single(group):
+        c = [int(v) for v in rank_counts.tolist()]
+        return c, list(c)
     recv = torch.empty_like(rank_counts)
     dist.all_to_all_single(recv, rank_counts.contiguous(), group=group)
     return [int(v) for v in rank_counts.tolist()], [int(v) for v in recv.tolist()]
@@ -98,6 +108,8 @@ def exchange_rows(send, send_counts, recv_counts, group=None):
     import torch.distributed as dist
 
     n = sum(send_counts)
+    if _single(group):
+        return send[:n]
     recv = torch.empty((sum(recv_counts),) + tuple(send.shape[1:]), dtype=send.dtype, device=send.device)
     dist.all_to_all_single(recv, send[:n].contiguous(), output_split_sizes=recv_counts,
                            input_split_sizes=send_counts, group=group)
