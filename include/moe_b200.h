@@ -195,6 +195,40 @@ moe_status moe_ep_pack_rows(const void* x, int T, int H, const int32_t* send_tok
 moe_status moe_ep_combine(const void* y_back, const int32_t* token_rows, int T, int world, int H, const void* y_add,
                           void* y, void* stream);
 
+/* ---- doorbells: host <-> device hand-off rings over mapped pinned memory ------------------
+ * Replace src/doorbell (doorbell.cu:15-149, mapped.rs:18-141, payload_ring.rs:14-81): the top-k
+ * doorbell that brings a layer's routing to the host thread without a stream sync
+ * (d2h/topk.rs:20-125) and the result doorbell that brings CPU-computed expert outputs back to the
+ * device (h2d/result.rs:27-123). A ring is `depth` slots of slot_bytes (rounded up to 16) behind a
+ * {seq, consumed, status} header in cudaHostAllocMapped memory. Publishing slot n (1-based) stores
+ * the payload, fences, then sets seq = n; the consumer waits for seq >= n, reads the slot and sets
+ * consumed = n; a producer waits while seq - consumed == depth. Device-side waits are bounded
+ * (about one second): one that runs out records MOE_ERR_TIMEOUT in the ring (see moe_ring_check)
+ * and its kernel returns without writing its destination. Host waits take timeout_us (< 0: none).
+ * One producer and one consumer per ring; the producer's calls must be made from one thread. */
+typedef struct moe_ring moe_ring;
+moe_status moe_ring_create(int device, int depth, size_t slot_bytes, moe_ring** out);
+void moe_ring_destroy(moe_ring* ring);
+size_t moe_ring_slot_bytes(const moe_ring* ring);
+/* Device -> host. Enqueues on `stream` a copy of src0[0:n0] followed by src1[0:n1] (device memory;
+ * src1 may be NULL with n1 = 0) into the next slot; *seq_out = the slot's number, the target the
+ * host waits for. */
+moe_status moe_ring_publish_from_device(moe_ring* ring, const void* src0, size_t n0, const void* src1, size_t n1,
+                                        void* stream, uint32_t* seq_out);
+/* Waits on the calling host thread until slot `target` is published, copies n bytes of it to dst
+ * (host memory) and releases the slot. MOE_ERR_TIMEOUT when it does not arrive in time. */
+moe_status moe_ring_host_take(moe_ring* ring, uint32_t target, void* dst, size_t n, int64_t timeout_us);
+/* Host -> device. Copies src[0:n] (host memory) into the next slot once one is free and publishes
+ * it; *seq_out = its number. */
+moe_status moe_ring_host_publish(moe_ring* ring, const void* src, size_t n, int64_t timeout_us, uint32_t* seq_out);
+/* Enqueues on `stream` a wait for slot `target` and a copy of n bytes of it to dst (device
+ * memory); later work on the stream sees dst filled. */
+moe_status moe_ring_device_take(moe_ring* ring, uint32_t target, void* dst, size_t n, void* stream);
+/* Synchronises `stream`, then reads and clears the ring's status: MOE_OK or MOE_ERR_TIMEOUT. */
+moe_status moe_ring_check(moe_ring* ring, void* stream);
+/* Current header counters (host view). */
+void moe_ring_counters(const moe_ring* ring, uint32_t* seq, uint32_t* consumed);
+
 /* Library version string. */
 const char* moe_version(void);
 

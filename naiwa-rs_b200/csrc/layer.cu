@@ -31,22 +31,6 @@ moe_status cuda_fail(cudaError_t e, const char* what) {
   return e == cudaErrorMemoryAllocation ? MOE_ERR_OOM : MOE_ERR_CUDA;
 }
 
-// ---- device guard ------------------------------------------------------------------------------
-
-struct DeviceGuard {
-  int prev = -1;
-  bool ok = true;
-  explicit DeviceGuard(int dev) {
-    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-    if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
-  }
-  ~DeviceGuard() {
-    int cur = -1;
-    cudaGetDevice(&cur);
-    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
-  }
-};
-
 }  // namespace moe
 
 using namespace moe;

@@ -89,4 +89,19 @@ moe_status tc_tile_list(const int32_t* counts, const int32_t* active, const int3
                         int32_t* n_list, cudaStream_t st);
 moe_status tc_gemm(int wdtype, const TcArgs& a, cudaStream_t st);
 
+// Makes `dev` current for the guard's lifetime and restores the previous device afterwards.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = true;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
 }  // namespace moe

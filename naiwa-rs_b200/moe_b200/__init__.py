@@ -13,3 +13,4 @@ from .layer import (  # noqa: F401
     ExpertLoadContext, MoeConfig, RoutedExperts, RoutedExpertsProvider, plan_pairs, route_tokens,
 )
 from .ep import ExpertParallelMoE, ep_combine, ep_dispatch, ep_pack_rows  # noqa: F401,E402
+from .doorbell import Ring  # noqa: F401,E402

@@ -91,6 +91,16 @@ def lib():
             "moe_ep_dispatch_plan": (i, [P, P, i, i, i, i, P, P, P, P, P, P, P, P]),
             "moe_ep_pack_rows": (i, [P, i, i, P, P, i, P, P]),
             "moe_ep_combine": (i, [P, P, i, i, i, P, P, P]),
+            "moe_ring_create": (i, [i, i, ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
+            "moe_ring_destroy": (None, [P]),
+            "moe_ring_slot_bytes": (ctypes.c_size_t, [P]),
+            "moe_ring_publish_from_device": (i, [P, P, ctypes.c_size_t, P, ctypes.c_size_t, P,
+                                                 ctypes.POINTER(ctypes.c_uint32)]),
+            "moe_ring_host_take": (i, [P, ctypes.c_uint32, P, ctypes.c_size_t, ctypes.c_int64]),
+            "moe_ring_host_publish": (i, [P, P, ctypes.c_size_t, ctypes.c_int64, ctypes.POINTER(ctypes.c_uint32)]),
+            "moe_ring_device_take": (i, [P, ctypes.c_uint32, P, ctypes.c_size_t, P]),
+            "moe_ring_check": (i, [P, P]),
+            "moe_ring_counters": (None, [P, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)]),
             "moe_version": (ctypes.c_char_p, []),
         }
         for name, (res, args) in sigs.items():
