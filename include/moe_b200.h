@@ -84,6 +84,11 @@ typedef struct {
   float routed_scale;            /* multiplier on routed weights (1.0 when unused) */
   int device;                    /* CUDA ordinal (reference: ctx.layer_device) */
   int max_tokens;                /* largest T of one forward call; sizes scratch at create */
+  /* Expert cache (the reference's CachedLayer slots, cached_layer.rs:1056-1228): 0 keeps every
+   * expert in device memory; 0 < cache_slots < num_experts keeps all experts in pinned host memory
+   * (already in the device layout) and cache_slots of them in device slots, managed with
+   * moe_cache_split / moe_cache_upload. A forward then runs only the resident experts' pairs. */
+  int cache_slots;
 } moe_layer_desc;
 
 /* Replaces RoutedExpertsProvider::build (src/moe/provider.rs:316-615): validates the shape,
@@ -195,6 +200,51 @@ moe_status moe_ep_pack_rows(const void* x, int T, int H, const int32_t* send_tok
 moe_status moe_ep_combine(const void* y_back, const int32_t* token_rows, int T, int world, int H, const void* y_add,
                           void* y, void* stream);
 
+/* ---- expert cache (layers created with cache_slots > 0) ------------------------------------
+ * One layer, one compute stream: the calls below and the layer's forwards must be issued from one
+ * host thread onto the same stream. */
+
+/* Route split (src/moe/stages/route.rs:19-158): for each routed pair (host ids, n_pairs), hit[p] = 1
+ * when its expert is resident, 0 when it is a miss, 2 for MOE_ID_NONE. Resident experts that are hit
+ * get this call's LRU tick; every routed pair counts toward its expert's hit count. Ids >= E other
+ * than MOE_ID_NONE fail with MOE_ERR_BAD_IDS (route.rs:52-68). Host only: no stream work. */
+moe_status moe_cache_split(moe_layer* layer, const uint32_t* ids, int n_pairs, uint8_t* hit);
+
+/* Paging (CachedLayer::admit / replace, cached_layer.rs:1056-1228; CopyStream upload with its read
+ * fence, copy_stream.rs:22-26, 66-102, 291-410): makes `experts` resident in order, each into a free
+ * slot, else into the least-recently-used slot whose expert is in neither `experts` nor `protect`;
+ * stops when no slot can be freed. Copies run on the layer's copy stream from the pinned host store,
+ * after the last forward that may read the slot; the next forward on `stream` waits for them, and the
+ * slot map is updated on `stream`. *n_loaded = experts brought in by this call. */
+moe_status moe_cache_upload(moe_layer* layer, const uint32_t* experts, int n, const uint32_t* protect, int n_protect,
+                            void* stream, int* n_loaded);
+
+/* Number of slots (0 without a cache); slot_expert [slots] receives each slot's expert or -1. */
+int moe_cache_slots(const moe_layer* layer, int32_t* slot_expert);
+
+/* Counters since create: pair hits and misses of moe_cache_split, experts uploaded and their bytes;
+ * hit_counts [E] (optional) receives each expert's routed-pair count. */
+moe_status moe_cache_stats(const moe_layer* layer, int64_t* hits, int64_t* misses, int64_t* uploads,
+                           int64_t* upload_bytes, uint64_t* hit_counts);
+
+/* ---- the cache's decision functions (host only, no CUDA) ----------------------------------- */
+/* top_k_ids (cached_layer.rs:358-363): the k largest logits, largest first, ties to the lowest
+ * index, f32 total order. Returns the count written (min(k, n)). */
+int moe_policy_top_k_ids(const float* logits, int n, int k, int32_t* out);
+/* union_by_votes (:367-379): every listed expert once, by votes, then best rank, then id. */
+int moe_policy_union_by_votes(const int32_t* const* rankings, const int32_t* lens, int n_rankings, int32_t* out);
+/* streamed_misses (:385-398): the distinct missed experts ranked by total routed weight (ties to the
+ * lower id), the first min(ceil(frac * distinct), cap). Rows of (id, weight) pairs, row_lens[rows]. */
+int moe_policy_streamed_misses(const uint32_t* ids, const float* weights, const int32_t* row_lens, int rows,
+                               float frac, int cap, uint32_t* out);
+/* lru_victim (:401-410): the slot of the least-recently-used published expert not in `protect`
+ * (ties to the lower expert id), its expert in *expert_out; -1 when there is none. */
+int moe_policy_lru_victim(const int32_t* slot_expert, const int32_t* slot_published, const uint64_t* last_use,
+                          int n_slots, const int32_t* protect, int n_protect, int32_t* expert_out);
+/* fill_candidate (:344-355): the most-routed expert not in a slot (ties to the lowest id); -1 when
+ * every slot is taken. */
+int moe_policy_fill_candidate(const int32_t* slot_expert, int n_slots, const uint64_t* hit_counts, int n_experts);
+
 /* ---- doorbells: host <-> device hand-off rings over mapped pinned memory ------------------
  * Replace src/doorbell (doorbell.cu:15-149, mapped.rs:18-141, payload_ring.rs:14-81): the top-k
  * doorbell that brings a layer's routing to the host thread without a stream sync
@@ -228,6 +278,32 @@ moe_status moe_ring_device_take(moe_ring* ring, uint32_t target, void* dst, size
 moe_status moe_ring_check(moe_ring* ring, void* stream);
 /* Current header counters (host view). */
 void moe_ring_counters(const moe_ring* ring, uint32_t* seq, uint32_t* consumed);
+
+/* ---- the CPU expert path and its executor --------------------------------------------------
+ * Replace CpuExperts::forward (src/moe/expert.rs:59-117), the miss stage's fused decode
+ * (src/moe/stages/cpu_miss.rs:21-54) and the result executor (src/executor.rs:116-166, 220-231,
+ * 330-378). The CPU experts keep a host copy of Q8_0 or BF16 GGML stacks (desc with host pointers). */
+typedef struct moe_cpu_experts moe_cpu_experts;
+typedef struct moe_executor moe_executor;
+moe_status moe_cpu_experts_create(const moe_layer_desc* desc, int n_threads, moe_cpu_experts** out);
+void moe_cpu_experts_destroy(moe_cpu_experts* cpu);
+/* Synchronous: y [T, H] f32 (host) = sum over the routed pairs with select[p] != 0 (select NULL: all),
+ * skipping MOE_ID_NONE and weight-0 slots, of w * down(silu(gate x) * up x); x [T, H] bf16 host. */
+moe_status moe_cpu_forward(const moe_cpu_experts* cpu, const uint16_t* x, const uint32_t* ids, const float* weights,
+                           int T, int width, const uint8_t* select, float* y);
+/* An executor runs moe_cpu_forward jobs FIFO on a worker thread and publishes each result ([T, H]
+ * f32) into `result_ring` (a host -> device ring whose slots hold max T * H * 4 bytes, used by this
+ * executor alone). submit copies its inputs, returns at once, and gives the ring slot the result
+ * will occupy in *target (take it with moe_ring_device_take). A failed job publishes zeros and its
+ * error is returned by the next submit or drain as MOE_ERR_WORKER. */
+moe_status moe_executor_create(moe_cpu_experts* cpu, moe_ring* result_ring, moe_executor** out);
+moe_status moe_executor_submit(moe_executor* ex, const uint16_t* x, const uint32_t* ids, const float* weights, int T,
+                               int width, const uint8_t* select, uint32_t* target);
+/* Waits until every submitted job has published; returns a latched job error if any. */
+moe_status moe_executor_drain(moe_executor* ex);
+void moe_executor_destroy(moe_executor* ex);
+/* y = bf16(y + add) over n elements (device): folds a CPU result into the GPU's output. */
+moe_status moe_add_f32_into_bf16(void* y, const float* add, int64_t n, void* stream);
 
 /* Library version string. */
 const char* moe_version(void);

@@ -1,0 +1,304 @@
+// cpu_executor.cu — routed experts on the host CPU and the asynchronous hand-off of their results.
+//
+// Reference: the CPU expert path CpuExperts::forward (src/moe/expert.rs:59-117) and the fused decode
+// the miss stage calls (src/moe/stages/cpu_miss.rs:21-54, mistralrs_quant::fused_moe_decode: gate +
+// up + SiLU per distinct (expert, row), then down and the router-weighted sum), and the executor
+// that runs such a job on a worker thread and publishes its rows through the result doorbell
+// (src/executor.rs:116-166, Pending::upload :220-231, SetFlag :330-378).
+//
+// moe_cpu_experts owns a host copy of the GGML stacks (Q8_0 or BF16) and computes any subset of a
+// call's routed pairs in two passes over a pool of std::threads: pass 1 gives h = silu(gate x) *
+// (up x) per selected pair (f32 accumulation, Q8_0 blocks dequantised on the fly), pass 2 gives
+// y[t] = sum over the token's selected pairs, in slot order, of w * (down h). moe_executor runs
+// those jobs FIFO on one worker thread and publishes each [T, H] f32 result into a host -> device
+// moe_ring; the device takes it with moe_ring_device_take (bounded wait) and folds it into the
+// GPU's output with moe_add_f32_into_bf16. A job that fails publishes zeros (so the device never
+// waits for it) and latches its error, which the next submit returns (executor.rs:124).
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <condition_variable>
+#include <cstring>
+#include <deque>
+#include <functional>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "moe_internal.cuh"
+
+using namespace moe;
+
+namespace {
+
+inline float f16_bits_to_f32(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1f, man = h & 0x3ffu, bits;
+  if (exp == 0) {
+    if (man == 0) bits = sign;
+    else {  // subnormal: renormalise
+      int e = -1;
+      do {
+        man <<= 1;
+        ++e;
+      } while (!(man & 0x400u));
+      bits = sign | ((uint32_t)(127 - 15 - e) << 23) | ((man & 0x3ffu) << 13);
+    }
+  } else if (exp == 31) bits = sign | 0x7f800000u | (man << 13);
+  else bits = sign | ((exp + 127 - 15) << 23) | (man << 13);
+  float f;
+  std::memcpy(&f, &bits, 4);
+  return f;
+}
+
+inline float bf16_bits_to_f32(uint16_t h) {
+  const uint32_t b = (uint32_t)h << 16;
+  float f;
+  std::memcpy(&f, &b, 4);
+  return f;
+}
+
+// Runs f(i) for i in [0, n) on `threads` threads (the caller's thread included).
+void parallel_for(int n, int threads, const std::function<void(int)>& f) {
+  if (n <= 0) return;
+  const int t = std::max(1, std::min(threads, n));
+  std::atomic<int> next{0};
+  auto body = [&] {
+    for (int i; (i = next.fetch_add(1)) < n;) f(i);
+  };
+  std::vector<std::thread> pool;
+  pool.reserve(t - 1);
+  for (int i = 1; i < t; ++i) pool.emplace_back(body);
+  body();
+  for (auto& th : pool) th.join();
+}
+
+}  // namespace
+
+struct moe_cpu_experts {
+  int E = 0, k = 0, H = 0, I = 0, wdtype = 0, threads = 1;
+  std::vector<uint8_t> gate, up, down;  // GGML bytes, [E, N, K] stacked
+
+  int64_t row_bytes(int K) const { return wdtype == MOE_DTYPE_Q8_0 ? (int64_t)K / 32 * 34 : (int64_t)K * 2; }
+
+  // dot of row r of expert e's [N, K] projection with x (f32, K long)
+  float dot(const std::vector<uint8_t>& stack, int N, int K, int e, int r, const float* x) const {
+    const uint8_t* row = stack.data() + ((int64_t)e * N + r) * row_bytes(K);
+    float acc = 0.0f;
+    if (wdtype == MOE_DTYPE_Q8_0) {
+      for (int b = 0; b < K / 32; ++b) {
+        const uint8_t* blk = row + b * 34;
+        uint16_t dh;
+        std::memcpy(&dh, blk, 2);
+        const int8_t* q = reinterpret_cast<const int8_t*>(blk + 2);
+        const float* xb = x + b * 32;
+        float s = 0.0f;
+        for (int i = 0; i < 32; ++i) s += (float)q[i] * xb[i];
+        acc += f16_bits_to_f32(dh) * s;
+      }
+    } else {
+      const uint16_t* w = reinterpret_cast<const uint16_t*>(row);
+      for (int i = 0; i < K; ++i) acc += bf16_bits_to_f32(w[i]) * x[i];
+    }
+    return acc;
+  }
+};
+
+struct moe_executor {
+  moe_cpu_experts* cpu = nullptr;
+  moe_ring* ring = nullptr;
+  int64_t publish_timeout_us = 10'000'000;
+  struct Job {
+    std::vector<uint16_t> x;
+    std::vector<uint32_t> ids;
+    std::vector<float> w;
+    std::vector<uint8_t> select;
+    int T = 0, width = 0;
+  };
+  std::thread worker;
+  std::mutex m;
+  std::condition_variable cv, idle_cv;
+  std::deque<Job> jobs;
+  bool stop = false, busy = false;
+  uint32_t next_target = 0;
+  std::string error;  // latched worker error, returned by the next submit
+  moe_status error_status = MOE_OK;
+};
+
+static moe_status cpu_forward_impl(const moe_cpu_experts* c, const uint16_t* x_bf16, const uint32_t* ids,
+                                   const float* w, int T, int width, const uint8_t* select, float* y) {
+  const int H = c->H, I = c->I, E = c->E;
+  for (int64_t p = 0; p < (int64_t)T * width; ++p)
+    if (ids[p] != MOE_ID_NONE && ids[p] >= (uint32_t)E)
+      return fail(MOE_ERR_BAD_IDS, "moe_cpu_forward: routed expert id >= num_experts");
+  std::vector<float> xf((size_t)T * H);
+  for (size_t i = 0; i < xf.size(); ++i) xf[i] = bf16_bits_to_f32(x_bf16[i]);
+  // the selected pairs (weight-0 slots skipped, as the reference's fused decode does)
+  std::vector<int> pairs;
+  for (int p = 0; p < T * width; ++p)
+    if ((!select || select[p]) && ids[p] != MOE_ID_NONE && w[p] != 0.0f) pairs.push_back(p);
+  std::vector<float> h((size_t)pairs.size() * I);
+  // pass 1: gate + up + SiLU per selected (expert, row)
+  parallel_for((int)pairs.size(), c->threads, [&](int i) {
+    const int p = pairs[i], t = p / width, e = (int)ids[p];
+    const float* xt = xf.data() + (size_t)t * H;
+    float* hp = h.data() + (size_t)i * I;
+    for (int n = 0; n < I; ++n) {
+      const float g = c->dot(c->gate, I, H, e, n, xt), u = c->dot(c->up, I, H, e, n, xt);
+      hp[n] = g / (1.0f + std::exp(-g)) * u;
+    }
+  });
+  // pass 2: per token, down of each selected pair in slot order, weighted and summed
+  std::vector<int> first((size_t)T + 1, 0);
+  for (int p : pairs) first[p / width + 1]++;
+  for (int t = 0; t < T; ++t) first[t + 1] += first[t];
+  parallel_for(T, c->threads, [&](int t) {
+    float* yt = y + (size_t)t * H;
+    for (int n = 0; n < H; ++n) yt[n] = 0.0f;
+    for (int i = first[t]; i < first[t + 1]; ++i) {
+      const int p = pairs[i], e = (int)ids[p];
+      const float wt = w[p];
+      const float* hp = h.data() + (size_t)i * I;
+      for (int n = 0; n < H; ++n) yt[n] += wt * c->dot(c->down, H, I, e, n, hp);
+    }
+  });
+  return MOE_OK;
+}
+
+static void executor_loop(moe_executor* ex) {
+  for (;;) {
+    moe_executor::Job job;
+    {
+      std::unique_lock<std::mutex> lk(ex->m);
+      ex->cv.wait(lk, [&] { return ex->stop || !ex->jobs.empty(); });
+      if (ex->jobs.empty()) return;  // stop requested and nothing left
+      job = std::move(ex->jobs.front());
+      ex->jobs.pop_front();
+      ex->busy = true;
+    }
+    std::vector<float> y((size_t)job.T * ex->cpu->H, 0.0f);
+    moe_status st = cpu_forward_impl(ex->cpu, job.x.data(), job.ids.data(), job.w.data(), job.T, job.width,
+                                     job.select.empty() ? nullptr : job.select.data(), y.data());
+    std::string msg = st == MOE_OK ? std::string() : last_error_message();
+    if (st != MOE_OK) std::fill(y.begin(), y.end(), 0.0f);  // publish zeros: the device never waits in vain
+    uint32_t seq = 0;
+    const moe_status ps = moe_ring_host_publish(ex->ring, y.data(), y.size() * sizeof(float), ex->publish_timeout_us, &seq);
+    std::lock_guard<std::mutex> lk(ex->m);
+    if (st != MOE_OK && ex->error_status == MOE_OK) {
+      ex->error_status = MOE_ERR_WORKER;
+      ex->error = "cpu executor job failed: " + msg;
+    }
+    if (ps != MOE_OK && ex->error_status == MOE_OK) {
+      ex->error_status = MOE_ERR_WORKER;
+      ex->error = "cpu executor could not publish its result: " + last_error_message();
+    }
+    ex->busy = false;
+    ex->idle_cv.notify_all();
+  }
+}
+
+extern "C" {
+
+moe_status moe_cpu_experts_create(const moe_layer_desc* d, int n_threads, moe_cpu_experts** out) {
+  if (!out) return fail(MOE_ERR_INVALID, "moe_cpu_experts_create: null out");
+  *out = nullptr;
+  if (!d) return fail(MOE_ERR_INVALID, "moe_cpu_experts_create: null desc");
+  if (d->wdtype != MOE_DTYPE_Q8_0 && d->wdtype != MOE_DTYPE_BF16)
+    return fail(MOE_ERR_UNSUPPORTED, "moe_cpu_experts_create: the CPU path serves Q8_0 and BF16 stacks");
+  if (d->weights_on_device) return fail(MOE_ERR_INVALID, "moe_cpu_experts_create: stacks must be host memory");
+  if (d->num_experts <= 0 || d->hidden <= 0 || d->inter <= 0 || d->hidden % 32 || d->inter % 32)
+    return fail(MOE_ERR_INVALID, "moe_cpu_experts_create: bad shape");
+  if (!d->gate || !d->up || !d->down) return fail(MOE_ERR_INVALID, "moe_cpu_experts_create: null stack");
+  moe_cpu_experts* c = new moe_cpu_experts();
+  c->E = d->num_experts;
+  c->k = d->top_k;
+  c->H = d->hidden;
+  c->I = d->inter;
+  c->wdtype = d->wdtype;
+  c->threads = n_threads > 0 ? n_threads : (int)std::max(1u, std::thread::hardware_concurrency());
+  const int64_t gu = c->row_bytes(c->H) * c->I * c->E, dn = c->row_bytes(c->I) * c->H * c->E;
+  c->gate.assign(static_cast<const uint8_t*>(d->gate), static_cast<const uint8_t*>(d->gate) + gu);
+  c->up.assign(static_cast<const uint8_t*>(d->up), static_cast<const uint8_t*>(d->up) + gu);
+  c->down.assign(static_cast<const uint8_t*>(d->down), static_cast<const uint8_t*>(d->down) + dn);
+  *out = c;
+  return MOE_OK;
+}
+
+void moe_cpu_experts_destroy(moe_cpu_experts* c) { delete c; }
+
+moe_status moe_cpu_forward(const moe_cpu_experts* c, const uint16_t* x, const uint32_t* ids, const float* weights,
+                           int T, int width, const uint8_t* select, float* y) {
+  if (!c) return fail(MOE_ERR_INVALID, "moe_cpu_forward: null experts");
+  if (T < 0 || width <= 0) return fail(MOE_ERR_INVALID, "moe_cpu_forward: need T >= 0 and width > 0");
+  if (T == 0) return MOE_OK;
+  if (!x || !ids || !weights || !y) return fail(MOE_ERR_INVALID, "moe_cpu_forward: null pointer");
+  return cpu_forward_impl(c, x, ids, weights, T, width, select, y);
+}
+
+moe_status moe_executor_create(moe_cpu_experts* cpu, moe_ring* result_ring, moe_executor** out) {
+  if (!out) return fail(MOE_ERR_INVALID, "moe_executor_create: null out");
+  *out = nullptr;
+  if (!cpu || !result_ring) return fail(MOE_ERR_INVALID, "moe_executor_create: null experts or ring");
+  moe_executor* ex = new moe_executor();
+  ex->cpu = cpu;
+  ex->ring = result_ring;
+  ex->worker = std::thread(executor_loop, ex);
+  *out = ex;
+  return MOE_OK;
+}
+
+moe_status moe_executor_submit(moe_executor* ex, const uint16_t* x, const uint32_t* ids, const float* weights, int T,
+                               int width, const uint8_t* select, uint32_t* target) {
+  if (!ex) return fail(MOE_ERR_INVALID, "moe_executor_submit: null executor");
+  if (T <= 0 || width <= 0 || !x || !ids || !weights || !target)
+    return fail(MOE_ERR_INVALID, "moe_executor_submit: bad arguments");
+  if ((size_t)T * ex->cpu->H * sizeof(float) > moe_ring_slot_bytes(ex->ring))
+    return fail(MOE_ERR_INVALID, "moe_executor_submit: T * hidden f32 exceeds the result ring's slot");
+  std::lock_guard<std::mutex> lk(ex->m);
+  if (ex->error_status != MOE_OK) {  // a failed earlier job surfaces here (executor.rs:124)
+    const moe_status st = ex->error_status;
+    const std::string msg = ex->error;
+    ex->error_status = MOE_OK;
+    ex->error.clear();
+    return fail(st, msg);
+  }
+  moe_executor::Job job;
+  job.T = T;
+  job.width = width;
+  job.x.assign(x, x + (size_t)T * ex->cpu->H);
+  job.ids.assign(ids, ids + (size_t)T * width);
+  job.w.assign(weights, weights + (size_t)T * width);
+  if (select) job.select.assign(select, select + (size_t)T * width);
+  ex->jobs.push_back(std::move(job));
+  *target = ++ex->next_target;  // jobs publish in FIFO order: the n-th job is the ring's n-th slot
+  ex->cv.notify_one();
+  return MOE_OK;
+}
+
+moe_status moe_executor_drain(moe_executor* ex) {
+  if (!ex) return fail(MOE_ERR_INVALID, "moe_executor_drain: null executor");
+  std::unique_lock<std::mutex> lk(ex->m);
+  ex->idle_cv.wait(lk, [&] { return ex->jobs.empty() && !ex->busy; });
+  if (ex->error_status != MOE_OK) {
+    const moe_status st = ex->error_status;
+    const std::string msg = ex->error;
+    ex->error_status = MOE_OK;
+    ex->error.clear();
+    return fail(st, msg);
+  }
+  return MOE_OK;
+}
+
+void moe_executor_destroy(moe_executor* ex) {
+  if (!ex) return;
+  {
+    std::lock_guard<std::mutex> lk(ex->m);
+    ex->stop = true;
+  }
+  ex->cv.notify_all();
+  if (ex->worker.joinable()) ex->worker.join();
+  delete ex;
+}
+
+}  // extern "C"

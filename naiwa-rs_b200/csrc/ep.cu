@@ -145,6 +145,12 @@ __global__ void ep_combine_kernel(const uint4* __restrict__ y_back, const int32_
   }
 }
 
+// y = bf16(float(y) + add), n elements.
+__global__ void add_f32_into_bf16_kernel(__nv_bfloat16* __restrict__ y, const float* __restrict__ add, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = __float2bfloat16_rn(__bfloat162float(y[i]) + add[i]);
+}
+
 }  // namespace moe
 
 using namespace moe;
@@ -196,6 +202,17 @@ moe_status moe_ep_combine(const void* y_back, const int32_t* token_rows, int T, 
   ep_combine_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(y_back), token_rows, T, world, H / 8, static_cast<const uint4*>(y_add),
       static_cast<uint4*>(y));
+  MOE_CUDA_TRY(cudaGetLastError());
+  return MOE_OK;
+}
+
+moe_status moe_add_f32_into_bf16(void* y, const float* add, int64_t n, void* stream) {
+  if (n < 0) return fail(MOE_ERR_INVALID, "moe_add_f32_into_bf16: n < 0");
+  if (n == 0) return MOE_OK;
+  if (!y || !add) return fail(MOE_ERR_INVALID, "moe_add_f32_into_bf16: null pointer");
+  const int threads = 256;
+  add_f32_into_bf16_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<__nv_bfloat16*>(y), add, n);
   MOE_CUDA_TRY(cudaGetLastError());
   return MOE_OK;
 }

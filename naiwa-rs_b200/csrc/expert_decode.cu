@@ -205,6 +205,7 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(Exp
   const int chunk = blockIdx.x % p.units_per_expert;
   if (a_idx >= *p.n_active) return;
   const int e = p.active[a_idx];
+  const int es = p.slot_of ? p.slot_of[e] : e;  // weights: the expert's cache slot
   const int base = p.offsets[e];
   const int count = p.offsets[e + 1] - base;
   const int ntm = NTM;
@@ -231,8 +232,8 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(Exp
     // first weight groups go out before the staging so HBM latency overlaps it
     typename WT::Stage st[STAGES];
     if (tile_ok) {
-      WT::load(p, e, tile, kb_begin, kb_end, lane, st[0]);
-      WT::load(p, e, tile, kb_begin + G, kb_end, lane, st[1]);
+      WT::load(p, es, tile, kb_begin, kb_end, lane, st[0]);
+      WT::load(p, es, tile, kb_begin + G, kb_end, lane, st[1]);
     }
     if (threadIdx.x < tpp) spair[threadIdx.x] = threadIdx.x < ntok ? p.perm[base + p0 + threadIdx.x] : -1;
     for (int n = warp; n < ntok; n += WARPS) {
@@ -246,11 +247,11 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(Exp
     for (int t = 0; t < NTM; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
     if (tile_ok) {
       for (int kb0 = kb_begin; kb0 < kb_end; kb0 += STAGES * G) {
-        WT::load(p, e, tile, kb0 + 2 * G, kb_end, lane, st[2]);
+        WT::load(p, es, tile, kb0 + 2 * G, kb_end, lane, st[2]);
         WT::template compute<NTM>(st[0], kb0, kb_end, xs, ntm, nt_used, lane, acc);
-        WT::load(p, e, tile, kb0 + 3 * G, kb_end, lane, st[0]);
+        WT::load(p, es, tile, kb0 + 3 * G, kb_end, lane, st[0]);
         WT::template compute<NTM>(st[1], kb0 + G, kb_end, xs, ntm, nt_used, lane, acc);
-        WT::load(p, e, tile, kb0 + 4 * G, kb_end, lane, st[1]);
+        WT::load(p, es, tile, kb0 + 4 * G, kb_end, lane, st[1]);
         WT::template compute<NTM>(st[2], kb0 + 2 * G, kb_end, xs, ntm, nt_used, lane, acc);
       }
     }
@@ -331,7 +332,7 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(Exp
 
 // y[t][c] = sum_j ypair[t*width + j][c] (j in order) -> bf16; pairs with a bad id are skipped.
 __global__ void combine_kernel(const float* __restrict__ ypair, const uint32_t* __restrict__ ids, int T, int width,
-                               int H, int E, __nv_bfloat16* __restrict__ y) {
+                               int H, int E, __nv_bfloat16* __restrict__ y, const int32_t* __restrict__ slot_of) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // one float4 per thread
   const int64_t total = (int64_t)T * H / 4;
   if (i >= total) return;
@@ -340,7 +341,7 @@ __global__ void combine_kernel(const float* __restrict__ ypair, const uint32_t* 
   float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int j = 0; j < width; ++j) {
     const int pr = t * width + j;
-    if (ids[pr] >= (uint32_t)E) continue;
+    if (!pair_live(ids[pr], E, slot_of)) continue;
     float4 v = reinterpret_cast<const float4*>(ypair + (int64_t)pr * H)[c4];
     s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
   }
@@ -419,12 +420,12 @@ moe_status launch_expert_gemv(int wdtype, ExpertParams p, int max_active, int ro
 }
 
 moe_status launch_combine(const float* ypair, const uint32_t* ids, int T, int width, int H, int E, void* y,
-                          cudaStream_t st) {
+                          cudaStream_t st, const int32_t* slot_of) {
   const int64_t total = (int64_t)T * H / 4;
   if (total == 0) return MOE_OK;
   const int threads = 256;
   combine_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, st>>>(
-      ypair, ids, T, width, H, E, static_cast<__nv_bfloat16*>(y));
+      ypair, ids, T, width, H, E, static_cast<__nv_bfloat16*>(y), slot_of);
   MOE_CUDA_TRY(cudaGetLastError());
   return MOE_OK;
 }

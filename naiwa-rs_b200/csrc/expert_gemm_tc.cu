@@ -205,6 +205,7 @@ struct GemmParams {
   const float* route_w;   // phase 1: routing weight per pair
   float* out;             // phase 0: h [pairs, N_rows/2]; phase 1: ypair [pairs, N_rows]
   int32_t* err;
+  const int32_t* slot_of;  // [E] cache slot of each expert, or null: weights indexed by expert id
 };
 
 // Weight formats. Weights stream through a shared-memory ring in "units" (one contiguous 1-D bulk
@@ -341,7 +342,7 @@ constexpr int gemm_smem_bytes() {
 // frees its tensor memory and returns.
 
 struct Item {
-  int e, base, n0, nval, nmma, tile;
+  int e, es, base, n0, nval, nmma, tile;  // es: the expert's weight slot
 };
 
 __device__ __forceinline__ Item decode_item(const GemmParams& p, int w) {
@@ -350,6 +351,7 @@ __device__ __forceinline__ Item decode_item(const GemmParams& p, int w) {
   it.tile = w % p.tiles;
   const int entry = __ldg(p.tile_list + ti);
   it.e = __ldg(p.active + (entry >> 16));
+  it.es = p.slot_of ? __ldg(p.slot_of + it.e) : it.e;
   it.base = __ldg(p.offsets + it.e);
   const int count = __ldg(p.offsets + it.e + 1) - it.base;
   it.n0 = (entry & 0xffff) * BN;
@@ -432,7 +434,7 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
             break;
           }
           mbar_expect_tx(&raw_full[slot], W::UNIT_BYTES);
-          bulk_load(sR + slot * W::UNIT_BYTES, W::unit_src(p, it.e, it.tile, u), W::UNIT_BYTES, &raw_full[slot]);
+          bulk_load(sR + slot * W::UNIT_BYTES, W::unit_src(p, it.es, it.tile, u), W::UNIT_BYTES, &raw_full[slot]);
           s_units_issued = g + 1;
         }
       }
@@ -581,7 +583,7 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
         if (stop) break;
         typename W::Raw raw[C::QPW];
 #pragma unroll
-        for (int d = 0; d < C::QPW; ++d) W::read(p, sR + slot * W::UNIT_BYTES, it.e, it.tile, kc, drow, dq0 + d, raw[d]);
+        for (int d = 0; d < C::QPW; ++d) W::read(p, sR + slot * W::UNIT_BYTES, it.es, it.tile, kc, drow, dq0 + d, raw[d]);
         if ((kc + 1) % W::CHUNKS_PER_UNIT == 0) {  // last read of this unit: hand the slot back
           __syncwarp();
           if (lane == 0) mbar_arrive(&raw_free[slot]);
@@ -929,6 +931,7 @@ static moe_status launch_tc(const TcArgs& a, cudaStream_t st) {
   p.route_w = a.route_w;
   p.out = a.out;
   p.err = a.err;
+  p.slot_of = a.slot_of;
   static int sms[64] = {};
   if (!sms[dev & 63]) MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev));
   // persistent: CTAS_PER_SM CTAs per SM (or one per work item when there are fewer)

@@ -10,6 +10,8 @@
 #include <mutex>
 #include <string>
 
+#include <vector>
+
 #include "moe_internal.cuh"
 #include <cmath>
 
@@ -20,6 +22,7 @@ namespace moe {
 static thread_local std::string g_last_error;
 
 void set_error(const std::string& msg) { g_last_error = msg; }
+const std::string& last_error_message() { return g_last_error; }
 
 moe_status fail(moe_status st, const std::string& msg) {
   g_last_error = msg;
@@ -76,7 +79,29 @@ struct moe_layer {
   alignas(128) unsigned char tmap_h[128];
   int64_t weight_bytes = 0;
   int64_t scratch_bytes = 0;
+  // expert cache (cache_slots > 0): every expert in pinned host memory in the device layout, `slots`
+  // of them in the device banks above; slot_of maps expert -> slot (-1: not resident)
+  int slots = 0;
+  uint8_t* hs_gu_q = nullptr;
+  uint8_t* hs_gu_s = nullptr;
+  uint8_t* hs_dn_q = nullptr;
+  uint8_t* hs_dn_s = nullptr;
+  float* hs_gu_scale = nullptr;
+  float* hs_dn_scale = nullptr;
+  int64_t gu_scale_stride = 0, dn_scale_stride = 0;  // floats per expert (tensor-core FP8 scales)
+  int32_t* slot_of = nullptr;                         // device [E]
+  std::vector<int> slot_expert;                       // [slots], -1 empty
+  std::vector<uint64_t> last_use;                     // [slots]
+  std::vector<int> slot_of_host;                      // [E]
+  std::vector<uint64_t> hit_counts;                   // [E] routed pairs seen per expert
+  uint64_t tick = 0;
+  cudaStream_t copy_stream = nullptr;
+  cudaEvent_t last_read = nullptr;    // recorded after every forward: the slots' readers
+  cudaEvent_t copies_done = nullptr;  // recorded after the latest uploads
+  bool copies_pending = false;
+  int64_t stat_hits = 0, stat_misses = 0, stat_uploads = 0, stat_upload_bytes = 0;
 };
+
 
 static void free_scratch(moe_layer* L) {
   cudaFree(L->counts);
@@ -156,6 +181,79 @@ static moe_status alloc_scratch(moe_layer* L, int max_tokens) {
   return MOE_OK;
 }
 
+// Device slot-map edits carried in the launch arguments (no host buffer to race with).
+struct SlotEdits {
+  int n;
+  int expert[64];
+  int slot[64];
+};
+
+__global__ void slot_edit_kernel(int32_t* __restrict__ slot_of, SlotEdits ed) {
+  if ((int)threadIdx.x < ed.n) slot_of[ed.expert[threadIdx.x]] = ed.slot[threadIdx.x];
+}
+
+static void free_cache(moe_layer* L) {
+  if (L->hs_gu_q) cudaFreeHost(L->hs_gu_q);
+  if (L->hs_gu_s) cudaFreeHost(L->hs_gu_s);
+  if (L->hs_dn_q) cudaFreeHost(L->hs_dn_q);
+  if (L->hs_dn_s) cudaFreeHost(L->hs_dn_s);
+  if (L->hs_gu_scale) cudaFreeHost(L->hs_gu_scale);
+  if (L->hs_dn_scale) cudaFreeHost(L->hs_dn_scale);
+  L->hs_gu_q = L->hs_gu_s = L->hs_dn_q = L->hs_dn_s = nullptr;
+  L->hs_gu_scale = L->hs_dn_scale = nullptr;
+  cudaFree(L->slot_of);
+  L->slot_of = nullptr;
+  if (L->copy_stream) cudaStreamDestroy(L->copy_stream);
+  if (L->last_read) cudaEventDestroy(L->last_read);
+  if (L->copies_done) cudaEventDestroy(L->copies_done);
+  L->copy_stream = nullptr;
+  L->last_read = L->copies_done = nullptr;
+}
+
+// Moves a projection's E-expert device buffer into pinned host memory and replaces it by a bank of
+// `slots` experts. stride: bytes per expert.
+static moe_status to_host_store(uint8_t** dev_buf, uint8_t** host_buf, int64_t stride, int E, int slots, int64_t* acct) {
+  if (!*dev_buf || stride == 0) return MOE_OK;
+  void* h = nullptr;
+  MOE_CUDA_TRY(cudaHostAlloc(&h, (size_t)(stride * E), cudaHostAllocPortable));
+  *host_buf = static_cast<uint8_t*>(h);
+  MOE_CUDA_TRY(cudaMemcpy(h, *dev_buf, (size_t)(stride * E), cudaMemcpyDeviceToHost));
+  cudaFree(*dev_buf);
+  *dev_buf = nullptr;
+  *acct -= stride * E;
+  return dalloc(dev_buf, (size_t)(stride * slots), acct);
+}
+
+static moe_status setup_cache(moe_layer* L, int64_t* acct) {
+  const int E = L->d.num_experts, S = L->slots;
+  MOE_TRY(to_host_store(&L->gu_q, &L->hs_gu_q, L->gu_q_stride, E, S, acct));
+  MOE_TRY(to_host_store(&L->gu_s, &L->hs_gu_s, L->gu_s_stride, E, S, acct));
+  MOE_TRY(to_host_store(&L->dn_q, &L->hs_dn_q, L->dn_q_stride, E, S, acct));
+  MOE_TRY(to_host_store(&L->dn_s, &L->hs_dn_s, L->dn_s_stride, E, S, acct));
+  if (L->gu_scale) {
+    uint8_t* g = reinterpret_cast<uint8_t*>(L->gu_scale);
+    uint8_t* hg = nullptr;
+    MOE_TRY(to_host_store(&g, &hg, L->gu_scale_stride * 4, E, S, acct));
+    L->gu_scale = reinterpret_cast<float*>(g);
+    L->hs_gu_scale = reinterpret_cast<float*>(hg);
+    uint8_t* d = reinterpret_cast<uint8_t*>(L->dn_scale);
+    uint8_t* hd = nullptr;
+    MOE_TRY(to_host_store(&d, &hd, L->dn_scale_stride * 4, E, S, acct));
+    L->dn_scale = reinterpret_cast<float*>(d);
+    L->hs_dn_scale = reinterpret_cast<float*>(hd);
+  }
+  MOE_TRY(dalloc(&L->slot_of, sizeof(int32_t) * E, acct));
+  MOE_CUDA_TRY(cudaMemset(L->slot_of, 0xFF, sizeof(int32_t) * E));  // nothing resident
+  MOE_CUDA_TRY(cudaStreamCreateWithFlags(&L->copy_stream, cudaStreamNonBlocking));
+  MOE_CUDA_TRY(cudaEventCreateWithFlags(&L->last_read, cudaEventDisableTiming));
+  MOE_CUDA_TRY(cudaEventCreateWithFlags(&L->copies_done, cudaEventDisableTiming));
+  L->slot_expert.assign(S, -1);
+  L->last_use.assign(S, 0);
+  L->slot_of_host.assign(E, -1);
+  L->hit_counts.assign(E, 0);
+  return MOE_OK;
+}
+
 static void free_weights(moe_layer* L) {
   cudaFree(L->gu_q);
   cudaFree(L->gu_s);
@@ -217,6 +315,7 @@ static moe_status validate_desc(const moe_layer_desc* d) {
     return fail(MOE_ERR_UNSUPPORTED, "unknown weight format");
   if (!d->gate || !d->up || !d->down) return fail(MOE_ERR_INVALID, "null expert stack");
   if (d->max_tokens <= 0) return fail(MOE_ERR_INVALID, "max_tokens must be positive");
+  if (d->cache_slots < 0) return fail(MOE_ERR_INVALID, "cache_slots must be >= 0");
   return MOE_OK;
 }
 
@@ -237,6 +336,7 @@ moe_status moe_layer_create(const moe_layer_desc* desc, moe_layer** out) {
   auto cleanup = [&](moe_status st) {
     free_weights(L);
     free_scratch(L);
+    free_cache(L);
     delete L;
     return st;
   };
@@ -298,6 +398,12 @@ moe_status moe_layer_create(const moe_layer_desc* desc, moe_layer** out) {
     cudaError_t e = cudaMemcpy(L->router_b, desc->router_bias, sizeof(float) * E,
                                on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMemcpy(router bias)"));
+  }
+  if (desc->cache_slots > 0 && desc->cache_slots < E) {
+    L->slots = desc->cache_slots;
+    L->gu_scale_stride = L->gu_scale ? tc_scale_count(w, 2 * I, H) : 0;
+    L->dn_scale_stride = L->dn_scale ? tc_scale_count(w, H, I) : 0;
+    if ((st = setup_cache(L, &acct)) != MOE_OK) return cleanup(st);
   }
   L->weight_bytes = acct;
   // the desc keeps no caller pointers beyond create
@@ -393,7 +499,12 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int n_pairs = (int)n64;
   const int E = L->d.num_experts, H = L->d.hidden, I = L->d.inter;
-  PlanOut po{L->counts, L->offsets, L->perm, L->active, L->n_active, L->err};
+  const int32_t* slot_of = L->slots ? L->slot_of : nullptr;
+  if (L->slots && L->copies_pending) {  // uploads issued since the last forward land first
+    MOE_CUDA_TRY(cudaStreamWaitEvent(st, L->copies_done, 0));
+    L->copies_pending = false;
+  }
+  PlanOut po{L->counts, L->offsets, L->perm, L->active, L->n_active, L->err, slot_of};
   MOE_TRY(mark(events, 0, st));
   MOE_TRY(plan_pairs(ids, n_pairs, E, po, L->plan_ws, L->plan_ws_bytes, st));
   MOE_TRY(mark(events, 1, st));
@@ -421,6 +532,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
     ga.err = L->err;
     ga.tmap = L->tmap_x;
     ga.max_tiles = (n_pairs + TC_BN - 1) / TC_BN + max_active;
+    ga.slot_of = slot_of;
     MOE_TRY(tc_gemm(w, ga, st));
     MOE_TRY(mark(events, 2, st));
     MOE_TRY(tc_gather(nullptr, L->h, I, width, L->perm, n_pairs, L->offsets + E, L->h16, L->hscale, st));
@@ -436,7 +548,8 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
     da.tmap = L->tmap_h;
     MOE_TRY(tc_gemm(w, da, st));
     MOE_TRY(mark(events, 3, st));
-    MOE_TRY(launch_combine(L->ypair, ids, T, width, H, E, y, st));
+    MOE_TRY(launch_combine(L->ypair, ids, T, width, H, E, y, st, slot_of));
+    if (L->slots) MOE_CUDA_TRY(cudaEventRecord(L->last_read, st));  // the slots' readers
     return mark(events, 4, st);
   }
 
@@ -459,6 +572,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   gp.perm = L->perm;
   gp.active = L->active;
   gp.n_active = L->n_active;
+  gp.slot_of = slot_of;
   MOE_TRY(launch_expert_gemv(L->d.wdtype, gp, max_active, pick_rowt(gp.tiles, gp.tpp, est, L->sms), st));
   MOE_TRY(mark(events, 2, st));
 
@@ -479,7 +593,8 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   dp.out = L->ypair;
   MOE_TRY(launch_expert_gemv(L->d.wdtype, dp, max_active, pick_rowt(dp.tiles, dp.tpp, est, L->sms), st));
   MOE_TRY(mark(events, 3, st));
-  MOE_TRY(launch_combine(L->ypair, ids, T, width, H, E, y, st));
+  MOE_TRY(launch_combine(L->ypair, ids, T, width, H, E, y, st, slot_of));
+  if (L->slots) MOE_CUDA_TRY(cudaEventRecord(L->last_read, st));  // the slots' readers
   return mark(events, 4, st);
 }
 
@@ -491,6 +606,7 @@ void moe_layer_destroy(moe_layer* L) {
   cudaDeviceSynchronize();
   free_weights(L);
   free_scratch(L);
+  free_cache(L);
   delete L;
 }
 
@@ -538,5 +654,144 @@ moe_status moe_plan_pairs(const uint32_t* ids, int n_pairs, int E, int32_t* coun
 size_t moe_plan_workspace_bytes(int n_pairs, int E) { return plan_workspace_bytes(n_pairs, E); }
 
 const char* moe_version(void) { return "moe_b200 0.1 (sm_100a)"; }
+
+}  // extern "C"
+
+// ---- expert cache: route split (a2) and paging (a8) ----------------------------------------------
+
+extern "C" {
+
+moe_status moe_cache_split(moe_layer* L, const uint32_t* ids, int n_pairs, uint8_t* hit) {
+  if (!L) return fail(MOE_ERR_INVALID, "moe_cache_split: null layer");
+  if (!L->slots) return fail(MOE_ERR_INVALID, "moe_cache_split: the layer has no expert cache (cache_slots = 0)");
+  if (n_pairs < 0 || (n_pairs && (!ids || !hit))) return fail(MOE_ERR_INVALID, "moe_cache_split: bad arguments");
+  const int E = L->d.num_experts;
+  for (int p = 0; p < n_pairs; ++p)
+    if (ids[p] != MOE_ID_NONE && ids[p] >= (uint32_t)E)
+      return fail(MOE_ERR_BAD_IDS, "moe_cache_split: routed expert id " + std::to_string(ids[p]) + " >= num_experts");
+  const uint64_t tick = ++L->tick;
+  for (int p = 0; p < n_pairs; ++p) {
+    const uint32_t id = ids[p];
+    if (id == MOE_ID_NONE) {
+      hit[p] = 2;
+      continue;
+    }
+    L->hit_counts[id] += 1;
+    const int s = L->slot_of_host[id];
+    if (s >= 0) {
+      L->last_use[s] = tick;
+      hit[p] = 1;
+      ++L->stat_hits;
+    } else {
+      hit[p] = 0;
+      ++L->stat_misses;
+    }
+  }
+  return MOE_OK;
+}
+
+moe_status moe_cache_upload(moe_layer* L, const uint32_t* experts, int n, const uint32_t* protect, int n_protect,
+                            void* stream, int* n_loaded) {
+  if (n_loaded) *n_loaded = 0;
+  if (!L) return fail(MOE_ERR_INVALID, "moe_cache_upload: null layer");
+  if (!L->slots) return fail(MOE_ERR_INVALID, "moe_cache_upload: the layer has no expert cache (cache_slots = 0)");
+  if (n < 0 || n_protect < 0 || (n && !experts) || (n_protect && !protect))
+    return fail(MOE_ERR_INVALID, "moe_cache_upload: bad arguments");
+  const int E = L->d.num_experts;
+  for (int i = 0; i < n; ++i)
+    if (experts[i] >= (uint32_t)E) return fail(MOE_ERR_BAD_IDS, "moe_cache_upload: expert id >= num_experts");
+  DeviceGuard guard(L->dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // experts to keep: the caller's protect list and everything this call brings in
+  std::vector<int> keep;
+  keep.reserve((size_t)(n + n_protect));
+  for (int i = 0; i < n_protect; ++i)
+    if (protect[i] < (uint32_t)E) keep.push_back((int)protect[i]);
+  for (int i = 0; i < n; ++i) keep.push_back((int)experts[i]);
+  std::vector<int> published(L->slots, 1);
+  SlotEdits ed{};
+  bool waited = false;
+  int loaded = 0;
+  auto flush = [&]() -> moe_status {
+    if (ed.n) {
+      slot_edit_kernel<<<1, 64, 0, st>>>(L->slot_of, ed);
+      MOE_CUDA_TRY(cudaGetLastError());
+      ed.n = 0;
+    }
+    return MOE_OK;
+  };
+  for (int i = 0; i < n; ++i) {
+    const int e = (int)experts[i];
+    if (L->slot_of_host[e] >= 0) continue;  // already resident
+    int slot = -1;
+    for (int s = 0; s < L->slots; ++s)
+      if (L->slot_expert[s] < 0) {
+        slot = s;
+        break;
+      }
+    if (slot < 0) {
+      int victim = -1;
+      slot = moe_policy_lru_victim(L->slot_expert.data(), published.data(), L->last_use.data(), L->slots, keep.data(),
+                                   (int)keep.size(), &victim);
+      if (slot < 0) break;  // every slot holds an expert this call needs
+      L->slot_of_host[victim] = -1;
+      if (ed.n == 64) MOE_TRY(flush());
+      ed.expert[ed.n] = victim;
+      ed.slot[ed.n++] = -1;
+    }
+    if (!waited) {  // the previous forward's reads of any slot finish before a slot is overwritten
+      MOE_CUDA_TRY(cudaStreamWaitEvent(L->copy_stream, L->last_read, 0));
+      waited = true;
+    }
+    auto copy = [&](void* bank, const void* store, int64_t stride) -> moe_status {
+      if (!bank || !stride) return MOE_OK;
+      MOE_CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(bank) + (int64_t)slot * stride,
+                                   static_cast<const uint8_t*>(store) + (int64_t)e * stride, (size_t)stride,
+                                   cudaMemcpyHostToDevice, L->copy_stream));
+      L->stat_upload_bytes += stride;
+      return MOE_OK;
+    };
+    MOE_TRY(copy(L->gu_q, L->hs_gu_q, L->gu_q_stride));
+    MOE_TRY(copy(L->gu_s, L->hs_gu_s, L->gu_s_stride));
+    MOE_TRY(copy(L->dn_q, L->hs_dn_q, L->dn_q_stride));
+    MOE_TRY(copy(L->dn_s, L->hs_dn_s, L->dn_s_stride));
+    MOE_TRY(copy(L->gu_scale, L->hs_gu_scale, L->gu_scale_stride * 4));
+    MOE_TRY(copy(L->dn_scale, L->hs_dn_scale, L->dn_scale_stride * 4));
+    L->slot_expert[slot] = e;
+    L->last_use[slot] = L->tick;
+    L->slot_of_host[e] = slot;
+    if (ed.n == 64) MOE_TRY(flush());
+    ed.expert[ed.n] = e;
+    ed.slot[ed.n++] = slot;
+    ++loaded;
+    ++L->stat_uploads;
+  }
+  if (loaded) {
+    MOE_CUDA_TRY(cudaEventRecord(L->copies_done, L->copy_stream));
+    L->copies_pending = true;
+  }
+  MOE_TRY(flush());
+  if (n_loaded) *n_loaded = loaded;
+  return MOE_OK;
+}
+
+int moe_cache_slots(const moe_layer* L, int32_t* slot_expert) {
+  if (!L || !L->slots) return 0;
+  if (slot_expert)
+    for (int s = 0; s < L->slots; ++s) slot_expert[s] = L->slot_expert[s];
+  return L->slots;
+}
+
+moe_status moe_cache_stats(const moe_layer* L, int64_t* hits, int64_t* misses, int64_t* uploads,
+                           int64_t* upload_bytes, uint64_t* hit_counts) {
+  if (!L) return fail(MOE_ERR_INVALID, "moe_cache_stats: null layer");
+  if (hits) *hits = L->stat_hits;
+  if (misses) *misses = L->stat_misses;
+  if (uploads) *uploads = L->stat_uploads;
+  if (upload_bytes) *upload_bytes = L->stat_upload_bytes;
+  if (hit_counts)
+    for (size_t e = 0; e < L->hit_counts.size(); ++e) hit_counts[e] = L->hit_counts[e];
+  return MOE_OK;
+}
 
 }  // extern "C"

@@ -20,6 +20,7 @@ namespace moe {
 void set_error(const std::string& msg);
 moe_status fail(moe_status st, const std::string& msg);
 moe_status cuda_fail(cudaError_t e, const char* what);
+const std::string& last_error_message();  // this thread's last failure message
 
 #define MOE_CUDA_TRY(expr)                                   \
   do {                                                       \
@@ -176,6 +177,13 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* 
   *total = warp_sums[32];
   __syncthreads();
   return r;
+}
+
+// A routed pair runs when its id names an expert (< E) that is resident: with an expert cache,
+// slot_of[id] >= 0; without one (slot_of null) every expert is. MOE_ID_NONE and non-resident
+// experts are skipped; ids >= E other than MOE_ID_NONE are the caller's error.
+__device__ __forceinline__ bool pair_live(uint32_t id, int E, const int32_t* slot_of) {
+  return id < (uint32_t)E && (!slot_of || slot_of[id] >= 0);
 }
 
 }  // namespace moe

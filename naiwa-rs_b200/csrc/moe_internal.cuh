@@ -23,6 +23,7 @@ struct PlanOut {
   int32_t* active;    // [E]
   int32_t* n_active;  // [1]
   int32_t* err;       // [1] or null
+  const int32_t* slot_of = nullptr;  // [E] cache slot of each expert (-1: not resident) or null (all resident)
 };
 moe_status plan_pairs(const uint32_t* ids, int n_pairs, int E, const PlanOut& o, void* ws, size_t ws_bytes,
                       cudaStream_t st);
@@ -50,10 +51,11 @@ struct ExpertParams {
   const int32_t* active;      // [E]
   const int32_t* n_active;    // [1]
   int units_per_expert;
+  const int32_t* slot_of;     // [E] cache slot of each expert, or null: weights indexed by expert id
 };
 moe_status launch_expert_gemv(int wdtype, ExpertParams p, int max_active, int rowt, cudaStream_t st);
 moe_status launch_combine(const float* ypair, const uint32_t* ids, int T, int width, int H, int E, void* y,
-                          cudaStream_t st);
+                          cudaStream_t st, const int32_t* slot_of = nullptr);
 int choose_tpp(int K, double mean_tokens_per_expert);
 size_t expert_smem_bytes(int K, int tpp, int rowt, int warps);
 
@@ -74,6 +76,7 @@ struct TcArgs {
   int32_t* err;
   const void* tmap;
   int max_tiles;  // grid bound on (expert, token-tile) entries
+  const int32_t* slot_of = nullptr;  // [E] cache slot of each expert, or null
 };
 constexpr int TC_BN = 128;  // tokens per tensor-core tile
 moe_status make_row_tmap(void* map_out, const void* base, int64_t rows, int cols);

@@ -25,14 +25,15 @@ constexpr int PLAN_SINGLE_MAX = 8 * PLAN_CHUNK;
 // base[e]: first free position of expert e before this chunk (advanced by the chunk's counts).
 // whist: [PLAN_WARPS][E] shared scratch.
 __device__ __forceinline__ void rank_chunk(const uint32_t* __restrict__ ids, int n_pairs, int E, int c0,
-                                           int* base, int* whist, int32_t* __restrict__ perm) {
+                                           int* base, int* whist, int32_t* __restrict__ perm,
+                                           const int32_t* __restrict__ slot_of) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int i = threadIdx.x; i < PLAN_WARPS * E; i += PLAN_THREADS) whist[i] = 0;
   __syncthreads();
   const int p = c0 + threadIdx.x;
   const bool valid = p < n_pairs;
   uint32_t id = valid ? ids[p] : 0xffffffffu;
-  const bool good = valid && id < (uint32_t)E;
+  const bool good = valid && pair_live(id, E, slot_of);
   unsigned grp = __match_any_sync(FULL, good ? id : 0xfffffffeu);
   const int lrank = __popc(grp & ((1u << lane) - 1u));
   if (good && lrank == 0) whist[warp * E + id] = __popc(grp);
@@ -68,8 +69,8 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_single_kernel(const uint32_
   int bad = 0;
   for (int p = threadIdx.x; p < n_pairs; p += PLAN_THREADS) {
     uint32_t id = ids[p];
-    if (id < (uint32_t)E) atomicAdd(&cnt[id], 1);
-    else if (id != MOE_ID_NONE) bad = 1;  // the sentinel is an empty slot
+    if (pair_live(id, E, o.slot_of)) atomicAdd(&cnt[id], 1);
+    else if (id >= (uint32_t)E && id != MOE_ID_NONE) bad = 1;  // the sentinel is an empty slot
   }
   if (bad && o.err) atomicExch(o.err, (int)MOE_ERR_BAD_IDS);
   __syncthreads();
@@ -87,20 +88,21 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_single_kernel(const uint32_
   if (threadIdx.x == E - 1) o.offsets[E] = off + c;
   if (threadIdx.x == 0) *o.n_active = total;
   __syncthreads();
-  for (int c0 = 0; c0 < n_pairs; c0 += PLAN_CHUNK) rank_chunk(ids, n_pairs, E, c0, base, whist, o.perm);
+  for (int c0 = 0; c0 < n_pairs; c0 += PLAN_CHUNK) rank_chunk(ids, n_pairs, E, c0, base, whist, o.perm, o.slot_of);
 }
 
 // Large plans: per-chunk histograms -> scan -> per-chunk stable scatter.
 __global__ void __launch_bounds__(PLAN_THREADS) plan_hist_kernel(const uint32_t* __restrict__ ids, int n_pairs, int E,
-                                                                  int32_t* __restrict__ chunk_counts, int32_t* err) {
+                                                                  int32_t* __restrict__ chunk_counts, int32_t* err,
+                                                                  const int32_t* __restrict__ slot_of) {
   extern __shared__ int psm[];
   for (int e = threadIdx.x; e < E; e += PLAN_THREADS) psm[e] = 0;
   __syncthreads();
   const int p = blockIdx.x * PLAN_CHUNK + threadIdx.x;
   if (p < n_pairs) {
     uint32_t id = ids[p];
-    if (id < (uint32_t)E) atomicAdd(&psm[id], 1);
-    else if (id != MOE_ID_NONE && err) atomicExch(err, (int)MOE_ERR_BAD_IDS);
+    if (pair_live(id, E, slot_of)) atomicAdd(&psm[id], 1);
+    else if (id >= (uint32_t)E && id != MOE_ID_NONE && err) atomicExch(err, (int)MOE_ERR_BAD_IDS);
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += PLAN_THREADS) chunk_counts[(size_t)blockIdx.x * E + e] = psm[e];
@@ -133,13 +135,14 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_scan_kernel(int n_chunks, i
 
 __global__ void __launch_bounds__(PLAN_THREADS) plan_scatter_kernel(const uint32_t* __restrict__ ids, int n_pairs, int E,
                                                                      const int32_t* __restrict__ chunk_base,
-                                                                     int32_t* __restrict__ perm) {
+                                                                     int32_t* __restrict__ perm,
+                                                                     const int32_t* __restrict__ slot_of) {
   extern __shared__ int psm[];
   int* base = psm;                 // [E]
   int* whist = psm + PLAN_MAX_E;   // [(PLAN_WARPS + 1) * E]
   for (int e = threadIdx.x; e < E; e += PLAN_THREADS) base[e] = chunk_base[(size_t)blockIdx.x * E + e];
   __syncthreads();
-  rank_chunk(ids, n_pairs, E, blockIdx.x * PLAN_CHUNK, base, whist, perm);
+  rank_chunk(ids, n_pairs, E, blockIdx.x * PLAN_CHUNK, base, whist, perm, slot_of);
 }
 
 size_t plan_workspace_bytes(int n_pairs, int E) {
@@ -179,11 +182,11 @@ moe_status plan_pairs(const uint32_t* ids, int n_pairs, int E, const PlanOut& o,
   if (!ws || ws_bytes < plan_workspace_bytes(n_pairs, E))
     return fail(MOE_ERR_INVALID, "moe_plan_pairs: workspace too small");
   int32_t* chunk = static_cast<int32_t*>(ws);
-  plan_hist_kernel<<<n_chunks, PLAN_THREADS, E * sizeof(int), st>>>(ids, n_pairs, E, chunk, o.err);
+  plan_hist_kernel<<<n_chunks, PLAN_THREADS, E * sizeof(int), st>>>(ids, n_pairs, E, chunk, o.err, o.slot_of);
   MOE_CUDA_TRY(cudaGetLastError());
   plan_scan_kernel<<<1, PLAN_THREADS, 0, st>>>(n_chunks, E, chunk, o);
   MOE_CUDA_TRY(cudaGetLastError());
-  plan_scatter_kernel<<<n_chunks, PLAN_THREADS, scatter_smem(E), st>>>(ids, n_pairs, E, chunk, o.perm);
+  plan_scatter_kernel<<<n_chunks, PLAN_THREADS, scatter_smem(E), st>>>(ids, n_pairs, E, chunk, o.perm, o.slot_of);
   MOE_CUDA_TRY(cudaGetLastError());
   return MOE_OK;
 }

@@ -56,6 +56,7 @@ class LayerDesc(ctypes.Structure):
         ("routed_scale", ctypes.c_float),
         ("device", ctypes.c_int),
         ("max_tokens", ctypes.c_int),
+        ("cache_slots", ctypes.c_int),
     ]
 
 
@@ -91,6 +92,23 @@ def lib():
             "moe_ep_dispatch_plan": (i, [P, P, i, i, i, i, P, P, P, P, P, P, P, P]),
             "moe_ep_pack_rows": (i, [P, i, i, P, P, i, P, P]),
             "moe_ep_combine": (i, [P, P, i, i, i, P, P, P]),
+            "moe_cache_split": (i, [P, P, i, P]),
+            "moe_cache_upload": (i, [P, P, i, P, i, P, ctypes.POINTER(ctypes.c_int)]),
+            "moe_cache_slots": (i, [P, P]),
+            "moe_cache_stats": (i, [P, P, P, P, P, P]),
+            "moe_policy_top_k_ids": (i, [P, i, i, P]),
+            "moe_policy_union_by_votes": (i, [P, P, i, P]),
+            "moe_policy_streamed_misses": (i, [P, P, P, i, f, i, P]),
+            "moe_policy_lru_victim": (i, [P, P, P, i, P, i, P]),
+            "moe_policy_fill_candidate": (i, [P, i, P, i]),
+            "moe_cpu_experts_create": (i, [ctypes.POINTER(LayerDesc), i, ctypes.POINTER(ctypes.c_void_p)]),
+            "moe_cpu_experts_destroy": (None, [P]),
+            "moe_cpu_forward": (i, [P, P, P, P, i, i, P, P]),
+            "moe_executor_create": (i, [P, P, ctypes.POINTER(ctypes.c_void_p)]),
+            "moe_executor_submit": (i, [P, P, P, P, i, i, P, ctypes.POINTER(ctypes.c_uint32)]),
+            "moe_executor_drain": (i, [P]),
+            "moe_executor_destroy": (None, [P]),
+            "moe_add_f32_into_bf16": (i, [P, P, ctypes.c_int64, P]),
             "moe_ring_create": (i, [i, i, ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
             "moe_ring_destroy": (None, [P]),
             "moe_ring_slot_bytes": (ctypes.c_size_t, [P]),

@@ -73,6 +73,7 @@ class ExpertLoadContext:
     router_weight: Any = None  # [E, H] bf16 (torch tensor or numpy uint16)
     router_bias: Any = None    # [E] f32
     max_tokens: int = 256
+    cache_slots: int = 0  # > 0: expert cache with this many device slots (CachedLayer)
     _keep: list = field(default_factory=list)
 
 
@@ -133,12 +134,47 @@ class RoutedExperts:
         d.routed_scale = cfg.routed_scaling_factor
         d.device = ctx.device
         d.max_tokens = ctx.max_tokens
+        d.cache_slots = int(ctx.cache_slots)
         handle = ctypes.c_void_p()
         if on_dev:
             torch.cuda.synchronize(ctx.device)
         check(lib().moe_layer_create(ctypes.byref(d), ctypes.byref(handle)))
         self._h = handle
         self.max_tokens = ctx.max_tokens
+        self.cache_slots = int(ctx.cache_slots) if 0 < ctx.cache_slots < cfg.num_experts else 0
+
+    # -- expert cache (cache_slots > 0) ---------------------------------------------------------
+    def cache_split(self, ids) -> np.ndarray:
+        """Route split of host ids ([T, k] or flat): 1 hit, 0 miss, 2 empty slot (route.rs:19-158)."""
+        a = np.ascontiguousarray(np.asarray(ids).astype(np.uint32).reshape(-1))
+        hit = np.empty(a.size, np.uint8)
+        check(lib().moe_cache_split(self._h, ctypes.c_void_p(a.ctypes.data), a.size, ctypes.c_void_p(hit.ctypes.data)))
+        return hit
+
+    def cache_upload(self, experts, protect=(), stream=None) -> int:
+        """Make `experts` resident (admit / LRU replace outside `protect`); returns how many came in."""
+        e = np.ascontiguousarray(np.asarray(list(experts), dtype=np.uint32))
+        pr = np.ascontiguousarray(np.asarray(list(protect), dtype=np.uint32))
+        n = ctypes.c_int()
+        check(lib().moe_cache_upload(self._h, ctypes.c_void_p(e.ctypes.data if e.size else None), e.size,
+                                     ctypes.c_void_p(pr.ctypes.data if pr.size else None), pr.size,
+                                     ctypes.c_void_p(_stream(stream)), ctypes.byref(n)))
+        return int(n.value)
+
+    def cache_resident(self) -> np.ndarray:
+        """Each slot's expert (-1: empty)."""
+        n = lib().moe_cache_slots(self._h, None)
+        out = np.empty(n, np.int32)
+        if n:
+            lib().moe_cache_slots(self._h, ctypes.c_void_p(out.ctypes.data))
+        return out
+
+    def cache_stats(self) -> dict:
+        v = [ctypes.c_int64() for _ in range(4)]
+        hc = np.zeros(self.num_experts, np.uint64)
+        check(lib().moe_cache_stats(self._h, *[ctypes.byref(x) for x in v], ctypes.c_void_p(hc.ctypes.data)))
+        return {"hits": v[0].value, "misses": v[1].value, "uploads": v[2].value, "upload_bytes": v[3].value,
+                "hit_counts": hc}
 
     # -- lifecycle ------------------------------------------------------------------------------
     def close(self):
