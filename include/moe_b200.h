@@ -305,6 +305,16 @@ void moe_executor_destroy(moe_executor* ex);
 /* y = bf16(y + add) over n elements (device): folds a CPU result into the GPU's output. */
 moe_status moe_add_f32_into_bf16(void* y, const float* add, int64_t n, void* stream);
 
+/* ---- prefill chunking (src/moe/prefill_stream.rs:1362-1694) -------------------------------- */
+/* moe_forward over T tokens in consecutive chunks of as many tokens as the layer's scratch holds at
+ * this width (max_tokens * top_k / width), so a long prompt needs no scratch beyond create/warmup. */
+moe_status moe_forward_chunked(moe_layer* layer, const void* x, int T, const uint32_t* ids, const float* weights,
+                               int width, void* y, void* stream);
+/* out[i] = ids[i] when ids[i] is one of `experts` (host list, E <= 1024), else MOE_ID_NONE (device
+ * arrays of n ids): one wave of a paged prefill runs only the experts uploaded for it. */
+moe_status moe_select_ids(const uint32_t* ids, int64_t n, int E, const uint32_t* experts, int n_experts,
+                          uint32_t* out, void* stream);
+
 /* Library version string. */
 const char* moe_version(void);
 

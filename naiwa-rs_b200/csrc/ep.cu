@@ -145,6 +145,19 @@ __global__ void ep_combine_kernel(const uint4* __restrict__ y_back, const int32_
   }
 }
 
+// out[i] = ids[i] when its expert is in the bitmap `keep` (bit e of word e / 32), else MOE_ID_NONE.
+struct ExpertSet {
+  uint32_t words[32];  // E <= 1024
+};
+
+__global__ void select_ids_kernel(const uint32_t* __restrict__ ids, int64_t n, int E, ExpertSet keep,
+                                  uint32_t* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t id = ids[i];
+  out[i] = (id < (uint32_t)E && ((keep.words[id >> 5] >> (id & 31)) & 1u)) ? id : MOE_ID_NONE;
+}
+
 // y = bf16(float(y) + add), n elements.
 __global__ void add_f32_into_bf16_kernel(__nv_bfloat16* __restrict__ y, const float* __restrict__ add, int64_t n) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -202,6 +215,21 @@ moe_status moe_ep_combine(const void* y_back, const int32_t* token_rows, int T, 
   ep_combine_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(y_back), token_rows, T, world, H / 8, static_cast<const uint4*>(y_add),
       static_cast<uint4*>(y));
+  MOE_CUDA_TRY(cudaGetLastError());
+  return MOE_OK;
+}
+
+moe_status moe_select_ids(const uint32_t* ids, int64_t n, int E, const uint32_t* experts, int n_experts,
+                          uint32_t* out, void* stream) {
+  if (n < 0 || E <= 0 || E > 1024 || n_experts < 0) return fail(MOE_ERR_INVALID, "moe_select_ids: need 0 < E <= 1024");
+  if (n == 0) return MOE_OK;
+  if (!ids || !out || (n_experts && !experts)) return fail(MOE_ERR_INVALID, "moe_select_ids: null pointer");
+  ExpertSet keep{};
+  for (int i = 0; i < n_experts; ++i)
+    if (experts[i] < (uint32_t)E) keep.words[experts[i] >> 5] |= 1u << (experts[i] & 31);
+  const int threads = 256;
+  select_ids_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      ids, n, E, keep, out);
   MOE_CUDA_TRY(cudaGetLastError());
   return MOE_OK;
 }

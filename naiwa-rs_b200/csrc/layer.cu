@@ -795,3 +795,19 @@ moe_status moe_cache_stats(const moe_layer* L, int64_t* hits, int64_t* misses, i
 }
 
 }  // extern "C"
+
+extern "C" moe_status moe_forward_chunked(moe_layer* L, const void* x, int T, const uint32_t* ids, const float* weights,
+                                          int width, void* y, void* stream) {
+  if (!L) return fail(MOE_ERR_INVALID, "moe_forward_chunked: null layer");
+  if (T < 0 || width <= 0) return fail(MOE_ERR_INVALID, "moe_forward_chunked: need T >= 0 and width > 0");
+  const int chunk = L->cap_pairs / width;  // the most tokens one forward's scratch holds at this width
+  if (chunk <= 0) return fail(MOE_ERR_INVALID, "moe_forward_chunked: width exceeds the layer's scratch");
+  const int H = L->d.hidden;
+  for (int t0 = 0; t0 < T; t0 += chunk) {
+    const int n = T - t0 < chunk ? T - t0 : chunk;
+    MOE_TRY(forward_impl(L, static_cast<const __nv_bfloat16*>(x) + (int64_t)t0 * H, n, ids + (int64_t)t0 * width,
+                         weights + (int64_t)t0 * width, width, static_cast<__nv_bfloat16*>(y) + (int64_t)t0 * H,
+                         stream, nullptr));
+  }
+  return MOE_OK;
+}

@@ -109,6 +109,8 @@ def lib():
             "moe_executor_drain": (i, [P]),
             "moe_executor_destroy": (None, [P]),
             "moe_add_f32_into_bf16": (i, [P, P, ctypes.c_int64, P]),
+            "moe_select_ids": (i, [P, ctypes.c_int64, i, P, i, P, P]),
+            "moe_forward_chunked": (i, [P, P, i, P, P, i, P, P]),
             "moe_ring_create": (i, [i, i, ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
             "moe_ring_destroy": (None, [P]),
             "moe_ring_slot_bytes": (ctypes.c_size_t, [P]),

@@ -215,7 +215,12 @@ class RoutedExperts:
         check(lib().moe_route(self._h, _ptr(x2), T, _ptr(ids), _ptr(w), ctypes.c_void_p(_stream(stream))))
         return ids, w
 
-    def forward(self, xs, topk_weights, topk_ids, out=None, stream=None):
+    def forward_chunked(self, xs, topk_weights, topk_ids, out=None, stream=None):
+        """forward over any number of tokens, in chunks the layer's scratch holds (prefill chunking,
+        prefill_stream.rs:1362-1694)."""
+        return self.forward(xs, topk_weights, topk_ids, out=out, stream=stream, _entry="moe_forward_chunked")
+
+    def forward(self, xs, topk_weights, topk_ids, out=None, stream=None, _entry="moe_forward"):
         """sum_j topk_weights[t, j] * expert(topk_ids[t, j])(xs[t]) for every token, in xs's shape."""
         torch = _torch()
         shape = xs.shape
@@ -238,8 +243,8 @@ class RoutedExperts:
             raise MoeError(_lib.MOE_ERR_INVALID, "forward: topk_weights and topk_ids shapes differ")
         width = ids.shape[1]
         y = out if out is not None else torch.empty_like(x2)
-        check(lib().moe_forward(self._h, _ptr(x2), T, _ptr(ids), _ptr(w), width, _ptr(y),
-                                ctypes.c_void_p(_stream(stream))))
+        check(getattr(lib(), _entry)(self._h, _ptr(x2), T, _ptr(ids), _ptr(w), width, _ptr(y),
+                                     ctypes.c_void_p(_stream(stream))))
         return y.reshape(shape)
 
     __call__ = forward

@@ -97,6 +97,50 @@ class PagedMoE:
 
     __call__ = forward
 
+    def prefill(self, xs, topk_weights, topk_ids, chunk: int | None = None, stream=None):
+        """A prompt through the cached layer (PrefillStream::forward, prefill_stream.rs:1362-1694): chunks
+        of at most `chunk` tokens (default: what the layer's scratch holds); per chunk, its distinct
+        experts in waves of at most `slots` (resident ones first, so they need no upload); each wave
+        uploads its experts, runs the forward on ids restricted to them (moe_select_ids) and the wave
+        outputs are summed per token in f32 and rounded once (moe_ep_combine). All on the GPU."""
+        import ctypes
+
+        from ._lib import check, lib
+        from .ep import ep_combine
+        from .layer import _ptr, _stream
+
+        torch = _torch()
+        T, H = xs.shape
+        k = topk_ids.shape[1]
+        chunk = int(chunk or max(1, self.layer.max_tokens))
+        ids_all = topk_ids.to(torch.int32).contiguous()
+        w_all = topk_weights.to(torch.float32).contiguous()
+        ids_host = ids_all.cpu().numpy().view(np.uint32)
+        y = torch.empty_like(xs)
+        S = self.layer.cache_slots
+        for c0 in range(0, T, chunk):
+            c1 = min(T, c0 + chunk)
+            n = c1 - c0
+            ids_c, w_c, x_c = ids_all[c0:c1], w_all[c0:c1], xs[c0:c1]
+            flat = ids_host[c0:c1].reshape(-1)
+            distinct = sorted(set(flat[flat != 0xFFFFFFFF].tolist()))
+            res = set(int(e) for e in self.layer.cache_resident() if e >= 0)
+            order = [e for e in distinct if e in res] + [e for e in distinct if e not in res]
+            waves = [order[i:i + S] for i in range(0, len(order), S)] or [[]]
+            outs = []
+            for wave in waves:
+                self.layer.cache_upload(wave, protect=wave, stream=stream)
+                sel = torch.empty_like(ids_c)
+                ev = np.ascontiguousarray(np.asarray(wave, dtype=np.uint32))
+                check(lib().moe_select_ids(_ptr(ids_c), ids_c.numel(), self.layer.num_experts,
+                                           ctypes.c_void_p(ev.ctypes.data if ev.size else None), ev.size, _ptr(sel),
+                                           ctypes.c_void_p(_stream(stream))))
+                outs.append(self.layer.forward(x_c, w_c, sel, stream=stream))
+            rows = torch.arange(n, device=xs.device, dtype=torch.int32)
+            token_rows = torch.stack([rows + i * n for i in range(len(outs))], dim=1).contiguous()
+            y[c0:c1] = ep_combine(torch.cat(outs), token_rows, n, stream=stream)
+        return y
+
     def check(self, stream=None):
         self.layer.check()
         self.topk_ring.check(stream)
