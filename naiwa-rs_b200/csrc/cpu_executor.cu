@@ -81,28 +81,6 @@ struct moe_cpu_experts {
   std::vector<uint8_t> gate, up, down;  // GGML bytes, [E, N, K] stacked
 
   int64_t row_bytes(int K) const { return wdtype == MOE_DTYPE_Q8_0 ? (int64_t)K / 32 * 34 : (int64_t)K * 2; }
-
-  // dot of row r of expert e's [N, K] projection with x (f32, K long)
-  float dot(const std::vector<uint8_t>& stack, int N, int K, int e, int r, const float* x) const {
-    const uint8_t* row = stack.data() + ((int64_t)e * N + r) * row_bytes(K);
-    float acc = 0.0f;
-    if (wdtype == MOE_DTYPE_Q8_0) {
-      for (int b = 0; b < K / 32; ++b) {
-        const uint8_t* blk = row + b * 34;
-        uint16_t dh;
-        std::memcpy(&dh, blk, 2);
-        const int8_t* q = reinterpret_cast<const int8_t*>(blk + 2);
-        const float* xb = x + b * 32;
-        float s = 0.0f;
-        for (int i = 0; i < 32; ++i) s += (float)q[i] * xb[i];
-        acc += f16_bits_to_f32(dh) * s;
-      }
-    } else {
-      const uint16_t* w = reinterpret_cast<const uint16_t*>(row);
-      for (int i = 0; i < K; ++i) acc += bf16_bits_to_f32(w[i]) * x[i];
-    }
-    return acc;
-  }
 };
 
 struct moe_executor {
@@ -126,6 +104,41 @@ struct moe_executor {
   moe_status error_status = MOE_OK;
 };
 
+// Row r of expert e's [N, K] projection, dequantised to f32.
+static void dequant_row(const moe_cpu_experts* c, const std::vector<uint8_t>& stack, int N, int K, int e, int r,
+                        float* out) {
+  const uint8_t* row = stack.data() + ((int64_t)e * N + r) * c->row_bytes(K);
+  if (c->wdtype == MOE_DTYPE_Q8_0) {
+    for (int b = 0; b < K / 32; ++b) {
+      const uint8_t* blk = row + b * 34;
+      uint16_t dh;
+      std::memcpy(&dh, blk, 2);
+      const float d = f16_bits_to_f32(dh);
+      const int8_t* q = reinterpret_cast<const int8_t*>(blk + 2);
+      for (int i = 0; i < 32; ++i) out[b * 32 + i] = d * (float)q[i];
+    }
+  } else {
+    const uint16_t* w = reinterpret_cast<const uint16_t*>(row);
+    for (int i = 0; i < K; ++i) out[i] = bf16_bits_to_f32(w[i]);
+  }
+}
+
+static inline float dot_f32(const float* a, const float* b, int n) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  int i = 0;
+  for (; i + 4 <= n; i += 4) {
+    s0 += a[i] * b[i];
+    s1 += a[i + 1] * b[i + 1];
+    s2 += a[i + 2] * b[i + 2];
+    s3 += a[i + 3] * b[i + 3];
+  }
+  for (; i < n; ++i) s0 += a[i] * b[i];
+  return (s0 + s1) + (s2 + s3);
+}
+
+// Two passes over the selected pairs grouped by expert, so every weight row is dequantised once per
+// call however many of the call's tokens use the expert: pass 1 h = silu(gate x) * (up x) per pair,
+// pass 2 ypair = w * (down h) per pair; then y[t] sums the token's pairs in slot order.
 static moe_status cpu_forward_impl(const moe_cpu_experts* c, const uint16_t* x_bf16, const uint32_t* ids,
                                    const float* w, int T, int width, const uint8_t* select, float* y) {
   const int H = c->H, I = c->I, E = c->E;
@@ -134,33 +147,56 @@ static moe_status cpu_forward_impl(const moe_cpu_experts* c, const uint16_t* x_b
       return fail(MOE_ERR_BAD_IDS, "moe_cpu_forward: routed expert id >= num_experts");
   std::vector<float> xf((size_t)T * H);
   for (size_t i = 0; i < xf.size(); ++i) xf[i] = bf16_bits_to_f32(x_bf16[i]);
-  // the selected pairs (weight-0 slots skipped, as the reference's fused decode does)
+  // selected pairs (weight-0 slots skipped, as the reference's fused decode does), grouped by expert
   std::vector<int> pairs;
   for (int p = 0; p < T * width; ++p)
     if ((!select || select[p]) && ids[p] != MOE_ID_NONE && w[p] != 0.0f) pairs.push_back(p);
-  std::vector<float> h((size_t)pairs.size() * I);
-  // pass 1: gate + up + SiLU per selected (expert, row)
-  parallel_for((int)pairs.size(), c->threads, [&](int i) {
-    const int p = pairs[i], t = p / width, e = (int)ids[p];
-    const float* xt = xf.data() + (size_t)t * H;
-    float* hp = h.data() + (size_t)i * I;
-    for (int n = 0; n < I; ++n) {
-      const float g = c->dot(c->gate, I, H, e, n, xt), u = c->dot(c->up, I, H, e, n, xt);
-      hp[n] = g / (1.0f + std::exp(-g)) * u;
+  std::stable_sort(pairs.begin(), pairs.end(), [&](int a, int b) { return ids[a] < ids[b]; });
+  std::vector<int> seg_start;  // experts' ranges in `pairs`
+  for (size_t i = 0; i < pairs.size(); ++i)
+    if (i == 0 || ids[pairs[i]] != ids[pairs[i - 1]]) seg_start.push_back((int)i);
+  seg_start.push_back((int)pairs.size());
+  const int n_seg = (int)seg_start.size() - 1;
+  std::vector<float> h((size_t)pairs.size() * I), ypair((size_t)pairs.size() * H);
+  constexpr int RB = 32;  // rows per task
+  const int gu_blocks = (I + RB - 1) / RB, dn_blocks = (H + RB - 1) / RB;
+  // pass 1
+  parallel_for(n_seg * gu_blocks, c->threads, [&](int task) {
+    const int sg = task / gu_blocks, r0 = (task % gu_blocks) * RB, r1 = std::min(I, r0 + RB);
+    const int e = (int)ids[pairs[seg_start[sg]]];
+    std::vector<float> gw(H), uw(H);
+    for (int r = r0; r < r1; ++r) {
+      dequant_row(c, c->gate, I, H, e, r, gw.data());
+      dequant_row(c, c->up, I, H, e, r, uw.data());
+      for (int i = seg_start[sg]; i < seg_start[sg + 1]; ++i) {
+        const float* xt = xf.data() + (size_t)(pairs[i] / width) * H;
+        const float g = dot_f32(gw.data(), xt, H), u = dot_f32(uw.data(), xt, H);
+        h[(size_t)i * I + r] = g / (1.0f + std::exp(-g)) * u;
+      }
     }
   });
-  // pass 2: per token, down of each selected pair in slot order, weighted and summed
-  std::vector<int> first((size_t)T + 1, 0);
-  for (int p : pairs) first[p / width + 1]++;
-  for (int t = 0; t < T; ++t) first[t + 1] += first[t];
+  // pass 2
+  parallel_for(n_seg * dn_blocks, c->threads, [&](int task) {
+    const int sg = task / dn_blocks, r0 = (task % dn_blocks) * RB, r1 = std::min(H, r0 + RB);
+    const int e = (int)ids[pairs[seg_start[sg]]];
+    std::vector<float> dw(I);
+    for (int r = r0; r < r1; ++r) {
+      dequant_row(c, c->down, H, I, e, r, dw.data());
+      for (int i = seg_start[sg]; i < seg_start[sg + 1]; ++i)
+        ypair[(size_t)i * H + r] = w[pairs[i]] * dot_f32(dw.data(), h.data() + (size_t)i * I, I);
+    }
+  });
+  // y[t]: the token's pairs in slot order
+  std::vector<int> pos((size_t)T * width, -1);
+  for (size_t i = 0; i < pairs.size(); ++i) pos[pairs[i]] = (int)i;
   parallel_for(T, c->threads, [&](int t) {
     float* yt = y + (size_t)t * H;
     for (int n = 0; n < H; ++n) yt[n] = 0.0f;
-    for (int i = first[t]; i < first[t + 1]; ++i) {
-      const int p = pairs[i], e = (int)ids[p];
-      const float wt = w[p];
-      const float* hp = h.data() + (size_t)i * I;
-      for (int n = 0; n < H; ++n) yt[n] += wt * c->dot(c->down, H, I, e, n, hp);
+    for (int j = 0; j < width; ++j) {
+      const int i = pos[(size_t)t * width + j];
+      if (i < 0) continue;
+      const float* yp = ypair.data() + (size_t)i * H;
+      for (int n = 0; n < H; ++n) yt[n] += yp[n];
     }
   });
   return MOE_OK;
