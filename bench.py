@@ -752,10 +752,15 @@ def run_stack(args):
     gen.manual_seed(44)
     x0 = torch.randn((SEQS, H), generator=gen, device=dev).to(torch.bfloat16)
 
+    def rmsnorm(x):  # the model's pre-MoE norm (plumbing): keeps the residual stream bounded
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+
     def step(x):
         for layer, pm in zip(layers, paged):
-            ids, w = layer.route(x)
-            x = x + pm.forward(x, w, ids)
+            xn = rmsnorm(x)
+            ids, w = layer.route(xn)
+            x = x + pm.forward(xn, w, ids)
         return x
 
     x = x0
@@ -786,7 +791,8 @@ def run_stack(args):
         "data": "synthetic: seeded N(0,0.02) Q8_0 experts and routers, N(0,1) bf16 activations",
         "config": {"workload": f"BASELINE config 4 (MoE layers only, attention excluded): {L} Qwen3-30B-A3B-shaped "
                                "Q8_0 layers (E128 k8 H2048 I768), 32 of 128 experts per layer in GPU slots, the rest "
-                               "in pinned host memory; 32 sequences per decode step, residual stream x += moe(x)",
+                               "in pinned host memory; 32 sequences per decode step, residual stream "
+                               "x += moe(rmsnorm(x)) carried across steps",
                    "layers": L, "cache_slots": SLOTS, "sequences": SEQS, "cpu_threads": ncpu,
                    "miss_policy": "streamed_misses(frac 1.0, cap 32) into free LRU slots, the rest on the CPU"},
         "tokens_per_s": SEQS / (p50 / 1e3), "hit_rate": hits / max(pairs, 1), "cpu_pair_share": cpu_pairs / max(pairs, 1),
