@@ -627,7 +627,10 @@ def run_ep(args):
     gen.manual_seed(900 + rank)
     bias = (torch.randn(EP_E, generator=gen, device=dev) * 0.01).float()
     x = torch.randn((T, EP_H), generator=gen, device=dev).to(torch.bfloat16)
-    layer = M.ExpertParallelMoE(local_layer, rank, world, epr, shared=shared)
+    if world > 1 and args.ep_transport == "p2p":
+        layer = M.PeerExpertParallelMoE(local_layer, rank, world, epr, max_tokens=T, shared=shared)
+    else:
+        layer = M.ExpertParallelMoE(local_layer, rank, world, epr, shared=shared)
 
     def step(xin):
         ids, w = M.route_tokens(xin, w_router, EP_K, M.ROUTER_SIGMOID_GROUP, bias=bias, n_group=8, topk_group=4,
@@ -660,8 +663,10 @@ def run_ep(args):
         barrier()
         torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
-    send_counts, recv_counts = layer.last_counts
-    rows_out = sum(send_counts) - send_counts[rank]
+    rows_out = None
+    if getattr(layer, "last_counts", None):
+        send_counts, recv_counts = layer.last_counts
+        rows_out = sum(send_counts) - send_counts[rank]
     # end to end: this rank's activations copied in from pinned host memory and the output read back
     hx = x.cpu().pin_memory()
     hy = torch.empty_like(hx).pin_memory()
@@ -680,6 +685,8 @@ def run_ep(args):
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps)
+    if hasattr(layer, "check"):
+        layer.check()
     local_layer.check()
     shared.check()
     try:
@@ -699,6 +706,8 @@ def run_ep(args):
             "config": {"workload": "BASELINE config 5: E256 (+1 shared) top-8 sigmoid group-limited (8 groups, "
                                    "top-4), H7168 I2048 FP8; 8192 tokens per step split over the ranks",
                        "experts_per_rank": epr, "tokens_per_rank": T, "parallelism": f"ep{world}",
+                       "exchange": ("NVLink peer-memory kernels" if world > 1 and args.ep_transport == "p2p"
+                                    else "NCCL all-to-all" if world > 1 else "none (one rank)"),
                        "l2": "inputs larger than L2 (11.3 GB of FP8 experts over the ranks)"},
             "roofline": {"kernel": "whole step (route, dispatch, NCCL all-to-all, grouped GEMM, return, combine)",
                          "bound": "tensor", "achieved": round(tflops, 1), "peak": tpeak * world,
@@ -710,6 +719,8 @@ def run_ep(args):
             "gpu_launches": 17 * args.steps,
             "clocks": clk.summary(),
         }), flush=True)
+    if hasattr(layer, "close"):
+        layer.close()
     local_layer.close()
     shared.close()
     if world > 1:
@@ -819,6 +830,8 @@ def main():
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep", "stack"],
                     help="decode: BASELINE config 2 (the headline); prefill: config 3; ep: config 5; "
                          "stack: config 4")
+    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
+                    help="ep workload at N > 1: NVLink peer-memory kernels (default) or NCCL all-to-alls")
     ap.add_argument("--batches", default=None,
                     help="comma-separated batch sizes replacing the ragged sweep (profiling runs only)")
     args = ap.parse_args()

@@ -315,6 +315,44 @@ moe_status moe_forward_chunked(moe_layer* layer, const void* x, int T, const uin
 moe_status moe_select_ids(const uint32_t* ids, int64_t n, int E, const uint32_t* experts, int n_experts,
                           uint32_t* out, void* stream);
 
+/* ---- expert parallelism over NVLink peer memory (one process per GPU, >= 2 GPUs) ----------
+ * No counterpart in the reference. Replaces the NCCL all-to-alls around the per-rank layer with
+ * kernels that store rows straight into the peers' memory (CUDA IPC mappings, plain loads/stores,
+ * no multicast). Each rank creates one peer object (cap_rows = the most tokens one rank sends per
+ * call), exports its handle, gathers every rank's handle by any host channel and connects. Per call
+ * (epoch = 1, 2, ... identical on every rank), on one stream:
+ *   moe_ep_dispatch_plan (above) -> moe_ep_peer_dispatch -> moe_ep_peer_receive -> moe_forward of the
+ *   local layer on moe_ep_peer_recv_rows (world * cap_rows rows) -> moe_ep_peer_return ->
+ *   moe_ep_peer_combine.
+ * No host synchronisation: the counts travel with the rows. Waits for other ranks are bounded (about
+ * five seconds); one that runs out records MOE_ERR_TIMEOUT (moe_ep_peer_check) and its kernel reads no
+ * peer data. The local layer needs max_tokens * top_k >= world * cap_rows * top_k. */
+typedef struct moe_ep_peer moe_ep_peer;
+moe_status moe_ep_peer_create(int device, int rank, int world, int cap_rows, int hidden, int top_k, moe_ep_peer** out);
+size_t moe_ep_peer_handle_bytes(void);
+moe_status moe_ep_peer_export(moe_ep_peer* peer, void* handle);
+/* handles: world * moe_ep_peer_handle_bytes() bytes, rank r's at r * moe_ep_peer_handle_bytes(). */
+moe_status moe_ep_peer_connect(moe_ep_peer* peer, const void* handles);
+void moe_ep_peer_destroy(moe_ep_peer* peer);
+/* This rank's receive rows: [world * cap_rows, hidden] bf16, region s holding source s's rows. */
+void* moe_ep_peer_recv_rows(moe_ep_peer* peer);
+/* Source: the plan's rows (rank_counts, send_token, send_ids, send_weights of moe_ep_dispatch_plan)
+ * from x [T, hidden] bf16 into the destinations' receive regions, then this epoch's flags. */
+moe_status moe_ep_peer_dispatch(moe_ep_peer* peer, const void* x, int T, const int32_t* rank_counts,
+                                const int32_t* send_token, const uint32_t* send_ids, const float* send_weights,
+                                uint32_t epoch, void* stream);
+/* Destination: waits for every source's rows of this epoch; ids/weights [world * cap_rows, top_k]
+ * (device) receive the local slots, MOE_ID_NONE past each source's count. */
+moe_status moe_ep_peer_receive(moe_ep_peer* peer, uint32_t epoch, uint32_t* ids, float* weights, void* stream);
+/* Destination: y_local [world * cap_rows, hidden] bf16 (the local forward's output) back to the sources. */
+moe_status moe_ep_peer_return(moe_ep_peer* peer, const void* y_local, uint32_t epoch, void* stream);
+/* Source: waits for every destination's return of this epoch; y [T, hidden] = y_add (or 0) + the
+ * token's returned rows in rank order, f32, rounded once (rank_counts / token_rows of the plan). */
+moe_status moe_ep_peer_combine(moe_ep_peer* peer, uint32_t epoch, int T, const int32_t* rank_counts,
+                               const int32_t* token_rows, const void* y_add, void* y, void* stream);
+/* Synchronises `stream`, then reads and clears the peer status: MOE_OK or MOE_ERR_TIMEOUT. */
+moe_status moe_ep_peer_check(moe_ep_peer* peer, void* stream);
+
 /* Library version string. */
 const char* moe_version(void);
 

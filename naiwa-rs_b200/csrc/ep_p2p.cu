@@ -1,0 +1,450 @@
+// ep_p2p.cu — expert-parallel dispatch and return over NVLink peer memory (one process per GPU).
+//
+// No counterpart in the reference (one GPU plus CPU offload). This replaces the NCCL all-to-alls of
+// moe_b200/ep.py with kernels that store rows straight into the peers' memory:
+//
+//   every rank owns one device allocation, shared with the other ranks by CUDA IPC handles:
+//     recv_x    [W][cap][H] bf16    rows sent to me, region s written by source rank s
+//     recv_meta [W][cap][2k] int32  their (local id, weight bits) slots
+//     ret_y     [W][cap][H] bf16    my rows' outputs, region d written back by destination rank d
+//     disp_flag [W] u64             (epoch << 32 | row count) from source s, written by s
+//     ret_flag  [W] u64             (epoch << 32 | 0) from destination d, written by d
+//   and, local only: recv_count [W], two last-block counters, a status word.
+//
+//   moe_ep_peer_dispatch (source): rows of the dispatch plan (sorted by destination rank, then token)
+//     go to destination r's region [my rank] at their position within r's section, with 16-byte
+//     stores over NVLink; each block fences at system scope and counts itself done; the last block
+//     publishes every destination's flag with a system-scope release store (count 0 included).
+//   moe_ep_peer_receive (destination): one block waits, bounded, for all W flags of this epoch,
+//     records the counts and expands the regions into the local layer's inputs: ids/weights
+//     [W * cap, k] with MOE_ID_NONE for rows past a source's count (the plan skips them), so
+//     moe_forward runs on recv_x as it lies.
+//   moe_ep_peer_return (destination): each source's rows of the local output go back into that
+//     source's ret_y region [my rank]; last block publishes the return flags.
+//   moe_ep_peer_combine (source): one block waits, bounded, for all W return flags of this epoch;
+//     then y[t] = y_add[t] + sum over ranks of ret_y[r][position of (t, r)], f32, rounded once.
+//
+// Reuse is safe without resets: a source issues epoch n + 1's dispatch only after its combine of
+// epoch n, which waited for every destination's return, which each destination issued after its
+// forward had read recv_x; a destination's return of epoch n + 1 follows its receive of that epoch,
+// which follows the source's combine of epoch n. Every wait is bounded (RING-style %globaltimer
+// limit): one that runs out records MOE_ERR_TIMEOUT in the status word (moe_ep_peer_check) and the
+// kernel returns without reading the regions. No multicast: peers are reached by plain stores and
+// loads through IPC mappings only.
+#include <cstring>
+
+#include "moe_internal.cuh"
+
+namespace moe {
+
+constexpr int P2P_THREADS = 256;
+constexpr uint64_t P2P_WAIT_NS = 5ull * 1000ull * 1000ull * 1000ull;  // 5 s
+constexpr int P2P_MAX_WORLD = 64;
+
+struct PeerLayout {
+  size_t recv_x, recv_meta, ret_y, disp_flag, ret_flag, recv_count, counters, status, total;
+};
+
+static PeerLayout peer_layout(int W, int cap, int H, int k) {
+  PeerLayout l{};
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = o;
+    o += (bytes + 255) & ~(size_t)255;
+    return at;
+  };
+  l.recv_x = take((size_t)W * cap * H * 2);
+  l.recv_meta = take((size_t)W * cap * 2 * k * 4);
+  l.ret_y = take((size_t)W * cap * H * 2);
+  l.disp_flag = take((size_t)W * 8);
+  l.ret_flag = take((size_t)W * 8);
+  l.recv_count = take((size_t)W * 4);
+  l.counters = take(2 * 4);
+  l.status = take(4);
+  l.total = o;
+  return l;
+}
+
+struct PeerPtrs {
+  unsigned char* base[P2P_MAX_WORLD];  // every rank's allocation as this rank sees it (own included)
+};
+
+__device__ __forceinline__ uint64_t p2p_now() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys64(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Rank r's section of the send rows: [start[r], start[r] + counts[r]).
+__device__ __forceinline__ int rank_of_row(const int* start, int W, int row) {
+  int r = 0;
+  while (r + 1 < W && start[r + 1] <= row) ++r;
+  return r;
+}
+
+// Source: rows -> peers' recv regions; last block publishes the flags.
+__global__ void __launch_bounds__(P2P_THREADS) peer_dispatch_kernel(PeerPtrs peers, PeerLayout L, int me, int W, int cap,
+                                                                    int H, int k, uint32_t epoch,
+                                                                    const uint4* __restrict__ x,
+                                                                    const int32_t* __restrict__ rank_counts,
+                                                                    const int32_t* __restrict__ send_token,
+                                                                    const uint32_t* __restrict__ send_ids,
+                                                                    const float* __restrict__ send_w) {
+  __shared__ int start[P2P_MAX_WORLD + 1];
+  __shared__ int s_last;
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int r = 0; r < W; ++r) {
+      start[r] = run;
+      run += rank_counts[r];
+    }
+    start[W] = run;
+  }
+  __syncthreads();
+  const int n = start[W];
+  const int H16 = H / 8, lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (P2P_THREADS / 32);
+  for (int row = blockIdx.x * (P2P_THREADS / 32) + (threadIdx.x >> 5); row < n; row += warps) {
+    const int r = rank_of_row(start, W, row), pos = row - start[r];
+    if (pos >= cap) continue;  // cannot happen: a source sends each token at most once per rank
+    unsigned char* dst = peers.base[r];
+    uint4* dx = reinterpret_cast<uint4*>(dst + L.recv_x) + ((size_t)me * cap + pos) * H16;
+    const uint4* sx = x + (size_t)send_token[row] * H16;
+    for (int c = lane; c < H16; c += 32) dx[c] = ldg_nc(sx + c);
+    int32_t* dm = reinterpret_cast<int32_t*>(dst + L.recv_meta) + ((size_t)me * cap + pos) * 2 * k;
+    for (int j = lane; j < k; j += 32) {
+      dm[j] = (int32_t)send_ids[(size_t)row * k + j];
+      dm[k + j] = __float_as_int(send_w[(size_t)row * k + j]);
+    }
+  }
+  __threadfence_system();  // this block's peer stores are visible before it counts itself done
+  __syncthreads();
+  uint32_t* done = reinterpret_cast<uint32_t*>(peers.base[me] + L.counters);
+  if (threadIdx.x == 0) s_last = atomicAdd(&done[0], 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (s_last) {
+    __threadfence_system();
+    for (int r = threadIdx.x; r < W; r += P2P_THREADS) {
+      uint64_t* f = reinterpret_cast<uint64_t*>(peers.base[r] + L.disp_flag) + me;
+      st_release_sys64(f, ((uint64_t)epoch << 32) | (uint32_t)(start[r + 1] - start[r]));
+    }
+    if (threadIdx.x == 0) done[0] = 0;  // every block has counted: ready for the next epoch
+  }
+}
+
+// Waits (thread 0, bounded) until flags[0..W) all carry `epoch`; false after the time limit.
+__device__ bool wait_flags(const uint64_t* flags, int W, uint32_t epoch, int32_t* status) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    const uint64_t t0 = p2p_now();
+    int ok = 0;
+    for (;;) {
+      int all = 1;
+      for (int r = 0; r < W && all; ++r) all = (uint32_t)(ld_acquire_sys64(flags + r) >> 32) == epoch;
+      if (all) {
+        ok = 1;
+        break;
+      }
+      if (p2p_now() - t0 > P2P_WAIT_NS) break;
+      __nanosleep(128);
+    }
+    if (!ok) atomicExch(status, (int32_t)MOE_ERR_TIMEOUT);
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+// Destination: wait for every source of this epoch, then ids/weights for the local forward.
+__global__ void __launch_bounds__(P2P_THREADS) peer_receive_kernel(PeerPtrs peers, PeerLayout L, int me, int W, int cap,
+                                                                   int k, uint32_t epoch, uint32_t* __restrict__ ids,
+                                                                   float* __restrict__ w) {
+  unsigned char* mine = peers.base[me];
+  const uint64_t* flags = reinterpret_cast<const uint64_t*>(mine + L.disp_flag);
+  int32_t* counts = reinterpret_cast<int32_t*>(mine + L.recv_count);
+  int32_t* status = reinterpret_cast<int32_t*>(mine + L.status);
+  __shared__ int cnt[P2P_MAX_WORLD];
+  if (!wait_flags(flags, W, epoch, status)) {
+    // sources that did not arrive: run nothing (all slots empty), so the forward reads no region
+    for (size_t i = threadIdx.x; i < (size_t)W * cap * k; i += P2P_THREADS) ids[i] = MOE_ID_NONE;
+    for (int r = threadIdx.x; r < W; r += P2P_THREADS) counts[r] = 0;
+    return;
+  }
+  for (int r = threadIdx.x; r < W; r += P2P_THREADS) {
+    cnt[r] = (int)(uint32_t)(ld_acquire_sys64(flags + r) & 0xffffffffu);
+    counts[r] = cnt[r];
+  }
+  __syncthreads();
+  const int32_t* meta = reinterpret_cast<const int32_t*>(mine + L.recv_meta);
+  for (size_t i = threadIdx.x; i < (size_t)W * cap * k; i += P2P_THREADS) {
+    const size_t row = i / k;
+    const int j = (int)(i % k), s = (int)(row / cap), pos = (int)(row % cap);
+    if (pos < cnt[s]) {  // peer-written: L2-coherent loads, no stale L1 line from an earlier epoch
+      ids[i] = (uint32_t)__ldcg(meta + row * 2 * k + j);
+      w[i] = __int_as_float(__ldcg(meta + row * 2 * k + k + j));
+    } else {
+      ids[i] = MOE_ID_NONE;
+      w[i] = 0.0f;
+    }
+  }
+}
+
+// Destination: each source's output rows back into its ret_y region; last block publishes.
+__global__ void __launch_bounds__(P2P_THREADS) peer_return_kernel(PeerPtrs peers, PeerLayout L, int me, int W, int cap,
+                                                                  int H, uint32_t epoch, const uint4* __restrict__ y) {
+  __shared__ int s_last;
+  unsigned char* mine = peers.base[me];
+  const int32_t* counts = reinterpret_cast<const int32_t*>(mine + L.recv_count);
+  const int H16 = H / 8, lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (P2P_THREADS / 32);
+  for (int row = blockIdx.x * (P2P_THREADS / 32) + (threadIdx.x >> 5); row < W * cap; row += warps) {
+    const int s = row / cap, pos = row % cap;
+    if (pos >= counts[s]) continue;
+    uint4* d = reinterpret_cast<uint4*>(peers.base[s] + L.ret_y) + ((size_t)me * cap + pos) * H16;
+    const uint4* src = y + (size_t)row * H16;
+    for (int c = lane; c < H16; c += 32) d[c] = ldg_nc(src + c);
+  }
+  __threadfence_system();
+  __syncthreads();
+  uint32_t* done = reinterpret_cast<uint32_t*>(mine + L.counters) + 1;
+  if (threadIdx.x == 0) s_last = atomicAdd(done, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (s_last) {
+    __threadfence_system();
+    for (int s = threadIdx.x; s < W; s += P2P_THREADS) {
+      uint64_t* f = reinterpret_cast<uint64_t*>(peers.base[s] + L.ret_flag) + me;
+      st_release_sys64(f, (uint64_t)epoch << 32);
+    }
+    if (threadIdx.x == 0) *done = 0;
+  }
+}
+
+// Source: wait for every destination's return of this epoch (one block), then the combine.
+__global__ void __launch_bounds__(P2P_THREADS) peer_wait_return_kernel(PeerPtrs peers, PeerLayout L, int me, int W,
+                                                                       uint32_t epoch) {
+  unsigned char* mine = peers.base[me];
+  (void)wait_flags(reinterpret_cast<const uint64_t*>(mine + L.ret_flag), W, epoch,
+                   reinterpret_cast<int32_t*>(mine + L.status));
+}
+
+// y[t] = y_add[t] + sum_r ret_y[r][token_rows[t, r] - start[r]] (rows < 0 skipped); one warp per token.
+__global__ void peer_combine_kernel(PeerPtrs peers, PeerLayout L, int me, int W, int cap, int T, int H,
+                                    const int32_t* __restrict__ rank_counts, const int32_t* __restrict__ token_rows,
+                                    const uint4* __restrict__ y_add, uint4* __restrict__ y) {
+  __shared__ int start[P2P_MAX_WORLD];
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int r = 0; r < W; ++r) {
+      start[r] = run;
+      run += rank_counts[r];
+    }
+  }
+  __syncthreads();
+  const int32_t* status = reinterpret_cast<const int32_t*>(peers.base[me] + L.status);
+  const bool failed = *reinterpret_cast<const volatile int32_t*>(status) != 0;
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const int H8 = H / 8;
+  const uint4* ret = reinterpret_cast<const uint4*>(peers.base[me] + L.ret_y);
+  for (int c = lane; c < H8; c += 32) {
+    float acc[8];
+    if (y_add) {
+      const uint4 v = ldg_nc(y_add + (size_t)t * H8 + c);
+      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(b[i]);
+        acc[2 * i] = f.x;
+        acc[2 * i + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+    }
+    for (int r = 0; r < W && !failed; ++r) {
+      const int row = token_rows[(size_t)t * W + r];
+      if (row < 0) continue;
+      const uint4 v = __ldcg(ret + ((size_t)r * cap + (row - start[r])) * H8 + c);  // peer-written
+      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(b[i]);
+        acc[2 * i] += f.x;
+        acc[2 * i + 1] += f.y;
+      }
+    }
+    y[(size_t)t * H8 + c] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                                       pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+  }
+}
+
+}  // namespace moe
+
+using namespace moe;
+
+struct moe_ep_peer {
+  int dev = 0, rank = 0, world = 0, cap = 0, H = 0, k = 0;
+  PeerLayout L{};
+  unsigned char* local = nullptr;
+  PeerPtrs peers{};
+  bool opened[P2P_MAX_WORLD] = {};
+  int grid = 0;
+};
+
+extern "C" {
+
+moe_status moe_ep_peer_create(int device, int rank, int world, int cap_rows, int hidden, int top_k, moe_ep_peer** out) {
+  if (!out) return fail(MOE_ERR_INVALID, "moe_ep_peer_create: null out");
+  *out = nullptr;
+  if (world < 2 || world > P2P_MAX_WORLD || rank < 0 || rank >= world || cap_rows <= 0 || hidden <= 0 ||
+      hidden % 8 || top_k <= 0)
+    return fail(MOE_ERR_INVALID, "moe_ep_peer_create: need 2 <= world <= 64, 0 <= rank < world, H % 8 == 0");
+  DeviceGuard guard(device);
+  if (!guard.ok) return fail(MOE_ERR_CUDA, "moe_ep_peer_create: cannot select device");
+  moe_ep_peer* p = new moe_ep_peer();
+  p->dev = device;
+  p->rank = rank;
+  p->world = world;
+  p->cap = cap_rows;
+  p->H = hidden;
+  p->k = top_k;
+  p->L = peer_layout(world, cap_rows, hidden, top_k);
+  void* base = nullptr;
+  cudaError_t e = cudaMalloc(&base, p->L.total);
+  if (e != cudaSuccess) {
+    delete p;
+    return cuda_fail(e, "cudaMalloc(ep peer buffers)");
+  }
+  e = cudaMemset(base, 0, p->L.total);  // flags start at epoch 0, counters at 0
+  if (e != cudaSuccess) {
+    cudaFree(base);
+    delete p;
+    return cuda_fail(e, "cudaMemset(ep peer buffers)");
+  }
+  p->local = static_cast<unsigned char*>(base);
+  p->peers.base[rank] = p->local;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  p->grid = sms;
+  *out = p;
+  return MOE_OK;
+}
+
+size_t moe_ep_peer_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+moe_status moe_ep_peer_export(moe_ep_peer* p, void* handle) {
+  if (!p || !handle) return fail(MOE_ERR_INVALID, "moe_ep_peer_export: null argument");
+  DeviceGuard guard(p->dev);
+  cudaIpcMemHandle_t h;
+  MOE_CUDA_TRY(cudaIpcGetMemHandle(&h, p->local));
+  std::memcpy(handle, &h, sizeof(h));
+  return MOE_OK;
+}
+
+moe_status moe_ep_peer_connect(moe_ep_peer* p, const void* handles) {
+  if (!p || !handles) return fail(MOE_ERR_INVALID, "moe_ep_peer_connect: null argument");
+  DeviceGuard guard(p->dev);
+  for (int r = 0; r < p->world; ++r) {
+    if (r == p->rank || p->opened[r]) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const unsigned char*>(handles) + (size_t)r * sizeof(h), sizeof(h));
+    void* ptr = nullptr;
+    MOE_CUDA_TRY(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    p->peers.base[r] = static_cast<unsigned char*>(ptr);
+    p->opened[r] = true;
+  }
+  return MOE_OK;
+}
+
+void moe_ep_peer_destroy(moe_ep_peer* p) {
+  if (!p) return;
+  DeviceGuard guard(p->dev);
+  cudaDeviceSynchronize();
+  for (int r = 0; r < p->world; ++r)
+    if (p->opened[r]) cudaIpcCloseMemHandle(p->peers.base[r]);
+  cudaFree(p->local);
+  delete p;
+}
+
+void* moe_ep_peer_recv_rows(moe_ep_peer* p) { return p ? p->local + p->L.recv_x : nullptr; }
+
+static moe_status peer_ready(moe_ep_peer* p, const char* who) {
+  if (!p) return fail(MOE_ERR_INVALID, std::string(who) + ": null peer");
+  for (int r = 0; r < p->world; ++r)
+    if (!p->peers.base[r]) return fail(MOE_ERR_INVALID, std::string(who) + ": call moe_ep_peer_connect first");
+  return MOE_OK;
+}
+
+moe_status moe_ep_peer_dispatch(moe_ep_peer* p, const void* x, int T, const int32_t* rank_counts,
+                                const int32_t* send_token, const uint32_t* send_ids, const float* send_w,
+                                uint32_t epoch, void* stream) {
+  MOE_TRY(peer_ready(p, "moe_ep_peer_dispatch"));
+  if (T > p->cap) return fail(MOE_ERR_INVALID, "moe_ep_peer_dispatch: T exceeds cap_rows");
+  if (epoch == 0) return fail(MOE_ERR_INVALID, "moe_ep_peer_dispatch: epochs start at 1");
+  DeviceGuard guard(p->dev);
+  peer_dispatch_kernel<<<p->grid, P2P_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      p->peers, p->L, p->rank, p->world, p->cap, p->H, p->k, epoch, static_cast<const uint4*>(x), rank_counts,
+      send_token, send_ids, send_w);
+  MOE_CUDA_TRY(cudaGetLastError());
+  return MOE_OK;
+}
+
+moe_status moe_ep_peer_receive(moe_ep_peer* p, uint32_t epoch, uint32_t* ids, float* weights, void* stream) {
+  MOE_TRY(peer_ready(p, "moe_ep_peer_receive"));
+  if (!ids || !weights) return fail(MOE_ERR_INVALID, "moe_ep_peer_receive: null output");
+  DeviceGuard guard(p->dev);
+  peer_receive_kernel<<<1, P2P_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(p->peers, p->L, p->rank, p->world,
+                                                                               p->cap, p->k, epoch, ids, weights);
+  MOE_CUDA_TRY(cudaGetLastError());
+  return MOE_OK;
+}
+
+moe_status moe_ep_peer_return(moe_ep_peer* p, const void* y_local, uint32_t epoch, void* stream) {
+  MOE_TRY(peer_ready(p, "moe_ep_peer_return"));
+  if (!y_local) return fail(MOE_ERR_INVALID, "moe_ep_peer_return: null rows");
+  DeviceGuard guard(p->dev);
+  peer_return_kernel<<<p->grid, P2P_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      p->peers, p->L, p->rank, p->world, p->cap, p->H, epoch, static_cast<const uint4*>(y_local));
+  MOE_CUDA_TRY(cudaGetLastError());
+  return MOE_OK;
+}
+
+moe_status moe_ep_peer_combine(moe_ep_peer* p, uint32_t epoch, int T, const int32_t* rank_counts,
+                               const int32_t* token_rows, const void* y_add, void* y, void* stream) {
+  MOE_TRY(peer_ready(p, "moe_ep_peer_combine"));
+  if (T < 0 || !rank_counts || (T && (!token_rows || !y))) return fail(MOE_ERR_INVALID, "moe_ep_peer_combine: bad arguments");
+  DeviceGuard guard(p->dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  peer_wait_return_kernel<<<1, 32, 0, st>>>(p->peers, p->L, p->rank, p->world, epoch);
+  MOE_CUDA_TRY(cudaGetLastError());
+  if (T == 0) return MOE_OK;
+  const int threads = 256;
+  peer_combine_kernel<<<(unsigned)(((int64_t)T * 32 + threads - 1) / threads), threads, 0, st>>>(
+      p->peers, p->L, p->rank, p->world, p->cap, T, p->H, rank_counts, token_rows, static_cast<const uint4*>(y_add),
+      static_cast<uint4*>(y));
+  MOE_CUDA_TRY(cudaGetLastError());
+  return MOE_OK;
+}
+
+moe_status moe_ep_peer_check(moe_ep_peer* p, void* stream) {
+  if (!p) return fail(MOE_ERR_INVALID, "moe_ep_peer_check: null peer");
+  DeviceGuard guard(p->dev);
+  MOE_CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  int32_t st = 0;
+  MOE_CUDA_TRY(cudaMemcpy(&st, p->local + p->L.status, 4, cudaMemcpyDeviceToHost));
+  if (st != 0) {
+    MOE_CUDA_TRY(cudaMemset(p->local + p->L.status, 0, 4));
+    return fail((moe_status)st, "moe_ep_peer: a wait for another rank ran out (a peer stopped or fell behind)");
+  }
+  return MOE_OK;
+}
+
+}  // extern "C"

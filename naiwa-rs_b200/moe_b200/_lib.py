@@ -111,6 +111,17 @@ def lib():
             "moe_add_f32_into_bf16": (i, [P, P, ctypes.c_int64, P]),
             "moe_select_ids": (i, [P, ctypes.c_int64, i, P, i, P, P]),
             "moe_forward_chunked": (i, [P, P, i, P, P, i, P, P]),
+            "moe_ep_peer_create": (i, [i, i, i, i, i, i, ctypes.POINTER(ctypes.c_void_p)]),
+            "moe_ep_peer_handle_bytes": (ctypes.c_size_t, []),
+            "moe_ep_peer_export": (i, [P, P]),
+            "moe_ep_peer_connect": (i, [P, P]),
+            "moe_ep_peer_destroy": (None, [P]),
+            "moe_ep_peer_recv_rows": (P, [P]),
+            "moe_ep_peer_dispatch": (i, [P, P, i, P, P, P, P, ctypes.c_uint32, P]),
+            "moe_ep_peer_receive": (i, [P, ctypes.c_uint32, P, P, P]),
+            "moe_ep_peer_return": (i, [P, P, ctypes.c_uint32, P]),
+            "moe_ep_peer_combine": (i, [P, ctypes.c_uint32, i, P, P, P, P, P]),
+            "moe_ep_peer_check": (i, [P, P]),
             "moe_ring_create": (i, [i, i, ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
             "moe_ring_destroy": (None, [P]),
             "moe_ring_slot_bytes": (ctypes.c_size_t, [P]),

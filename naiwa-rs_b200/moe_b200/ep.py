@@ -163,3 +163,78 @@ class ExpertParallelMoE:
                           plan["token_rows"], T, y_add=y_shared, stream=stream)
 
     __call__ = forward
+
+
+class PeerExpertParallelMoE:
+    """ExpertParallelMoE with the exchange done by the library's NVLink peer-memory kernels instead of
+    NCCL all-to-alls: dispatch rows are stored straight into the destination ranks' receive regions,
+    outputs straight back into the sources' return regions, with epoch flags and bounded waits in
+    between and no host synchronisation (so a step can be captured in a CUDA graph). Needs one process
+    per GPU and world >= 2; the handles are exchanged once through torch.distributed.
+
+    `local` must be built with max_tokens >= world * max_tokens (the rows it may receive)."""
+
+    def __init__(self, local, rank: int, world: int, experts_per_rank: int, max_tokens: int, group=None,
+                 shared=None):
+        torch = _torch()
+        import torch.distributed as dist
+
+        self.local, self.rank, self.world, self.epr = local, rank, world, experts_per_rank
+        self.cap, self.group, self.shared = int(max_tokens), group, shared
+        self.H, self.k = local.hidden, local.top_k
+        h = ctypes.c_void_p()
+        check(lib().moe_ep_peer_create(local.device, rank, world, self.cap, self.H, self.k, ctypes.byref(h)))
+        self._h = h
+        nb = int(lib().moe_ep_peer_handle_bytes())
+        mine = (ctypes.c_ubyte * nb)()
+        check(lib().moe_ep_peer_export(self._h, ctypes.cast(mine, ctypes.c_void_p)))
+        gathered = [None] * world
+        dist.all_gather_object(gathered, bytes(mine), group=group)
+        allh = (ctypes.c_ubyte * (nb * world)).from_buffer_copy(b"".join(gathered))
+        check(lib().moe_ep_peer_connect(self._h, ctypes.cast(allh, ctypes.c_void_p)))
+        dist.barrier(group=group)
+        dev = torch.device("cuda", local.device)
+        R = world * self.cap
+        self.recv_ids = torch.empty((R, self.k), dtype=torch.int32, device=dev)
+        self.recv_w = torch.empty((R, self.k), dtype=torch.float32, device=dev)
+        self.y_local = torch.empty((R, self.H), dtype=torch.bfloat16, device=dev)
+        self.recv_rows = lib().moe_ep_peer_recv_rows(self._h)
+        self.epoch = 0
+
+    def forward(self, xs, topk_weights, topk_ids, stream=None):
+        torch = _torch()
+        T, H = xs.shape
+        if T > self.cap:
+            raise ValueError("PeerExpertParallelMoE.forward: T exceeds max_tokens")
+        self.epoch += 1
+        e = self.epoch
+        st = ctypes.c_void_p(_stream(stream))
+        xs = xs.contiguous()
+        plan = ep_dispatch(topk_ids, topk_weights, self.epr, self.world, stream=stream)
+        check(lib().moe_ep_peer_dispatch(self._h, _ptr(xs), T, _ptr(plan["rank_counts"]), _ptr(plan["send_token"]),
+                                         _ptr(plan["send_ids"]), _ptr(plan["send_w"]), e, st))
+        y_shared = None
+        if self.shared is not None:
+            ones = torch.ones((T, 1), dtype=torch.float32, device=xs.device)
+            zeros = torch.zeros((T, 1), dtype=torch.int32, device=xs.device)
+            y_shared = self.shared.forward(xs, ones, zeros, stream=stream)
+        check(lib().moe_ep_peer_receive(self._h, e, _ptr(self.recv_ids), _ptr(self.recv_w), st))
+        R = self.world * self.cap
+        check(lib().moe_forward(self.local._h, ctypes.c_void_p(self.recv_rows), R, _ptr(self.recv_ids),
+                                _ptr(self.recv_w), self.k, _ptr(self.y_local), st))
+        check(lib().moe_ep_peer_return(self._h, _ptr(self.y_local), e, st))
+        y = torch.empty((T, H), dtype=torch.bfloat16, device=xs.device)
+        check(lib().moe_ep_peer_combine(self._h, e, T, _ptr(plan["rank_counts"]), _ptr(plan["token_rows"]),
+                                        _ptr(y_shared), _ptr(y), st))
+        return y
+
+    __call__ = forward
+
+    def check(self, stream=None):
+        check(lib().moe_ep_peer_check(self._h, ctypes.c_void_p(_stream(stream))))
+        self.local.check()
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            lib().moe_ep_peer_destroy(self._h)
+            self._h = ctypes.c_void_p()
