@@ -448,7 +448,7 @@ def run_prefill(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    L, chunk, prompt = args.layers, 512, 4096
+    L, chunk, prompt = args.layers, args.chunk, 4096
     cfg = M.MoeConfig(num_experts=E, num_experts_per_tok=K_TOP, hidden_size=H, moe_intermediate_size=I)
     prov = M.RoutedExpertsProvider()
     layers = []
@@ -558,12 +558,12 @@ def run_prefill(args):
     for layer in layers:
         layer.check()
     print(json.dumps({
-        "metric": "MoE-layer tokens/s per B200 (prefill, Qwen3-30B-A3B-shaped Q4_K layer, 512-token chunks)",
+        "metric": f"MoE-layer tokens/s per B200 (prefill, Qwen3-30B-A3B-shaped Q4_K layer, {chunk}-token chunks)",
         "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "q4_k weights dequantised to f16 in tensor memory, tcgen05 f16 MMA, f32 accumulate",
         "data": "synthetic: seeded N(0,0.02) Q4_K experts, N(0,1) bf16 activations, Zipf(1.1) routing",
-        "config": {"workload": "BASELINE config 3: 4096-token prompt in 512-token chunks through "
+        "config": {"workload": f"BASELINE config 3: 4096-token prompt in {chunk}-token chunks through "
                                f"{L} distinct Q4_K layers (E128 k8 H2048 I768); routing ids drawn Zipf(1.1)",
                    "layers": L, "tokens_per_step": tokens,
                    "l2": "inputs larger than L2 (340 MB of Q4_K experts per layer)"},
@@ -830,6 +830,8 @@ def main():
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep", "stack"],
                     help="decode: BASELINE config 2 (the headline); prefill: config 3; ep: config 5; "
                          "stack: config 4")
+    ap.add_argument("--chunk", type=int, default=512,
+                    help="prefill workload: tokens per grouped pass (4096 = the whole prompt in one pass)")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="ep workload at N > 1: NVLink peer-memory kernels (default) or NCCL all-to-alls")
     ap.add_argument("--batches", default=None,

@@ -360,6 +360,79 @@ __device__ __forceinline__ Item decode_item(const GemmParams& p, int w) {
   return it;
 }
 
+// Epilogue of one work item for the calling warp: tensor-memory lanes 32 quad .. +31 (weight rows)
+// and the 16-column blocks cb0 <= cb < cb1 of accumulator columns (tokens). Gate/up: lanes 0..15
+// hold gate rows, 16..31 the matching up rows -> h = silu(g) * u. Down: ypair = w * (W h).
+__device__ __forceinline__ void epilogue_blocks(const GemmParams& p, const Item& it, uint32_t tbase, int quad, int lane,
+                                                int cb0, int cb1) {
+  // per-column scale (and, for the down projection, destination pair) of columns lane + 32 t
+  float csc[4];
+  int cpr[4];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const int n = lane + 32 * t;
+    csc[t] = 0.0f;
+    cpr[t] = 0;
+    if (n < it.nval) {
+      const int idx = it.base + it.n0 + n;
+      csc[t] = __ldg(p.tscale + idx);
+      if (p.phase == 1) {
+        cpr[t] = __ldg(p.perm + idx);
+        csc[t] *= __ldg(p.route_w + cpr[t]);
+      }
+    }
+  }
+#pragma unroll
+  for (int cb = 0; cb < BN / 16; ++cb) {  // compile-time block index: csc / cpr stay in registers
+    const int c0 = cb * 16;
+    if (cb < cb0 || cb >= cb1 || c0 >= it.nmma) continue;
+    float v[16];
+    tmem_ld16(tbase + (uint32_t)c0, v);
+    if (p.phase == 0) {
+      const int col = it.tile * 64 + quad * 16 + lane;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int n = c0 + i;
+        const float sc = __shfl_sync(FULL, csc[n >> 5], n & 31);
+        const float up = __shfl_down_sync(FULL, v[i], 16);
+        if (lane < 16 && n < it.nval) {
+          const float g = v[i] * sc, uu = up * sc;
+          p.out[(int64_t)(it.base + it.n0 + n) * (p.N_rows >> 1) + col] = __fdividef(g, 1.0f + __expf(-g)) * uu;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int n = c0 + i;
+        const float sc = __shfl_sync(FULL, csc[n >> 5], n & 31);
+        const int pr = __shfl_sync(FULL, cpr[n >> 5], n & 31);
+        if (n < it.nval) p.out[(int64_t)pr * p.N_rows + it.tile * BM + quad * 32 + lane] = v[i] * sc;
+      }
+    }
+  }
+}
+
+// With one accumulator (NACC == 1) the next item's MMAs wait for this item's epilogue. The gate/up
+// epilogue (SiLU, 16-lane stores) is long enough that the dequant warps take part: warps sharing a
+// lane quarter split the 8 column blocks (dequant warps w / 4 = 0, 1 take [0, 3) and [3, 6), the
+// epilogue warp [6, 8)). The down epilogue is short; there the epilogue warps alone do it and the
+// dequant warps run ahead into the next item.
+template <class C>
+__device__ __forceinline__ bool dequant_joins_epilogue(const GemmParams& p) {
+  return C::NACC == 1 && p.phase == 0;
+}
+
+template <class C>
+__device__ __forceinline__ void epilogue_range(const GemmParams& p, int part, int* cb0, int* cb1) {
+  if (!dequant_joins_epilogue<C>(p)) {
+    *cb0 = 0;
+    *cb1 = BN / 16;
+  } else {
+    *cb0 = part * 3;
+    *cb1 = part == 2 ? BN / 16 : part * 3 + 3;
+  }
+}
+
 template <class W, class C>
 __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
     expert_gemm_kernel(GemmParams p, const __grid_constant__ CUtensorMap tmap) {
@@ -402,7 +475,7 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
     }
     for (int s = 0; s < C::NACC; ++s) {
       mbar_init(&acc_full[s], 1);
-      mbar_init(&acc_free[s], EPI_WARPS);
+      mbar_init(&acc_free[s], EPI_WARPS + (dequant_joins_epilogue<C>(p) ? C::DQW : 0));
     }
     mbar_init(mma_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -508,59 +581,15 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
     for (int w = blockIdx.x; w < n_items; w += G, ++j) {
       const Item it = decode_item(p, w);
       const int acc = j % C::NACC;
-      // per-column scale (and, for the down projection, destination pair), columns lane + 32 t
-      float csc[4];
-      int cpr[4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int n = lane + 32 * t;
-        csc[t] = 0.0f;
-        cpr[t] = 0;
-        if (n < it.nval) {
-          const int idx = it.base + it.n0 + n;
-          csc[t] = __ldg(p.tscale + idx);
-          if (p.phase == 1) {
-            cpr[t] = __ldg(p.perm + idx);
-            csc[t] *= __ldg(p.route_w + cpr[t]);
-          }
-        }
-      }
       const bool ok = __all_sync(FULL, mbar_wait(&acc_full[acc], (j / C::NACC) & 1, abort));
       if (!ok) {
         if (lane == 0) s_abort = 1;
         break;
       }
       tc_fence_after();
-      const uint32_t tbase = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll
-      for (int cb = 0; cb < BN / 16; ++cb) {
-        const int c0 = cb * 16;
-        if (c0 >= it.nmma) break;
-        float v[16];
-        tmem_ld16(tbase + (uint32_t)c0, v);
-        if (p.phase == 0) {
-          // lanes 0..15: gate rows, lanes 16..31: the matching up rows
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int n = c0 + i;
-            const float sc = __shfl_sync(FULL, csc[n >> 5], n & 31);
-            const float up = __shfl_down_sync(FULL, v[i], 16);
-            if (lane < 16 && n < it.nval) {
-              const float g = v[i] * sc, uu = up * sc;
-              const int col = it.tile * 64 + quad * 16 + lane;
-              p.out[(int64_t)(it.base + it.n0 + n) * (p.N_rows >> 1) + col] = g / (1.0f + __expf(-g)) * uu;
-            }
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int n = c0 + i;
-            const float sc = __shfl_sync(FULL, csc[n >> 5], n & 31);
-            const int pr = __shfl_sync(FULL, cpr[n >> 5], n & 31);
-            if (n < it.nval) p.out[(int64_t)pr * p.N_rows + it.tile * BM + quad * 32 + lane] = v[i] * sc;
-          }
-        }
-      }
+      int cb0, cb1;
+      epilogue_range<C>(p, 2, &cb0, &cb1);
+      epilogue_blocks(p, it, tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN), quad, lane, cb0, cb1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_free[acc]);
@@ -571,7 +600,7 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
     // QPW 32-column quarters QPW (w / 4) .. of each chunk
     const int drow = threadIdx.x & (BM - 1), dq0 = (warp >> 2) * C::QPW;
     const uint32_t lane_base = tmem + ((uint32_t)(drow & ~31) << 16) + (uint32_t)C::A_COL0;
-    int q = 0, g = 0;
+    int q = 0, g = 0, j_item = 0;
     bool stop = false;
     for (int w = blockIdx.x; w < n_items && !stop; w += G) {
       const Item it = decode_item(p, w);
@@ -610,6 +639,19 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
         if (lane == 0) mbar_arrive(&a_full[sa]);
       }
       g += units;
+      if (dequant_joins_epilogue<C>(p) && !stop) {  // this item's share of the epilogue
+        const bool ok_acc = mbar_wait(&acc_full[0], (j_item & 1), abort);
+        stop = __any_sync(FULL, !ok_acc);
+        if (stop) break;
+        tc_fence_after();
+        int cb0, cb1;
+        epilogue_range<C>(p, warp >> 2, &cb0, &cb1);
+        epilogue_blocks(p, it, tmem + ((uint32_t)(drow & ~31) << 16), warp & 3, lane, cb0, cb1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_free[0]);
+      }
+      ++j_item;
     }
     if (stop && lane == 0) s_abort = 1;
   }
