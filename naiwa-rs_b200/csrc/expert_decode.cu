@@ -29,8 +29,11 @@ constexpr int MAX_TPP = 32;  // tokens per pass (4 n-tiles of 8)
 // ---- weight fragment streams ---------------------------------------------------------------------
 
 // Q8_0: per (tile, block) 512 B of quants; per (tile, group of 4 blocks) 128 B of scales holding
-// {d(row g), d(row g+8)} for the 4 blocks at byte g*16.
-struct WQ8 {
+// {d(row g), d(row g+8)} for the 4 blocks at byte g*16. UNITS: the same fragments grouped in 17 KB
+// units per (128-row tile, 128-column chunk), lane l's slot swizzled (repack.cu), scales inside the
+// unit; a pipeline stage (4 blocks) is then one unit of the warp's 16-row tile.
+template <bool UNITS>
+struct WQ8Stream {
   static constexpr bool kF16 = true;
   static constexpr int GROUP = 4;  // blocks per pipeline stage
   struct Stage {
@@ -39,15 +42,23 @@ struct WQ8 {
   };
   __device__ static __forceinline__ void load(const ExpertParams& p, int e, int tile, int kb0, int kb_end, int lane,
                                               Stage& st) {
-    const uint8_t* qb = p.wq + (int64_t)e * p.q_stride + ((int64_t)tile * p.kb_count + kb0) * 512 + lane * 16;
+    const uint8_t* qb;
+    const uint8_t* sb;
+    if (UNITS) {  // kb0 % 4 == 0: blocks kb0 .. kb0 + 3 are the unit's four blocks
+      const int g = lane >> 2, c = lane & 3;
+      const uint8_t* unit =
+          p.wq + (int64_t)e * p.q_stride + ((int64_t)(tile >> 3) * (p.kb_count >> 2) + (kb0 >> 2)) * Q8_UNIT_BYTES;
+      qb = unit + (tile & 7) * 4 * 512 + ((4 * g + (c ^ ((g >> 1) & 3))) << 4);
+      sb = unit + 8 * 4 * 512 + (tile & 7) * 128 + g * 16;
+    } else {
+      qb = p.wq + (int64_t)e * p.q_stride + ((int64_t)tile * p.kb_count + kb0) * 512 + lane * 16;
+      const int kbg_count = (p.kb_count + 3) >> 2;
+      sb = p.wsc + (int64_t)e * p.s_stride + ((int64_t)tile * kbg_count + (kb0 >> 2)) * 128 + (lane >> 2) * 16;
+    }
 #pragma unroll
     for (int u = 0; u < GROUP; ++u)
       if (kb0 + u < kb_end) st.q[u] = ldg_stream(qb + u * 512);
-    if (kb0 < kb_end) {
-      const int kbg_count = (p.kb_count + 3) >> 2;
-      st.s = ldg_stream(p.wsc + (int64_t)e * p.s_stride + ((int64_t)tile * kbg_count + (kb0 >> 2)) * 128 +
-                        (lane >> 2) * 16);
-    }
+    if (kb0 < kb_end) st.s = ldg_stream(sb);
   }
   // exact int8 -> f16 of the lane's 16 quant bytes: a0 (k16 step 0), a1 (step 1). The device layout
   // stores u = q + 128 (the repack flips the sign bit), so 0x64 in the high byte makes 1024 + u.
@@ -96,6 +107,9 @@ struct WQ8 {
 };
 
 // BF16: per (tile, block) 1 KB = two k16 steps of 512 B; lane's 16 B = its 8 A values.
+using WQ8 = WQ8Stream<false>;
+using WQ8U = WQ8Stream<true>;
+
 struct WBF16 {
   static constexpr bool kF16 = false;
   static constexpr int GROUP = 2;
@@ -414,6 +428,10 @@ moe_status launch_expert_gemv(int wdtype, ExpertParams p, int max_active, int ro
   const int grid = max_active * p.units_per_expert;
   if (grid <= 0) return MOE_OK;
   const size_t smem = expert_smem_bytes(p.K, p.tpp, rowt, rowt == 16 ? 16 : 8);
+  if (wdtype == MOE_DTYPE_Q8_0 && p.tile_major) {
+    if (p.K % 128 || p.N % 128) return fail(MOE_ERR_INVALID, "decode expert kernel: Q8_0 units need 128-multiples");
+    return launch1<WQ8U>(p, grid, smem, rowt, st);
+  }
   if (wdtype == MOE_DTYPE_Q8_0) return launch1<WQ8>(p, grid, smem, rowt, st);
   if (wdtype == MOE_DTYPE_BF16) return launch1<WBF16>(p, grid, smem, rowt, st);
   return fail(MOE_ERR_UNSUPPORTED, "decode expert kernel: weight format not built yet");

@@ -28,8 +28,11 @@
 //   Q4_K: per (expert, 128-row tile, 256-column super-block) the 128 rows' quant bytes (16 KB, same
 //         chunk swizzle) and
 //         their per-sub-block f16 pairs {d*sc, -dmin*m} (4 KB), precomputed at repack.
-// Gate/up tiles hold, per 32-row group, 16 gate rows then the 16 up rows of the same columns, so
-// one warp holds a gate value and its up partner after tcgen05.ld (SwiGLU by one shuffle).
+//   Q8_0: the decode GEMV's 17 KB units of m16n8k16 fragments (repack.cu); the dequant threads
+//         gather their row's bytes from them.
+// Gate/up tiles hold, per 16-row group, 8 gate rows then the 8 up rows of the same columns, so one
+// warp holds a gate value and its up partner after tcgen05.ld (SwiGLU by one shuffle), and a 16-row
+// MMA fragment of the decode GEMV holds 8 gate/up pairs.
 #include <cuda.h>
 
 #include <cstdlib>
@@ -41,9 +44,7 @@ namespace moe {
 namespace tc {
 
 constexpr int BM = 128;
-constexpr int BN = 128;
 constexpr int BK = 128;
-constexpr int B_BYTES = BN * BK * 2;  // one stage of f16 tokens
 constexpr int A_COLS = BK / 2;        // tensor-memory columns of one dequantised weight stage
 constexpr int EPI_WARPS = 4;
 
@@ -59,10 +60,20 @@ constexpr int EPI_WARPS = 4;
 //   Pair:  two CTAs per SM, 8 dequant warps each, 2 stages, 1 accumulator, 256 columns: two MMA
 //          issuers and two dequant pipelines per SM, each CTA's epilogue overlapping the other's
 //          main loop.
-template <int DQW_, int STG_, int NACC_, int RING_, int CTAS_>
+//   Decode: see below.
+// The dequant warps form DQG groups of DQW / DQG warps; group g takes the chunks q with
+// q % DQG == g, each group covering all 128 rows (one warp per lane quarter) and the 4 column
+// quarters of its chunks. One group per CTA works chunk by chunk in lockstep (the chunk's latency
+// chain: ring read, convert, tcgen05.st, wait, hand-off); several groups keep as many chunks in
+// flight.
+template <int DQW_, int STG_, int NACC_, int RING_, int CTAS_, int BN_, int DQG_ = 1>
 struct GemmShape {
+  static constexpr int BN = BN_;                // tokens per work item (accumulator columns)
+  static constexpr int B_BYTES = BN_ * BK * 2;  // one stage of f16 tokens
   static constexpr int DQW = DQW_;
-  static constexpr int QPW = 16 / DQW_;  // 32-column quarters of a chunk each dequant thread covers
+  static constexpr int DQG = DQG_;
+  static constexpr int WG = DQW_ / DQG_;   // warps per dequant group
+  static constexpr int QPW = 16 / WG;      // 32-column quarters of a chunk each dequant thread covers
   static constexpr int STG = STG_;
   static constexpr int NACC = NACC_;
   static constexpr int RING = RING_;
@@ -72,14 +83,25 @@ struct GemmShape {
   static constexpr int TLOAD_WARP = DQW_ + 2;
   static constexpr int EPI_WARP0 = DQW_ + 4;
   static constexpr int THREADS = (DQW_ + 4 + EPI_WARPS) * 32;
-  static constexpr int A_COL0 = NACC_ * BN;
+  static constexpr int A_COL0 = NACC_ * BN_;
   static constexpr int TMEM_COLS = (A_COL0 + STG_ * A_COLS) <= 256 ? 256 : 512;
   static_assert(A_COL0 + STG_ * A_COLS <= TMEM_COLS, "tensor memory budget");
   static_assert(TMEM_COLS * CTAS_ <= 512, "co-resident CTAs must fit tensor memory together");
-  static_assert(DQW_ % 4 == 0 && 16 % DQW_ == 0, "dequant warps cover whole lane quarters");
+  static_assert(DQW_ % DQG_ == 0 && WG % 4 == 0 && 16 % WG == 0, "dequant groups cover whole lane quarters");
+  // a group's chunks reuse its own stages and ring slots (both counts whole multiples of the groups),
+  // so its parity waits never fall two phases behind: each stage and slot it waits on was last used
+  // by the same group
+  static_assert(STG_ % DQG_ == 0, "stages are whole multiples of the groups");
+  static_assert(BN_ % 32 == 0 && BN_ <= 128, "token tiles are whole 32-row TMA boxes, N <= 128");
 };
-using WideShape = GemmShape<16, 4, 2, 4, 1>;
-using PairShape = GemmShape<8, 2, 1, 2, 2>;
+using WideShape = GemmShape<16, 4, 2, 4, 1, 128>;
+using PairShape = GemmShape<8, 2, 1, 2, 2, 128>;
+// Decode shapes: few tokens per expert, so the item count is set by the weight tiles and the kernel
+// is a weight stream whose rate is the number of chunks in flight per SM. Two CTAs per SM (two
+// MMA issuers and dequant pipelines) and small token tiles, which leave tensor memory for 3
+// dequantised stages per CTA: 32-token items with 2 accumulators, or 64-token items with one.
+using Decode32Shape = GemmShape<8, 3, 2, 6, 2, 32>;
+using Decode64Shape = GemmShape<8, 3, 1, 4, 2, 64>;
 constexpr int Q4K_UNIT = BM * 128 + BM * 32;
 constexpr int TMA_ROWS = 32;  // token rows per TMA box  // Q4_K unit: quants + per-sub-block scale pairs
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -111,13 +133,29 @@ __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
   return done != 0;
 }
 
+// The same test with a suspend-time hint: a thread whose phase is not complete sleeps until it
+// completes (or about SUSPEND_NS pass) instead of spinning, so waiting roles leave the issue slots
+// to the dequantising warps.
+constexpr uint32_t SUSPEND_NS = 1u << 20;
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t a, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{.reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      "selp.u32 %0, 1, 0, p;}"
+      : "=r"(done)
+      : "r"(a), "r"(parity), "r"(SUSPEND_NS)
+      : "memory");
+  return done != 0;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try(a, parity)) return true;
   const long long t0 = clock64();
   for (uint32_t i = 0; i < WAIT_POLLS; ++i) {
-    if (mbar_try(a, parity)) return true;
-    if ((i & 63) == 63 && ((abort && *abort) || clock64() - t0 > WAIT_CYCLES)) return false;
+    if (mbar_try_sleep(a, parity)) return true;
+    if ((abort && *abort) || clock64() - t0 > WAIT_CYCLES) return false;
   }
   return false;
 }
@@ -226,8 +264,8 @@ struct FP8W {
     const unsigned char* row = unit + r * BK;
     raw.q[0] = *reinterpret_cast<const uint4*>(row + (((2 * qq) ^ (r & 7)) << 4));
     raw.q[1] = *reinterpret_cast<const uint4*>(row + (((2 * qq + 1) ^ (r & 7)) << 4));
-    // merged gate/up tiles carry two scales per chunk: rows 16..31 of each 32-row group are up rows
-    raw.s = __ldg(p.wscale + (((int64_t)e * p.tiles + tile) * (p.K / BK) + kc) * 2 + ((r & 31) >> 4));
+    // merged gate/up tiles carry two scales per chunk: rows 8..15 of each 16-row group are up rows
+    raw.s = __ldg(p.wscale + (((int64_t)e * p.tiles + tile) * (p.K / BK) + kc) * 2 + ((r >> 3) & 1));
   }
   __device__ static __forceinline__ void dequant(const Raw& raw, int, int, uint4 (&out)[4]) {
     const __half2 s2 = __float2half2_rn(raw.s);
@@ -303,6 +341,66 @@ struct Q4KW {
   __device__ static __forceinline__ int chunk_of(int qq, int j) { return (j >> 1) * 4 + (qq & 1) * 2 + (j & 1); }
 };
 
+// Q8_0: the decode GEMV's units (repack.cu, repack_q8_units): per (expert, 128-row tile, 128-column
+// chunk) 16 KB of m16n8k16 A fragments, [16-row tile s][block][slot 4g + (c ^ ((g >> 1) & 3))][16 B],
+// lane (g, c)'s word j holding {row g, row g + 8} x columns 8j + 2c, +1 of the block (u = q + 128),
+// then per s 128 B of {d(row g), d(row g + 8)} block-scale pairs at g * 16 + block * 4.
+struct Q8W {
+  static constexpr int UNIT_BYTES = Q8_UNIT_BYTES;  // 17 KB
+  static constexpr int CHUNKS_PER_UNIT = 1;
+  struct Raw {
+    uint32_t p[8];  // word j's {column 8j + 2c, +1} bytes of this row for c = 2h, 2h + 1 at p[2j + h]
+    uint32_t d;     // f16 block scale in the low half
+  };
+  __device__ static __forceinline__ const uint8_t* unit_src(const GemmParams& p, int e, int tile, int u) {
+    return p.w + (int64_t)e * p.w_stride + ((int64_t)tile * (p.K / BK) + u) * UNIT_BYTES;
+  }
+  // thread (row r, quarter qq): row r's 32 quants of block qq, gathered from the four fragment slots
+  // of its g (each holds rows g and g + 8), and its scale
+  __device__ static __forceinline__ void read(const GemmParams&, const unsigned char* unit, int, int, int, int r,
+                                              int qq, Raw& raw) {
+    const int s16 = r >> 4, g = r & 7, up = (r >> 3) & 1;
+    const unsigned char* blk = unit + (s16 * 4 + qq) * 512 + g * 64;
+    const int f = (g >> 1) & 3;
+    uint4 v[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) v[c] = *reinterpret_cast<const uint4*>(blk + ((c ^ f) << 4));
+    const uint32_t sel = up ? 0x7632u : 0x5410u;  // bytes 2,3 (row g + 8) or 0,1 (row g) of two words
+    const uint32_t w[4][4] = {{v[0].x, v[0].y, v[0].z, v[0].w},
+                              {v[1].x, v[1].y, v[1].z, v[1].w},
+                              {v[2].x, v[2].y, v[2].z, v[2].w},
+                              {v[3].x, v[3].y, v[3].z, v[3].w}};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      raw.p[2 * j] = __byte_perm(w[0][j], w[1][j], sel);
+      raw.p[2 * j + 1] = __byte_perm(w[2][j], w[3][j], sel);
+    }
+    raw.d = *reinterpret_cast<const uint16_t*>(unit + 8 * 4 * 512 + s16 * 128 + g * 16 + qq * 4 + up * 2);
+  }
+  // (1024 + u) by the 0x64 exponent byte, minus 1152 -> q exactly, times d: one f16 rounding;
+  // out[j] = columns 8j .. 8j + 7 of the block in order
+  __device__ static __forceinline__ void dequant(const Raw& raw, int, int, uint4 (&out)[4]) {
+    const __half2 bias = __float2half2_rn(1152.0f);
+    const uint32_t dd = raw.d | (raw.d << 16);
+    const __half2 d2 = *reinterpret_cast<const __half2*>(&dd);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t h[4];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        uint32_t lo = __byte_perm(raw.p[2 * j + t], 0x64646464u, 0x4140);
+        uint32_t hi = __byte_perm(raw.p[2 * j + t], 0x64646464u, 0x4342);
+        __half2 a = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&lo), bias), d2);
+        __half2 b = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&hi), bias), d2);
+        h[2 * t] = *reinterpret_cast<uint32_t*>(&a);
+        h[2 * t + 1] = *reinterpret_cast<uint32_t*>(&b);
+      }
+      out[j] = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+  }
+  __device__ static __forceinline__ int chunk_of(int qq, int j) { return (qq & 1) * 4 + j; }
+};
+
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
@@ -314,9 +412,19 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Weight-ring slots of a (format, shape): the shape's RING, or fewer when the format's units do not
+// fit the shared memory left to each of the SM's CTAS_PER_SM CTAs (228 KB per SM, 1 KB reserved per
+// CTA, a little static shared memory).
 template <class W, class C>
-constexpr int gemm_smem_bytes() {
-  return C::RING * W::UNIT_BYTES + C::STG * B_BYTES + 1024 + 512;
+__host__ __device__ constexpr int ring_slots() {
+  constexpr int budget = 233472 / C::CTAS_PER_SM - 1024 - 64;
+  constexpr int fit = (budget - C::STG * C::B_BYTES - 1024 - 512) / W::UNIT_BYTES;
+  return fit < C::RING ? fit : C::RING;
+}
+
+template <class W, class C>
+__host__ __device__ constexpr int gemm_smem_bytes() {
+  return ring_slots<W, C>() * W::UNIT_BYTES + C::STG * C::B_BYTES + 1024 + 512;
 }
 
 // ---- the GEMM ------------------------------------------------------------------------------------
@@ -345,6 +453,7 @@ struct Item {
   int e, es, base, n0, nval, nmma, tile;  // es: the expert's weight slot
 };
 
+template <int BN>
 __device__ __forceinline__ Item decode_item(const GemmParams& p, int w) {
   Item it;
   const int ti = w / p.tiles;
@@ -361,15 +470,17 @@ __device__ __forceinline__ Item decode_item(const GemmParams& p, int w) {
 }
 
 // Epilogue of one work item for the calling warp: tensor-memory lanes 32 quad .. +31 (weight rows)
-// and the 16-column blocks cb0 <= cb < cb1 of accumulator columns (tokens). Gate/up: lanes 0..15
-// hold gate rows, 16..31 the matching up rows -> h = silu(g) * u. Down: ypair = w * (W h).
+// and the 16-column blocks cb0 <= cb < cb1 of accumulator columns (tokens). Gate/up: lanes 0..7 and
+// 16..23 hold gate rows, the 8 lanes above each the matching up rows -> h = silu(g) * u. Down:
+// ypair = w * (W h).
+template <int BN>
 __device__ __forceinline__ void epilogue_blocks(const GemmParams& p, const Item& it, uint32_t tbase, int quad, int lane,
                                                 int cb0, int cb1) {
   // per-column scale (and, for the down projection, destination pair) of columns lane + 32 t
-  float csc[4];
-  int cpr[4];
+  float csc[BN / 32];
+  int cpr[BN / 32];
 #pragma unroll
-  for (int t = 0; t < 4; ++t) {
+  for (int t = 0; t < BN / 32; ++t) {
     const int n = lane + 32 * t;
     csc[t] = 0.0f;
     cpr[t] = 0;
@@ -389,13 +500,13 @@ __device__ __forceinline__ void epilogue_blocks(const GemmParams& p, const Item&
     float v[16];
     tmem_ld16(tbase + (uint32_t)c0, v);
     if (p.phase == 0) {
-      const int col = it.tile * 64 + quad * 16 + lane;
+      const int col = it.tile * 64 + quad * 16 + (lane >> 4) * 8 + (lane & 7);
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int n = c0 + i;
         const float sc = __shfl_sync(FULL, csc[n >> 5], n & 31);
-        const float up = __shfl_down_sync(FULL, v[i], 16);
-        if (lane < 16 && n < it.nval) {
+        const float up = __shfl_down_sync(FULL, v[i], 8);
+        if (!(lane & 8) && n < it.nval) {
           const float g = v[i] * sc, uu = up * sc;
           p.out[(int64_t)(it.base + it.n0 + n) * (p.N_rows >> 1) + col] = __fdividef(g, 1.0f + __expf(-g)) * uu;
         }
@@ -419,30 +530,34 @@ __device__ __forceinline__ void epilogue_blocks(const GemmParams& p, const Item&
 // dequant warps run ahead into the next item.
 template <class C>
 __device__ __forceinline__ bool dequant_joins_epilogue(const GemmParams& p) {
-  return C::NACC == 1 && p.phase == 0;
+  return C::NACC == 1 && C::DQG == 1 && C::BN == 128 && p.phase == 0;
 }
 
 template <class C>
 __device__ __forceinline__ void epilogue_range(const GemmParams& p, int part, int* cb0, int* cb1) {
   if (!dequant_joins_epilogue<C>(p)) {
     *cb0 = 0;
-    *cb1 = BN / 16;
+    *cb1 = C::BN / 16;
   } else {
     *cb0 = part * 3;
-    *cb1 = part == 2 ? BN / 16 : part * 3 + 3;
+    *cb1 = part == 2 ? C::BN / 16 : part * 3 + 3;
   }
 }
 
 template <class W, class C>
 __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
     expert_gemm_kernel(GemmParams p, const __grid_constant__ CUtensorMap tmap) {
+  constexpr int R = ring_slots<W, C>();
+  static_assert(R >= 2 && R % C::DQG == 0, "weight ring: at least two slots, whole multiples of the groups");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  unsigned char* sB = smem;                                // [C::STG][B_BYTES]
-  unsigned char* sR = sB + C::STG * B_BYTES;              // [RING][UNIT_BYTES] raw weights
-  uint64_t* raw_full = reinterpret_cast<uint64_t*>(sR + C::RING * W::UNIT_BYTES);
-  uint64_t* raw_free = raw_full + C::RING;
-  uint64_t* b_full = raw_free + C::RING;
+  // 1024-byte aligned base, offset from the __shared__ array itself (not through an integer) so the
+  // compiler keeps the shared address space and the ring reads stay shared-memory loads
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  unsigned char* sB = smem;                                // [C::STG][C::B_BYTES]
+  unsigned char* sR = sB + C::STG * C::B_BYTES;           // [RING][UNIT_BYTES] raw weights
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(sR + R * W::UNIT_BYTES);
+  uint64_t* raw_free = raw_full + R;
+  uint64_t* b_full = raw_free + R;
   uint64_t* a_full = b_full + C::STG;
   uint64_t* stage_free = a_full + C::STG;  // MMAs of the stage's chunk done: weights and tokens reusable
   uint64_t* acc_full = stage_free + C::STG;
@@ -462,15 +577,15 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
   const int G = gridDim.x;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::RING; ++s) {
+    for (int s = 0; s < R; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_free[s], C::DQW);
+      mbar_init(&raw_free[s], W::CHUNKS_PER_UNIT * C::WG);  // each reading warp, once per chunk
     }
     for (int s = 0; s < C::STG; ++s) {
       mbar_init(&b_full[s], 1);
     }
     for (int s = 0; s < C::STG; ++s) {
-      mbar_init(&a_full[s], C::DQW);  // one arrival per dequant warp
+      mbar_init(&a_full[s], C::WG);  // one arrival per warp of the chunk's dequant group
       mbar_init(&stage_free[s], 1);
     }
     for (int s = 0; s < C::NACC; ++s) {
@@ -499,10 +614,10 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
     if (lane == 0) {
       int g = 0;
       for (int w = blockIdx.x; w < n_items && !*abort; w += G) {
-        const Item it = decode_item(p, w);
+        const Item it = decode_item<C::BN>(p, w);
         for (int u = 0; u < units; ++u, ++g) {
-          const int slot = g % C::RING;
-          if (g >= C::RING && !mbar_wait(&raw_free[slot], ((g / C::RING) - 1) & 1, abort)) {
+          const int slot = g % R;
+          if (g >= R && !mbar_wait(&raw_free[slot], ((g / R) - 1) & 1, abort)) {
             s_abort = 1;
             break;
           }
@@ -518,7 +633,7 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
     if (lane == 0) {
       int q = 0;
       for (int w = blockIdx.x; w < n_items && !*abort; w += G) {
-        const Item it = decode_item(p, w);
+        const Item it = decode_item<C::BN>(p, w);
         const int boxes = (it.nmma + TMA_ROWS - 1) / TMA_ROWS;  // only the tile's own token rows
         for (int kc = 0; kc < kchunks; ++kc, ++q) {
           const int b = q % C::STG;
@@ -529,7 +644,7 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
           mbar_expect_tx(&b_full[b], 2 * boxes * TMA_ROWS * 128);
           for (int h = 0; h < 2; ++h)
             for (int j = 0; j < boxes; ++j)
-              tma_load_2d(sB + b * B_BYTES + h * (BN * 128) + j * (TMA_ROWS * 128), &tmap, kc * BK + 64 * h,
+              tma_load_2d(sB + b * C::B_BYTES + h * (C::BN * 128) + j * (TMA_ROWS * 128), &tmap, kc * BK + 64 * h,
                           it.base + it.n0 + j * TMA_ROWS, &b_full[b]);
           s_tiles_issued = q + 1;
         }
@@ -542,7 +657,7 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
       const uint64_t bdesc0 = smem_desc(smem_u32(sB));
       int q = 0, j = 0;
       for (int w = blockIdx.x; w < n_items && !*abort; w += G, ++j) {
-        const Item it = decode_item(p, w);
+        const Item it = decode_item<C::BN>(p, w);
         const int acc = j % C::NACC;
         if (j >= C::NACC && !mbar_wait(&acc_free[acc], ((j / C::NACC) - 1) & 1, abort)) {
           s_abort = 1;
@@ -550,7 +665,7 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
         }
         tc_fence_after();
         const uint32_t idesc = idesc_f16(it.nmma);
-        const uint32_t dcol = tmem + (uint32_t)(acc * BN);
+        const uint32_t dcol = tmem + (uint32_t)(acc * C::BN);
         for (int kc = 0; kc < kchunks; ++kc, ++q) {
           const int sa = q % C::STG, b = q % C::STG;
           if (!mbar_wait(&a_full[sa], (q / C::STG) & 1, abort) || !mbar_wait(&b_full[b], (q / C::STG) & 1, abort)) {
@@ -559,10 +674,10 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
           }
           tc_fence_after();
           const uint32_t acol = tmem + (uint32_t)(C::A_COL0 + sa * A_COLS);
-          const uint64_t bd = bdesc0 + ((uint32_t)(b * B_BYTES) >> 4);
+          const uint64_t bd = bdesc0 + ((uint32_t)(b * C::B_BYTES) >> 4);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            umma_f16_ts(dcol, acol + (uint32_t)(k * 8), bd + (uint32_t)(((k >> 2) * (BN * 128) + (k & 3) * 32) >> 4),
+            umma_f16_ts(dcol, acol + (uint32_t)(k * 8), bd + (uint32_t)(((k >> 2) * (C::BN * 128) + (k & 3) * 32) >> 4),
                         idesc, (kc > 0 || k > 0) ? 1u : 0u);
           umma_commit(&stage_free[sa]);
         }
@@ -579,7 +694,7 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
     const int quad = warp & 3;  // tensor-memory lanes 32 quad .. +31
     int j = 0;
     for (int w = blockIdx.x; w < n_items; w += G, ++j) {
-      const Item it = decode_item(p, w);
+      const Item it = decode_item<C::BN>(p, w);
       const int acc = j % C::NACC;
       const bool ok = __all_sync(FULL, mbar_wait(&acc_full[acc], (j / C::NACC) & 1, abort));
       if (!ok) {
@@ -589,37 +704,35 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
       tc_fence_after();
       int cb0, cb1;
       epilogue_range<C>(p, 2, &cb0, &cb1);
-      epilogue_blocks(p, it, tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN), quad, lane, cb0, cb1);
+      epilogue_blocks<C::BN>(p, it, tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * C::BN), quad, lane, cb0, cb1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_free[acc]);
     }
   } else if (warp < C::DQW) {
     // ---------------- dequant ----------------
-    // warp w owns tensor-memory lanes 32 (w % 4) .. +31 (its weight rows, one per thread) and the
-    // QPW 32-column quarters QPW (w / 4) .. of each chunk
-    const int drow = threadIdx.x & (BM - 1), dq0 = (warp >> 2) * C::QPW;
+    // group grp = warp / WG takes the chunks q with q % DQG == grp; warp w owns tensor-memory lanes
+    // 32 (w % 4) .. +31 (its weight rows, one per thread) and the QPW 32-column quarters
+    // QPW ((w % WG) / 4) .. of each of its chunks
+    const int grp = warp / C::WG;
+    const int drow = threadIdx.x & (BM - 1), dq0 = ((warp % C::WG) >> 2) * C::QPW;
     const uint32_t lane_base = tmem + ((uint32_t)(drow & ~31) << 16) + (uint32_t)C::A_COL0;
     int q = 0, g = 0, j_item = 0;
     bool stop = false;
     for (int w = blockIdx.x; w < n_items && !stop; w += G) {
-      const Item it = decode_item(p, w);
+      const Item it = decode_item<C::BN>(p, w);
       for (int kc = 0; kc < kchunks; ++kc, ++q) {
-        const int gu = g + kc / W::CHUNKS_PER_UNIT, slot = gu % C::RING;
-        const bool ok_raw = mbar_wait(&raw_full[slot], (gu / C::RING) & 1, abort);
+        if (C::DQG > 1 && q % C::DQG != grp) continue;
+        const int gu = g + kc / W::CHUNKS_PER_UNIT, slot = gu % R;
+        const bool ok_raw = mbar_wait(&raw_full[slot], (gu / R) & 1, abort);
         // the tcgen05 stores below are warp-collective: every lane takes the same branch
         stop = __any_sync(FULL, !ok_raw);
         if (stop) break;
         typename W::Raw raw[C::QPW];
 #pragma unroll
         for (int d = 0; d < C::QPW; ++d) W::read(p, sR + slot * W::UNIT_BYTES, it.es, it.tile, kc, drow, dq0 + d, raw[d]);
-        if ((kc + 1) % W::CHUNKS_PER_UNIT == 0) {  // last read of this unit: hand the slot back
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&raw_free[slot]);
-        }
-        uint4 vals[C::QPW][4];
-#pragma unroll
-        for (int d = 0; d < C::QPW; ++d) W::dequant(raw[d], kc, dq0 + d, vals[d]);
+        __syncwarp();  // this warp's reads of the unit are done (one arrival per warp and chunk)
+        if (lane == 0) mbar_arrive(&raw_free[slot]);
         const int sa = q % C::STG;
         const bool ok_a = q < C::STG || mbar_wait(&stage_free[sa], ((q / C::STG) - 1) & 1, abort);
         stop = __any_sync(FULL, !ok_a);
@@ -629,9 +742,11 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
 #pragma unroll
         for (int d = 0; d < C::QPW; ++d) {
           const int dq = dq0 + d;
+          uint4 vals[4];
+          W::dequant(raw[d], kc, dq, vals);
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj)
-            tmem_st4(stage + (uint32_t)((dq >> 1) * 32 + W::chunk_of(dq, jj) * 4), vals[d][jj]);
+            tmem_st4(stage + (uint32_t)((dq >> 1) * 32 + W::chunk_of(dq, jj) * 4), vals[jj]);
         }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
@@ -646,7 +761,7 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
         tc_fence_after();
         int cb0, cb1;
         epilogue_range<C>(p, warp >> 2, &cb0, &cb1);
-        epilogue_blocks(p, it, tmem + ((uint32_t)(drow & ~31) << 16), warp & 3, lane, cb0, cb1);
+        epilogue_blocks<C::BN>(p, it, tmem + ((uint32_t)(drow & ~31) << 16), warp & 3, lane, cb0, cb1);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_free[0]);
@@ -661,8 +776,8 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
   // last C::STG token tiles issued (earlier ones were consumed, so their phases completed).
   const bool failed = s_abort != 0;
   if (failed && threadIdx.x == 0) {
-    for (int u = max(0, s_units_issued - C::RING); u < s_units_issued; ++u)
-      (void)mbar_wait(&raw_full[u % C::RING], (u / C::RING) & 1, nullptr);
+    for (int u = max(0, s_units_issued - R); u < s_units_issued; ++u)
+      (void)mbar_wait(&raw_full[u % R], (u / R) & 1, nullptr);
     for (int c = max(0, s_tiles_issued - C::STG); c < s_tiles_issued; ++c)
       (void)mbar_wait(&b_full[c % C::STG], (c / C::STG) & 1, nullptr);
     if (p.err) atomicExch(p.err, (int)MOE_ERR_TIMEOUT);
@@ -682,7 +797,7 @@ constexpr int TL_THREADS = 256;
 // entries; loads are independent per thread (a serial walk costs two dependent loads per expert).
 __global__ void __launch_bounds__(TL_THREADS) tile_list_kernel(const int32_t* __restrict__ counts,
                                                                const int32_t* __restrict__ active,
-                                                               const int32_t* __restrict__ n_active,
+                                                               const int32_t* __restrict__ n_active, int bn,
                                                                int32_t* __restrict__ list, int32_t* __restrict__ n_list) {
   __shared__ int s_warp[TL_THREADS / 32];
   __shared__ int s_base;
@@ -692,7 +807,7 @@ __global__ void __launch_bounds__(TL_THREADS) tile_list_kernel(const int32_t* __
   __syncthreads();
   for (int a0 = 0; a0 < na; a0 += TL_THREADS) {
     const int a = a0 + threadIdx.x;
-    const int nt = a < na ? (__ldg(counts + __ldg(active + a)) + BN - 1) / BN : 0;
+    const int nt = a < na ? (__ldg(counts + __ldg(active + a)) + bn - 1) / bn : 0;
     int incl = nt;  // inclusive scan within the warp, then across warps
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -775,12 +890,12 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, const fl
 
 // ---- repack: GGML stacks -> tile-major layouts ------------------------------------------------------
 
-// device row r of a merged gate/up tile t: group g = (r % 128) / 32, within-group i = r % 32;
-// i < 16 -> gate row 64 t + 16 g + i, else up row 64 t + 16 g + (i - 16).
+// device row r of a merged gate/up tile t: group g = (r % 128) / 16, within-group i = r % 16;
+// i < 8 -> gate row 64 t + 8 g + i, else up row 64 t + 8 g + (i - 8).
 __device__ __forceinline__ void gu_src(int tile, int r, int* which, int* row) {
-  const int g = r >> 5, i = r & 31;
-  *which = i >= 16;
-  *row = tile * 64 + g * 16 + (i & 15);
+  const int g = r >> 4, i = r & 15;
+  *which = i >= 8;
+  *row = tile * 64 + g * 8 + (i & 7);
 }
 
 // FP8: one thread per (e, tile, kchunk, row): 128 bytes + the scale
@@ -808,9 +923,9 @@ __global__ void repack_fp8_kernel(const uint8_t* __restrict__ a, const uint8_t* 
   // per (tile, chunk) two scales {rows of group half 0, rows of group half 1}: a merged tile holds gate
   // rows 64t..64t+63 and up rows 64t..64t+63, each inside one 128-row scale block of its projection;
   // an unmerged 128-row tile is one scale block, stored twice
-  if (r == 0 || r == 16) {
+  if (r == 0 || r == 8) {
     const float* ss = (which ? sb : sa);
-    dscale[(((int64_t)e * tiles + tile) * kch + kc) * 2 + (r >> 4)] =
+    dscale[(((int64_t)e * tiles + tile) * kch + kc) * 2 + (r >> 3)] =
         ss[((int64_t)e * (N_src / 128) + srow / 128) * kch + kc];
   }
 }
@@ -899,9 +1014,23 @@ moe_status make_row_tmap(void* map_out, const void* base, int64_t rows, int cols
 
 size_t tensor_map_bytes() { return sizeof(CUtensorMap); }
 
+// Decode batches (a few tokens per expert: mean <= 16, or <= 24) take the 32- or 64-token decode
+// shapes; prompts, whose busiest experts hold far more than the mean under skewed routing, the
+// 128-token prefill shapes.
+int tc_token_tile(int n_pairs, int E) {
+  static const int forced = [] {  // MOE_TC_BN=32|64|128 pins the choice (tuning knob)
+    const char* v = std::getenv("MOE_TC_BN");
+    return v ? std::atoi(v) : 0;
+  }();
+  if (forced == 32 || forced == 64 || forced == 128) return forced;
+  if ((int64_t)n_pairs <= 16ll * E) return 32;
+  return (int64_t)n_pairs <= 24ll * E ? 64 : 128;
+}
+
 int64_t tc_weight_bytes(int wdtype, int N, int K) {
   if (wdtype == MOE_DTYPE_FP8_E4M3_B128) return (int64_t)N * K;
   if (wdtype == MOE_DTYPE_Q4_K) return (int64_t)(N / tc::BM) * (K / 256) * tc::Q4K_UNIT;
+  if (wdtype == MOE_DTYPE_Q8_0) return (int64_t)(N / tc::BM) * (K / tc::BK) * Q8_UNIT_BYTES;
   return 0;
 }
 int64_t tc_scale_count(int wdtype, int N, int K) {
@@ -918,6 +1047,8 @@ moe_status tc_repack(int wdtype, const uint8_t* a, const uint8_t* b, const float
   } else if (wdtype == MOE_DTYPE_Q4_K) {
     const int64_t total = (int64_t)E * (rows / tc::BM) * (K / 256) * tc::BM;
     tc::repack_q4k_kernel<<<(unsigned)((total + t - 1) / t), t, 0, st>>>(a, b, E, N_src, K, dst);
+  } else if (wdtype == MOE_DTYPE_Q8_0) {
+    return repack_q8_units(a, b, E, N_src, K, dst, st);
   } else {
     return fail(MOE_ERR_UNSUPPORTED, "tensor-core path: weight format not built");
   }
@@ -937,9 +1068,10 @@ moe_status tc_gather(const void* x_bf16, const float* x_f32, int K, int width, c
   return MOE_OK;
 }
 
-moe_status tc_tile_list(const int32_t* counts, const int32_t* active, const int32_t* n_active, int32_t* list,
+moe_status tc_tile_list(const int32_t* counts, const int32_t* active, const int32_t* n_active, int bn, int32_t* list,
                         int32_t* n_list, cudaStream_t st) {
-  tc::tile_list_kernel<<<1, tc::TL_THREADS, 0, st>>>(counts, active, n_active, list, n_list);
+  if (bn != 32 && bn != 64 && bn != 128) return fail(MOE_ERR_INVALID, "tile list: bad token tile");
+  tc::tile_list_kernel<<<1, tc::TL_THREADS, 0, st>>>(counts, active, n_active, bn, list, n_list);
   MOE_CUDA_TRY(cudaGetLastError());
   return MOE_OK;
 }
@@ -976,8 +1108,10 @@ static moe_status launch_tc(const TcArgs& a, cudaStream_t st) {
   p.slot_of = a.slot_of;
   static int sms[64] = {};
   if (!sms[dev & 63]) MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev));
-  // persistent: CTAS_PER_SM CTAs per SM (or one per work item when there are fewer)
-  const int grid = (int)std::min<int64_t>((int64_t)a.max_tiles * p.tiles, (int64_t)sms[dev & 63] * C::CTAS_PER_SM);
+  // persistent: CTAS_PER_SM CTAs per SM (or one per work item when there are fewer); the token
+  // tiles of n_pairs sorted rows over at most max_active experts number at most n_pairs / BN + max_active
+  const int64_t max_tiles = (int64_t)(a.n_pairs + C::BN - 1) / C::BN + a.max_active;
+  const int grid = (int)std::min<int64_t>(max_tiles * p.tiles, (int64_t)sms[dev & 63] * C::CTAS_PER_SM);
   if (grid <= 0) return MOE_OK;
   tc::expert_gemm_kernel<W, C><<<grid, C::THREADS, tc::gemm_smem_bytes<W, C>(), st>>>(p, *static_cast<const CUtensorMap*>(a.tmap));
   MOE_CUDA_TRY(cudaGetLastError());
@@ -991,10 +1125,23 @@ moe_status tc_gemm(int wdtype, const TcArgs& a, cudaStream_t st) {
     const char* v = std::getenv("MOE_TC_SHAPE");
     return v && std::string(v) == "wide";
   }();
+  if (a.bn == tc::Decode32Shape::BN) {
+    if (wdtype == MOE_DTYPE_FP8_E4M3_B128) return launch_tc<tc::FP8W, tc::Decode32Shape>(a, st);
+    if (wdtype == MOE_DTYPE_Q4_K) return launch_tc<tc::Q4KW, tc::Decode32Shape>(a, st);
+    if (wdtype == MOE_DTYPE_Q8_0) return launch_tc<tc::Q8W, tc::Decode32Shape>(a, st);
+  } else if (a.bn == tc::Decode64Shape::BN) {
+    if (wdtype == MOE_DTYPE_FP8_E4M3_B128) return launch_tc<tc::FP8W, tc::Decode64Shape>(a, st);
+    if (wdtype == MOE_DTYPE_Q4_K) return launch_tc<tc::Q4KW, tc::Decode64Shape>(a, st);
+    if (wdtype == MOE_DTYPE_Q8_0) return launch_tc<tc::Q8W, tc::Decode64Shape>(a, st);
+  } else if (a.bn != tc::PairShape::BN) {
+    return fail(MOE_ERR_INVALID, "tensor-core path: token tile must be 32, 64 or 128");
+  }
   if (wdtype == MOE_DTYPE_FP8_E4M3_B128)
     return wide ? launch_tc<tc::FP8W, tc::WideShape>(a, st) : launch_tc<tc::FP8W, tc::PairShape>(a, st);
   if (wdtype == MOE_DTYPE_Q4_K)
     return wide ? launch_tc<tc::Q4KW, tc::WideShape>(a, st) : launch_tc<tc::Q4KW, tc::PairShape>(a, st);
+  if (wdtype == MOE_DTYPE_Q8_0)
+    return wide ? launch_tc<tc::Q8W, tc::WideShape>(a, st) : launch_tc<tc::Q8W, tc::PairShape>(a, st);
   return fail(MOE_ERR_UNSUPPORTED, "tensor-core path: weight format not built");
 }
 

@@ -6,6 +6,7 @@
 // expert is resident in HBM (180 GB holds every config of this path), so the per-call work is:
 // plan (histogram + stable permute) -> gate/up+SwiGLU -> down*weight -> combine, all on the
 // caller's stream with no host synchronisation, so a sequence of calls captures into one CUDA graph.
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -65,8 +66,9 @@ struct moe_layer {
   float* ypair = nullptr;
   void* route_ws = nullptr;
   size_t route_ws_bytes = 0;
-  // tensor-core path (Q4_K / FP8): tile-major weights, f16 staging, TMA maps
+  // tensor-core path (Q4_K / FP8 / Q8_0 at 128-multiples): tile-major weights, f16 staging, TMA maps
   bool tc = false;
+  bool q8_tiles = false;  // Q8_0 in units: GEMV or tcgen05 per call (q8_uses_gemm)
   float* gu_scale = nullptr;
   float* dn_scale = nullptr;
   void* x16 = nullptr;
@@ -170,7 +172,7 @@ static moe_status alloc_scratch(moe_layer* L, int max_tokens) {
     MOE_TRY(dalloc(&L->xscale, sizeof(float) * cap, &acc));
     MOE_TRY(dalloc(&L->h16, (size_t)cap * I * 2, &acc));
     MOE_TRY(dalloc(&L->hscale, sizeof(float) * cap, &acc));
-    MOE_TRY(dalloc(&L->tile_list, sizeof(int32_t) * ((size_t)cap / TC_BN + E + 1), &acc));
+    MOE_TRY(dalloc(&L->tile_list, sizeof(int32_t) * ((size_t)cap / TC_BN_MIN + E + 1), &acc));
     MOE_TRY(dalloc(&L->n_tiles, sizeof(int32_t), &acc));
     MOE_TRY(make_row_tmap(L->tmap_x, L->x16, cap, H));
     MOE_TRY(make_row_tmap(L->tmap_h, L->h16, cap, I));
@@ -341,6 +343,10 @@ moe_status moe_layer_create(const moe_layer_desc* desc, moe_layer** out) {
     return st;
   };
   L->tc = (w == MOE_DTYPE_Q4_K || w == MOE_DTYPE_FP8_E4M3_B128);
+  // Q8_0 with 128-multiple shapes: one copy of the weights in 17 KB units (repack_q8_units), read by
+  // the decode GEMV (few tokens per expert) and by the tcgen05 GEMM (more)
+  L->q8_tiles = w == MOE_DTYPE_Q8_0 && H % 128 == 0 && I % 128 == 0;
+  if (L->q8_tiles) L->tc = true;
   L->gu_q_stride = L->tc ? tc_weight_bytes(w, 2 * I, H) : device_q_bytes(w, 2 * I, H);
   L->gu_s_stride = L->tc ? 0 : device_s_bytes(w, 2 * I, H);
   L->dn_q_stride = L->tc ? tc_weight_bytes(w, H, I) : device_q_bytes(w, H, I);
@@ -454,6 +460,19 @@ static int pick_rowt(int tiles, int tpp, double est_active, int sms) {
 static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_t* ids, const float* weights,
                                int width, void* y, void* stream, void* const* events);
 
+// A Q8_0 unit-layout layer runs the tcgen05 GEMM once the batch averages 8 or more tokens per
+// expert (below that the GEMV streams the weights faster: it splits K across warps, so few experts
+// still fill the GPU, and its MMA work is still small); MOE_Q8_PATH=gemv|gemm pins the choice.
+static bool q8_uses_gemm(int n_pairs, int E) {
+  static const int forced = [] {
+    const char* v = std::getenv("MOE_Q8_PATH");
+    if (!v) return 0;
+    return std::string(v) == "gemm" ? 1 : std::string(v) == "gemv" ? -1 : 0;
+  }();
+  if (forced) return forced > 0;
+  return (int64_t)n_pairs >= 8ll * E;
+}
+
 moe_status moe_forward(moe_layer* L, const void* x, int T, const uint32_t* ids, const float* weights, int width,
                        void* y, void* stream) {
   return forward_impl(L, x, T, ids, weights, width, y, stream, nullptr);
@@ -510,9 +529,10 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   MOE_TRY(mark(events, 1, st));
   const int max_active = n_pairs < E ? n_pairs : E;
   const double est = (double)E * (1.0 - std::pow(1.0 - 1.0 / E, (double)n_pairs));
-  if (L->tc) {
+  if (L->tc && (!L->q8_tiles || q8_uses_gemm(n_pairs, E))) {
     const int w = L->d.wdtype;
-    MOE_TRY(tc_tile_list(L->counts, L->active, L->n_active, L->tile_list, L->n_tiles, st));
+    const int bn = tc_token_tile(n_pairs, E);
+    MOE_TRY(tc_tile_list(L->counts, L->active, L->n_active, bn, L->tile_list, L->n_tiles, st));
     MOE_TRY(tc_gather(x, nullptr, H, width, L->perm, n_pairs, L->offsets + E, L->x16, L->xscale, st));
     TcArgs ga{};
     ga.w = L->gu_q;
@@ -531,7 +551,9 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
     ga.out = L->h;
     ga.err = L->err;
     ga.tmap = L->tmap_x;
-    ga.max_tiles = (n_pairs + TC_BN - 1) / TC_BN + max_active;
+    ga.n_pairs = n_pairs;
+    ga.max_active = max_active;
+    ga.bn = bn;
     ga.slot_of = slot_of;
     MOE_TRY(tc_gemm(w, ga, st));
     MOE_TRY(mark(events, 2, st));
@@ -573,6 +595,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   gp.active = L->active;
   gp.n_active = L->n_active;
   gp.slot_of = slot_of;
+  gp.tile_major = L->q8_tiles ? 1 : 0;
   MOE_TRY(launch_expert_gemv(L->d.wdtype, gp, max_active, pick_rowt(gp.tiles, gp.tpp, est, L->sms), st));
   MOE_TRY(mark(events, 2, st));
 

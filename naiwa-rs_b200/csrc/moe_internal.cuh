@@ -30,7 +30,7 @@ moe_status plan_pairs(const uint32_t* ids, int n_pairs, int E, const PlanOut& o,
 size_t plan_workspace_bytes(int n_pairs, int E);
 
 struct ExpertParams {
-  const uint8_t* wq;   // fragment-native weights, expert-major
+  const uint8_t* wq;   // fragment-native weights, expert-major (or Q8_0 tile-major, tile_major = 1)
   const uint8_t* wsc;  // Q8_0 scales (null for BF16)
   int64_t q_stride;    // bytes per expert
   int64_t s_stride;
@@ -52,6 +52,7 @@ struct ExpertParams {
   const int32_t* n_active;    // [1]
   int units_per_expert;
   const int32_t* slot_of;     // [E] cache slot of each expert, or null: weights indexed by expert id
+  int tile_major;             // Q8_0 only: weights in 128 x 128 units (repack_q8_units)
 };
 moe_status launch_expert_gemv(int wdtype, ExpertParams p, int max_active, int rowt, cudaStream_t st);
 moe_status launch_combine(const float* ypair, const uint32_t* ids, int T, int width, int H, int E, void* y,
@@ -63,6 +64,11 @@ int64_t device_q_bytes(int wdtype, int N, int K);
 int64_t device_s_bytes(int wdtype, int N, int K);
 moe_status repack_projection(int wdtype, const uint8_t* a, const uint8_t* b, int E, int N_src, int K, uint8_t* dq,
                              uint8_t* ds, cudaStream_t st);
+// Q8_0 units: per (expert, 128-row tile, 128-column chunk) 16 KB of fragments + 1 KB of scales,
+// read by the decode GEMV (tile_major) and the tcgen05 GEMM.
+constexpr int Q8_UNIT_BYTES = 128 * 128 + 1024;
+moe_status repack_q8_units(const uint8_t* a, const uint8_t* b, int E, int N_src, int K, uint8_t* dst,
+                           cudaStream_t st);
 
 // tensor-core (tcgen05) grouped GEMM path for Q4_K and FP8 layers
 struct TcArgs {
@@ -75,10 +81,14 @@ struct TcArgs {
   float* out;
   int32_t* err;
   const void* tmap;
-  int max_tiles;  // grid bound on (expert, token-tile) entries
+  int n_pairs, max_active;            // grid bound: token tiles <= n_pairs / bn + max_active
+  int bn = 128;                       // tokens per work item: 32 / 64 (decode shapes) or 128 (prefill)
   const int32_t* slot_of = nullptr;  // [E] cache slot of each expert, or null
 };
-constexpr int TC_BN = 128;  // tokens per tensor-core tile
+constexpr int TC_BN_MIN = 32;  // smallest token tile (sizes the tile list)
+// Token tile for a forward of n_pairs pairs over E experts: 32 or 64 for decode batches (mean tokens
+// per expert <= 16 or <= 24), else 128.
+int tc_token_tile(int n_pairs, int E);
 moe_status make_row_tmap(void* map_out, const void* base, int64_t rows, int cols);
 size_t tensor_map_bytes();
 int64_t tc_weight_bytes(int wdtype, int N, int K);
@@ -88,7 +98,7 @@ moe_status tc_repack(int wdtype, const uint8_t* a, const uint8_t* b, const float
 // n_valid: device count of sorted positions the plan filled (offsets[E]); positions past it are skipped.
 moe_status tc_gather(const void* x_bf16, const float* x_f32, int K, int width, const int32_t* perm, int n_pairs,
                      const int32_t* n_valid, void* out_f16, float* scale, cudaStream_t st);
-moe_status tc_tile_list(const int32_t* counts, const int32_t* active, const int32_t* n_active, int32_t* list,
+moe_status tc_tile_list(const int32_t* counts, const int32_t* active, const int32_t* n_active, int bn, int32_t* list,
                         int32_t* n_list, cudaStream_t st);
 moe_status tc_gemm(int wdtype, const TcArgs& a, cudaStream_t st);
 

@@ -11,6 +11,14 @@
 // d(row g+8)} (128 B), so one 16-byte load gives a lane its two rows' scales for 4 blocks.
 // Gate and up are merged: tile t holds gate rows 8t..8t+7 then up rows 8t..8t+7, which puts a
 // gate value and its up partner in the same thread after the MMA (SwiGLU in registers).
+//
+// Q8_0 units (hidden and inter multiples of 128): the same fragments and scales, grouped per
+// (expert, 128-row tile, 128-column chunk) into one contiguous 17 KB unit that both the decode GEMV
+// and the tcgen05 GEMM stream (the GEMM as one bulk copy):
+//   [16-row tile s (8)][block (4)][fragment slot (32)][16 B]  then  [s (8)][128 B of scales],
+// lane l = 4g + c's fragment stored in slot 4g + (c ^ ((g >> 1) & 3)) (the GEMM's dequant threads,
+// one per weight row, read all four slots of their g; the swizzle spreads the eight g of a warp
+// over all 32 banks).
 #include "moe_internal.cuh"
 
 namespace moe {
@@ -121,7 +129,62 @@ __global__ void repack_bf16_kernel(RepackSrc s, int E, int tiles, uint8_t* __res
   reinterpret_cast<uint4*>(dq)[i] = v;
 }
 
+// one thread per (e, 128-row tile, chunk, 16-row tile s, block, lane): 16 quant bytes, and for c == 0
+// the {d(row g), d(row g + 8)} scale pair of the block
+__global__ void repack_q8_units_kernel(RepackSrc s, int E, int tiles128, uint8_t* __restrict__ dst) {
+  const int KB = s.K / 32, kch = s.K / 128;
+  const int64_t total = (int64_t)E * tiles128 * kch * 8 * 4 * 32;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int lane = (int)(i & 31);
+  const int blk = (int)((i >> 5) & 3);
+  const int st16 = (int)((i >> 7) & 7);
+  int64_t rest = i >> 10;
+  const int kc = (int)(rest % kch); rest /= kch;
+  const int t128 = (int)(rest % tiles128);
+  const int e = (int)(rest / tiles128);
+  const int tile = t128 * 8 + st16, kb = kc * 4 + blk;
+  const int row_bytes = KB * 34;
+  uint8_t out[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    int r, kk;
+    frag_pos(lane, j & 7, &r, &kk);
+    const int k = (j >> 3) * 16 + kk;
+    out[j] = src_row(s, e, tile, r, row_bytes)[kb * 34 + 2 + k] ^ 0x80;  // stored as u = q + 128
+  }
+  uint4 v;
+  memcpy(&v, out, 16);
+  const int g = lane >> 2, c = lane & 3;
+  uint8_t* unit = dst + (((int64_t)e * tiles128 + t128) * kch + kc) * Q8_UNIT_BYTES;
+  reinterpret_cast<uint4*>(unit + (st16 * 4 + blk) * 512)[4 * g + (c ^ ((g >> 1) & 3))] = v;
+  if (c == 0) {
+    const uint8_t* p0 = src_row(s, e, tile, g, row_bytes) + kb * 34;
+    const uint8_t* p1 = src_row(s, e, tile, g + 8, row_bytes) + kb * 34;
+    const uint32_t pair = (uint32_t)(p0[0] | (p0[1] << 8)) | ((uint32_t)(p1[0] | (p1[1] << 8)) << 16);
+    *reinterpret_cast<uint32_t*>(unit + 8 * 4 * 512 + st16 * 128 + g * 16 + blk * 4) = pair;
+  }
+}
+
 static int blocks_for(int64_t n, int t) { return (int)((n + t - 1) / t); }
+
+// merged: src a = gate [E, I, H], b = up [E, I, H] -> N = 2I device rows; else a = [E, N, K].
+moe_status repack_q8_units(const uint8_t* a, const uint8_t* b, int E, int N_src, int K, uint8_t* dst,
+                           cudaStream_t st) {
+  const int rows = b ? 2 * N_src : N_src;
+  if (rows % 128 || K % 128) return fail(MOE_ERR_INVALID, "Q8_0 units need 128-multiple rows and columns");
+  RepackSrc s;
+  s.a = a;
+  s.b = b;
+  s.N_src = N_src;
+  s.K = K;
+  s.expert_bytes = (int64_t)N_src * (K / 32) * 34;
+  const int t = 256;
+  repack_q8_units_kernel<<<blocks_for((int64_t)E * (rows / 128) * (K / 128) * 1024, t), t, 0, st>>>(s, E, rows / 128,
+                                                                                                   dst);
+  MOE_CUDA_TRY(cudaGetLastError());
+  return MOE_OK;
+}
 
 // Device bytes of one expert's projection in the device layout.
 int64_t device_q_bytes(int wdtype, int N, int K) {

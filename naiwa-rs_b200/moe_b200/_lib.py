@@ -67,12 +67,14 @@ _lib = None
 
 
 def lib():
-    """Load libmoe_b200.so (building it first when the sources are newer)."""
+    """Load libmoe_b200.so (building it first when the sources are newer). MOE_B200_LIB names
+    another build of the same library to load instead (an alternate build of the same sources)."""
     global _lib
     if _lib is None:
-        if not os.path.exists(LIB_PATH) or os.environ.get("MOE_B200_REBUILD") == "1":
+        alt = os.environ.get("MOE_B200_LIB")
+        if not alt and (not os.path.exists(LIB_PATH) or os.environ.get("MOE_B200_REBUILD") == "1"):
             _build.build()
-        L = ctypes.CDLL(LIB_PATH)
+        L = ctypes.CDLL(alt or LIB_PATH)
         P, i, f = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
         sigs = {
             "moe_layer_create": (i, [ctypes.POINTER(LayerDesc), ctypes.POINTER(ctypes.c_void_p)]),

@@ -263,9 +263,10 @@ def test_config1_bf16_full_size():
     assert rel_err(y.float().cpu().numpy(), want) < REL_TOL
 
 
-@pytest.mark.parametrize("T", [1, 256])
+@pytest.mark.parametrize("T", [1, 32, 256])
 def test_config2_q8_0_full_size(T):
-    """Qwen3-30B-A3B-shaped decode layer, Q8_0, top-8 renormalised softmax."""
+    """Qwen3-30B-A3B-shaped decode layer, Q8_0, top-8 renormalised softmax. The
+    weights sit in 128 x 128 units; T = 1 and 32 run the decode GEMV, T = 256 the tcgen05 GEMM."""
     rng = np.random.default_rng(2)
     E, k, H, I = 128, 8, 2048, 768
     gate = rng.normal(0, 0.02, (E, I, H)).astype(np.float32)
