@@ -217,11 +217,18 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(Exp
   extern __shared__ __align__(16) unsigned char smem[];
   const int a_idx = blockIdx.x / p.units_per_expert;
   const int chunk = blockIdx.x % p.units_per_expert;
-  if (a_idx >= *p.n_active) return;
-  const int e = p.active[a_idx];
-  const int es = p.slot_of ? p.slot_of[e] : e;  // weights: the expert's cache slot
-  const int base = p.offsets[e];
-  const int count = p.offsets[e + 1] - base;
+  // Gate/up follows the plan directly: wait for it. Down follows gate/up, so the plan (two kernels
+  // back) has completed when it starts: it reads the plan's outputs through L2 and issues its first
+  // weight loads before waiting for gate/up's h.
+  if (p.phase == 0) {
+    pdl_wait();
+    pdl_trigger();
+  }
+  if (a_idx >= __ldcg(p.n_active)) return;
+  const int e = __ldcg(p.active + a_idx);
+  const int es = p.slot_of ? __ldcg(p.slot_of + e) : e;  // weights: the expert's cache slot
+  const int base = __ldcg(p.offsets + e);
+  const int count = __ldcg(p.offsets + e + 1) - base;
   const int ntm = NTM;
   const int tpp = NTM * 8;
   const int K = p.K;
@@ -248,6 +255,10 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(Exp
     if (tile_ok) {
       WT::load(p, es, tile, kb_begin, kb_end, lane, st[0]);
       WT::load(p, es, tile, kb_begin + G, kb_end, lane, st[1]);
+    }
+    if (p.phase == 1 && p0 == 0) {  // h and the ypair rows belong to gate/up's grid until it completes
+      pdl_wait();
+      pdl_trigger();
     }
     if (threadIdx.x < tpp) spair[threadIdx.x] = threadIdx.x < ntok ? p.perm[base + p0 + threadIdx.x] : -1;
     for (int n = warp; n < ntok; n += WARPS) {
@@ -347,6 +358,8 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(Exp
 // y[t][c] = sum_j ypair[t*width + j][c] (j in order) -> bf16; pairs with a bad id are skipped.
 __global__ void combine_kernel(const float* __restrict__ ypair, const uint32_t* __restrict__ ids, int T, int width,
                                int H, int E, __nv_bfloat16* __restrict__ y, const int32_t* __restrict__ slot_of) {
+  pdl_wait();  // ypair from the down projection
+  pdl_trigger();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // one float4 per thread
   const int64_t total = (int64_t)T * H / 4;
   if (i >= total) return;
@@ -391,8 +404,7 @@ static moe_status launch3(const ExpertParams& p, int grid, size_t smem, cudaStre
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     attr[dev & 63] = true;
   }
-  expert_gemv_kernel<WT, ROWT, NTM, WARPS><<<grid, WARPS * 32, smem, st>>>(p);
-  MOE_CUDA_TRY(cudaGetLastError());
+  MOE_CUDA_TRY(launch_pdl(expert_gemv_kernel<WT, ROWT, NTM, WARPS>, dim3(grid), dim3(WARPS * 32), smem, st, p));
   return MOE_OK;
 }
 
@@ -442,9 +454,8 @@ moe_status launch_combine(const float* ypair, const uint32_t* ids, int T, int wi
   const int64_t total = (int64_t)T * H / 4;
   if (total == 0) return MOE_OK;
   const int threads = 256;
-  combine_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, st>>>(
-      ypair, ids, T, width, H, E, static_cast<__nv_bfloat16*>(y), slot_of);
-  MOE_CUDA_TRY(cudaGetLastError());
+  MOE_CUDA_TRY(launch_pdl(combine_kernel, dim3((unsigned)((total + threads - 1) / threads)), dim3(threads), 0, st,
+                          ypair, ids, T, width, H, E, static_cast<__nv_bfloat16*>(y), slot_of));
   return MOE_OK;
 }
 

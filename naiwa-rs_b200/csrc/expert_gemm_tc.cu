@@ -567,6 +567,8 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
   __shared__ volatile int s_abort;
   __shared__ int s_units_issued, s_tiles_issued;
 
+  pdl_wait();  // the tile list, the gathered tokens and the error word come from earlier kernels
+  pdl_trigger();
   // after any CTA gave up on a wait, the rest of the launch does no work
   if (p.err && *reinterpret_cast<volatile int32_t*>(p.err) == (int32_t)MOE_ERR_TIMEOUT) return;
   const int n_items = *p.n_tiles * p.tiles;
@@ -733,6 +735,15 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
         for (int d = 0; d < C::QPW; ++d) W::read(p, sR + slot * W::UNIT_BYTES, it.es, it.tile, kc, drow, dq0 + d, raw[d]);
         __syncwarp();  // this warp's reads of the unit are done (one arrival per warp and chunk)
         if (lane == 0) mbar_arrive(&raw_free[slot]);
+        // prefill shapes (up to two quarters): convert before waiting for the stage, so the
+        // conversion overlaps the MMAs still reading it; the decode shapes, whose MMAs rarely hold a
+        // stage, convert one quarter at a time after the wait (fewer live registers)
+        constexpr bool EARLY = C::QPW <= 2 && C::BN == 128;
+        uint4 vals[EARLY ? C::QPW : 1][4];
+        if (EARLY) {
+#pragma unroll
+          for (int d = 0; d < C::QPW; ++d) W::dequant(raw[d], kc, dq0 + d, vals[EARLY ? d : 0]);
+        }
         const int sa = q % C::STG;
         const bool ok_a = q < C::STG || mbar_wait(&stage_free[sa], ((q / C::STG) - 1) & 1, abort);
         stop = __any_sync(FULL, !ok_a);
@@ -742,11 +753,11 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
 #pragma unroll
         for (int d = 0; d < C::QPW; ++d) {
           const int dq = dq0 + d;
-          uint4 vals[4];
-          W::dequant(raw[d], kc, dq, vals);
+          const int vd = EARLY ? d : 0;
+          if (!EARLY) W::dequant(raw[d], kc, dq, vals[0]);
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj)
-            tmem_st4(stage + (uint32_t)((dq >> 1) * 32 + W::chunk_of(dq, jj) * 4), vals[jj]);
+            tmem_st4(stage + (uint32_t)((dq >> 1) * 32 + W::chunk_of(dq, jj) * 4), vals[vd][jj]);
         }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
@@ -801,6 +812,8 @@ __global__ void __launch_bounds__(TL_THREADS) tile_list_kernel(const int32_t* __
                                                                int32_t* __restrict__ list, int32_t* __restrict__ n_list) {
   __shared__ int s_warp[TL_THREADS / 32];
   __shared__ int s_base;
+  pdl_wait();  // the plan's counts and active list
+  pdl_trigger();
   const int na = *n_active;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) s_base = 0;
@@ -835,6 +848,8 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, const fl
                                    const int32_t* __restrict__ perm, int n_pairs, const int32_t* __restrict__ n_valid,
                                    __half* __restrict__ out, float* __restrict__ scale) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  pdl_wait();  // perm and the rows to gather come from earlier kernels
+  pdl_trigger();
   if (warp >= n_pairs || warp >= *n_valid) return;
   const int pair = x ? perm[warp] : warp;
   if (pair < 0 || pair >= n_pairs) return;
@@ -1057,22 +1072,21 @@ moe_status tc_repack(int wdtype, const uint8_t* a, const uint8_t* b, const float
 }
 
 moe_status tc_gather(const void* x_bf16, const float* x_f32, int K, int width, const int32_t* perm, int n_pairs,
-                     const int32_t* n_valid,
-                     void* out_f16, float* scale, cudaStream_t st) {
+                     const int32_t* n_valid, void* out_f16, float* scale, cudaStream_t st, bool pdl) {
   if (n_pairs <= 0) return MOE_OK;
   const int threads = 256;
   const int blocks = (int)(((int64_t)n_pairs * 32 + threads - 1) / threads);
-  tc::gather_rows_kernel<<<blocks, threads, 0, st>>>(static_cast<const __nv_bfloat16*>(x_bf16), x_f32, K, width, perm,
-                                                     n_pairs, n_valid, static_cast<__half*>(out_f16), scale);
-  MOE_CUDA_TRY(cudaGetLastError());
+  MOE_CUDA_TRY(launch_pdl_if(pdl, tc::gather_rows_kernel, dim3(blocks), dim3(threads), 0, st,
+                          static_cast<const __nv_bfloat16*>(x_bf16), x_f32, K, width, perm, n_pairs, n_valid,
+                          static_cast<__half*>(out_f16), scale));
   return MOE_OK;
 }
 
 moe_status tc_tile_list(const int32_t* counts, const int32_t* active, const int32_t* n_active, int bn, int32_t* list,
                         int32_t* n_list, cudaStream_t st) {
   if (bn != 32 && bn != 64 && bn != 128) return fail(MOE_ERR_INVALID, "tile list: bad token tile");
-  tc::tile_list_kernel<<<1, tc::TL_THREADS, 0, st>>>(counts, active, n_active, bn, list, n_list);
-  MOE_CUDA_TRY(cudaGetLastError());
+  MOE_CUDA_TRY(launch_pdl_if(bn < 128, tc::tile_list_kernel, dim3(1), dim3(tc::TL_THREADS), 0, st, counts, active,
+                             n_active, bn, list, n_list));
   return MOE_OK;
 }
 
@@ -1113,8 +1127,9 @@ static moe_status launch_tc(const TcArgs& a, cudaStream_t st) {
   const int64_t max_tiles = (int64_t)(a.n_pairs + C::BN - 1) / C::BN + a.max_active;
   const int grid = (int)std::min<int64_t>(max_tiles * p.tiles, (int64_t)sms[dev & 63] * C::CTAS_PER_SM);
   if (grid <= 0) return MOE_OK;
-  tc::expert_gemm_kernel<W, C><<<grid, C::THREADS, tc::gemm_smem_bytes<W, C>(), st>>>(p, *static_cast<const CUtensorMap*>(a.tmap));
-  MOE_CUDA_TRY(cudaGetLastError());
+  // programmatic launch for the decode shapes only: measured, it slows the prefill pipeline
+  MOE_CUDA_TRY(launch_pdl_if(C::BN < 128, tc::expert_gemm_kernel<W, C>, dim3(grid), dim3(C::THREADS),
+                             tc::gemm_smem_bytes<W, C>(), st, p, *static_cast<const CUtensorMap*>(a.tmap)));
   return MOE_OK;
 }
 

@@ -30,6 +30,14 @@ moe_status fail(moe_status st, const std::string& msg) {
   return st;
 }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("MOE_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 moe_status cuda_fail(cudaError_t e, const char* what) {
   g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
   return e == cudaErrorMemoryAllocation ? MOE_ERR_OOM : MOE_ERR_CUDA;
@@ -533,7 +541,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
     const int w = L->d.wdtype;
     const int bn = tc_token_tile(n_pairs, E);
     MOE_TRY(tc_tile_list(L->counts, L->active, L->n_active, bn, L->tile_list, L->n_tiles, st));
-    MOE_TRY(tc_gather(x, nullptr, H, width, L->perm, n_pairs, L->offsets + E, L->x16, L->xscale, st));
+    MOE_TRY(tc_gather(x, nullptr, H, width, L->perm, n_pairs, L->offsets + E, L->x16, L->xscale, st, bn < 128));
     TcArgs ga{};
     ga.w = L->gu_q;
     ga.wscale = L->gu_scale;
@@ -557,7 +565,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
     ga.slot_of = slot_of;
     MOE_TRY(tc_gemm(w, ga, st));
     MOE_TRY(mark(events, 2, st));
-    MOE_TRY(tc_gather(nullptr, L->h, I, width, L->perm, n_pairs, L->offsets + E, L->h16, L->hscale, st));
+    MOE_TRY(tc_gather(nullptr, L->h, I, width, L->perm, n_pairs, L->offsets + E, L->h16, L->hscale, st, bn < 128));
     TcArgs da = ga;
     da.w = L->dn_q;
     da.wscale = L->dn_scale;

@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "moe_b200.h"
 
@@ -35,6 +36,44 @@ const std::string& last_error_message();  // this thread's last failure message
   } while (0)
 
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+// ---- programmatic dependent launch ---------------------------------------------------------
+// The forward's kernels are launched with launch_pdl: each may start while the kernel before it in
+// the stream is still running, so its CTAs become resident and do their set-up (barriers, tensor
+// memory, for the down GEMV the first weight loads) during the other's tail. The contract every
+// such kernel keeps: pdl_wait() (which returns once the preceding kernel has completed and its
+// writes are visible; at once when there is no programmatic dependency) comes before any access to
+// data an earlier kernel wrote or reads, and pdl_trigger() (which lets the next kernel launch)
+// only after pdl_wait(). A kernel that starts therefore knows that every kernel two or more
+// places before it has completed. MOE_PDL=0 launches everything plainly.
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool pdl_enabled();
+
+// allow = false launches plainly (the kernel's pdl_wait / pdl_trigger are then no-ops).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_if(bool allow, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                 cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = allow && pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  return launch_pdl_if(true, kernel, grid, block, smem, st, std::forward<Args>(args)...);
+}
 
 // ---- device helpers -------------------------------------------------------------------------
 

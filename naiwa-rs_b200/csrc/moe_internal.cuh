@@ -96,8 +96,9 @@ int64_t tc_scale_count(int wdtype, int N, int K);
 moe_status tc_repack(int wdtype, const uint8_t* a, const uint8_t* b, const float* sa, const float* sb, int E, int N_src,
                      int K, uint8_t* dst, float* dscale, cudaStream_t st);
 // n_valid: device count of sorted positions the plan filled (offsets[E]); positions past it are skipped.
+// pdl: programmatic launch (the decode shapes' pipeline)
 moe_status tc_gather(const void* x_bf16, const float* x_f32, int K, int width, const int32_t* perm, int n_pairs,
-                     const int32_t* n_valid, void* out_f16, float* scale, cudaStream_t st);
+                     const int32_t* n_valid, void* out_f16, float* scale, cudaStream_t st, bool pdl);
 moe_status tc_tile_list(const int32_t* counts, const int32_t* active, const int32_t* n_active, int bn, int32_t* list,
                         int32_t* n_list, cudaStream_t st);
 moe_status tc_gemm(int wdtype, const TcArgs& a, cudaStream_t st);

@@ -59,6 +59,8 @@ __device__ __forceinline__ void rank_chunk(const uint32_t* __restrict__ ids, int
 // Whole plan in one CTA (n_pairs <= PLAN_SINGLE_MAX).
 __global__ void __launch_bounds__(PLAN_THREADS) plan_single_kernel(const uint32_t* __restrict__ ids, int n_pairs,
                                                                     int E, PlanOut o) {
+  pdl_wait();  // ids (and, for the later passes, the earlier passes' output)
+  pdl_trigger();
   extern __shared__ int psm[];
   int* cnt = psm;                      // [E]
   int* base = cnt + PLAN_MAX_E;        // [E]
@@ -95,6 +97,8 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_single_kernel(const uint32_
 __global__ void __launch_bounds__(PLAN_THREADS) plan_hist_kernel(const uint32_t* __restrict__ ids, int n_pairs, int E,
                                                                   int32_t* __restrict__ chunk_counts, int32_t* err,
                                                                   const int32_t* __restrict__ slot_of) {
+  pdl_wait();  // ids (and, for the later passes, the earlier passes' output)
+  pdl_trigger();
   extern __shared__ int psm[];
   for (int e = threadIdx.x; e < E; e += PLAN_THREADS) psm[e] = 0;
   __syncthreads();
@@ -110,6 +114,8 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_hist_kernel(const uint32_t*
 
 __global__ void __launch_bounds__(PLAN_THREADS) plan_scan_kernel(int n_chunks, int E, int32_t* __restrict__ chunk_counts,
                                                                   PlanOut o) {
+  pdl_wait();  // ids (and, for the later passes, the earlier passes' output)
+  pdl_trigger();
   __shared__ int wsum[64];
   const int e = threadIdx.x;
   int total_e = 0;
@@ -137,6 +143,8 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_scatter_kernel(const uint32
                                                                      const int32_t* __restrict__ chunk_base,
                                                                      int32_t* __restrict__ perm,
                                                                      const int32_t* __restrict__ slot_of) {
+  pdl_wait();  // ids (and, for the later passes, the earlier passes' output)
+  pdl_trigger();
   extern __shared__ int psm[];
   int* base = psm;                 // [E]
   int* whist = psm + PLAN_MAX_E;   // [(PLAN_WARPS + 1) * E]
@@ -174,7 +182,7 @@ moe_status plan_pairs(const uint32_t* ids, int n_pairs, int E, const PlanOut& o,
     attr_done[dev & 63] = true;
   }
   if (n_pairs <= PLAN_SINGLE_MAX) {
-    plan_single_kernel<<<1, PLAN_THREADS, single_smem(E), st>>>(ids, n_pairs, E, o);
+    MOE_CUDA_TRY(launch_pdl(plan_single_kernel, dim3(1), dim3(PLAN_THREADS), single_smem(E), st, ids, n_pairs, E, o));
     MOE_CUDA_TRY(cudaGetLastError());
     return MOE_OK;
   }
@@ -182,11 +190,13 @@ moe_status plan_pairs(const uint32_t* ids, int n_pairs, int E, const PlanOut& o,
   if (!ws || ws_bytes < plan_workspace_bytes(n_pairs, E))
     return fail(MOE_ERR_INVALID, "moe_plan_pairs: workspace too small");
   int32_t* chunk = static_cast<int32_t*>(ws);
-  plan_hist_kernel<<<n_chunks, PLAN_THREADS, E * sizeof(int), st>>>(ids, n_pairs, E, chunk, o.err, o.slot_of);
+  MOE_CUDA_TRY(launch_pdl(plan_hist_kernel, dim3(n_chunks), dim3(PLAN_THREADS), E * sizeof(int), st, ids, n_pairs, E,
+                          chunk, o.err, o.slot_of));
   MOE_CUDA_TRY(cudaGetLastError());
-  plan_scan_kernel<<<1, PLAN_THREADS, 0, st>>>(n_chunks, E, chunk, o);
+  MOE_CUDA_TRY(launch_pdl(plan_scan_kernel, dim3(1), dim3(PLAN_THREADS), 0, st, n_chunks, E, chunk, o));
   MOE_CUDA_TRY(cudaGetLastError());
-  plan_scatter_kernel<<<n_chunks, PLAN_THREADS, scatter_smem(E), st>>>(ids, n_pairs, E, chunk, o.perm, o.slot_of);
+  MOE_CUDA_TRY(launch_pdl(plan_scatter_kernel, dim3(n_chunks), dim3(PLAN_THREADS), scatter_smem(E), st, ids, n_pairs,
+                          E, chunk, o.perm, o.slot_of));
   MOE_CUDA_TRY(cudaGetLastError());
   return MOE_OK;
 }

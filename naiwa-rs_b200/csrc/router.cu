@@ -155,6 +155,8 @@ __global__ void __launch_bounds__(ROUTER_THREADS) route_kernel(RouteParams p, fl
   const int chunks = H / 8;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint4* xs = reinterpret_cast<uint4*>(smem);  // [TB][H/8]
+  pdl_wait();  // x may come from the kernel before
+  pdl_trigger();
 
   for (int i = threadIdx.x; i < TB * chunks; i += ROUTER_THREADS) {
     const int t = i / chunks, c = i - t * chunks;
@@ -244,8 +246,7 @@ static moe_status launch_route(const RouteParams& p, float* logits, unsigned* co
     attr_set[dev & 63] = true;
   }
   dim3 grid(ceil_div(p.T, TB), ceil_div(p.E, ROUTER_EB));
-  route_kernel<TB><<<grid, ROUTER_THREADS, sm, st>>>(p, logits, counts);
-  MOE_CUDA_TRY(cudaGetLastError());
+  MOE_CUDA_TRY(launch_pdl(route_kernel<TB>, grid, dim3(ROUTER_THREADS), sm, st, p, logits, counts));
   return MOE_OK;
 }
 
