@@ -37,6 +37,75 @@ const std::string& last_error_message();  // this thread's last failure message
 
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
+// ---- mbarriers and bulk copies (shared memory) -------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+constexpr uint32_t WAIT_POLLS = 1u << 22;               // backstop on try_wait polls
+constexpr long long WAIT_CYCLES = 400ll * 1000ll * 1000ll;  // ~200 ms of SM clock: a longer wait is declared stuck
+
+// Bounded parity wait: true when the phase completed; false after WAIT_CYCLES SM clocks (or
+// WAIT_POLLS polls), or as soon as another role of the CTA gave up (*abort set; nullptr: no such
+// check). The clock is read only once the first poll failed: the common, already-completed case
+// costs one try_wait.
+__device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{.reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;}"
+      : "=r"(done)
+      : "r"(a), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// The same test with a suspend-time hint: a thread whose phase is not complete sleeps until it
+// completes (or about SUSPEND_NS pass) instead of spinning, so waiting roles leave the issue slots
+// to the dequantising warps.
+constexpr uint32_t SUSPEND_NS = 1u << 20;
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t a, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{.reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      "selp.u32 %0, 1, 0, p;}"
+      : "=r"(done)
+      : "r"(a), "r"(parity), "r"(SUSPEND_NS)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try(a, parity)) return true;
+  const long long t0 = clock64();
+  for (uint32_t i = 0; i < WAIT_POLLS; ++i) {
+    if (mbar_try_sleep(a, parity)) return true;
+    if ((abort && *abort) || clock64() - t0 > WAIT_CYCLES) return false;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // ---- programmatic dependent launch ---------------------------------------------------------
 // The forward's kernels are launched with launch_pdl: each may start while the kernel before it in
 // the stream is still running, so its CTAs become resident and do their set-up (barriers, tensor
