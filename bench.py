@@ -32,6 +32,7 @@ sys.path.insert(0, os.path.join(ROOT, "naiwa-rs_b200"))
 sys.path.insert(0, ROOT)
 
 E, K_TOP, H, I = 128, 8, 2048, 768
+PLAN_SINGLE_MAX = 8 * 1024  # pairs the plan handles in one CTA (plan.cu)
 RAGGED = [1, 2, 4, 8, 16, 32, 64, 128, 256]
 BYTES_PER_EXPERT = 3 * I * H * 34 // 32  # 5,013,504 B of Q8_0 per expert (gate + up + down)
 METRIC = "MoE-layer tokens/s per B200 (decode, Qwen3-30B-A3B-shaped Q8_0 layer, ragged batch 1-256)"
@@ -398,7 +399,15 @@ def run_ours(args):
     if host_layer0 is not None:
         cpu_base = cpu_baseline_from_layer(host_layer0[0], host_layer0[1], budget_s=args.cpu_seconds)
 
-    launches_per_step = len(RAGGED) * L * 5  # route, plan, gate/up, down, combine
+    # per layer call: route, plan (one CTA up to 8 chunks of pairs, else histogram/scan/scatter), then
+    # the decode GEMV pair (gate/up, down) below 8 tokens per expert or the tcgen05 path (tile list,
+    # token gather, gate/up GEMM, h gather, down GEMM) at or above it, then combine
+    def launches_for(T):
+        pairs = T * K_TOP
+        plan = 1 if pairs <= PLAN_SINGLE_MAX else 3
+        experts = 5 if pairs >= 8 * E else 2
+        return 1 + plan + experts + 1
+    launches_per_step = L * sum(launches_for(T) for T in RAGGED)
     if rank == 0:
         out = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -410,7 +419,8 @@ def run_ours(args):
                        "layers": L, "tokens_per_step": tokens_per_step, "ragged_batches": RAGGED,
                        "l2": "inputs larger than L2 (30.8 GB of expert weights cycled per step)",
                        "parallelism": f"replicas x{world} (each GPU its own batch, no collective)"},
-            "roofline": {"kernel": "expert_gemv (gate/up+SwiGLU and down*weight, Q8_0)", "bound": "hbm",
+            "roofline": {"kernel": "expert FFN: decode GEMV below 8 tokens per expert, tcgen05 GEMM at or "
+                                   "above (gate/up+SwiGLU and down*weight, Q8_0 units)", "bound": "hbm",
                          "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "peak_source": peak_kind,
                          "traffic": None,

@@ -21,7 +21,9 @@ namespace moe {
 
 constexpr int ROUTER_THREADS = 256;
 constexpr int ROUTER_WARPS = ROUTER_THREADS / 32;
-constexpr int ROUTER_EB = 16;  // experts per CTA (2 per warp)
+constexpr int ROUTER_EB = 8;  // experts per CTA (one per warp: twice the CTAs of two per warp, and each
+                               // warp's row loads are one HBM round trip at decode sizes)
+constexpr int ROUTER_LOADS = 8;  // 16-byte router-row loads in flight per lane (a whole H = 2048 row)
 constexpr int ROUTER_MAX_E = 1024;
 
 // Warp argmax over candidates not yet taken: the winning index (largest total-order key, ties to
@@ -170,13 +172,13 @@ __global__ void __launch_bounds__(ROUTER_THREADS) route_kernel(RouteParams p, fl
 #pragma unroll
     for (int t = 0; t < TB; ++t) acc[t] = 0.0f;
     const __nv_bfloat16* wr = p.w + (size_t)e * H;
-    for (int c0 = lane; c0 < chunks; c0 += 4 * 32) {
-      uint4 wv[4];
+    for (int c0 = lane; c0 < chunks; c0 += ROUTER_LOADS * 32) {
+      uint4 wv[ROUTER_LOADS];
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < ROUTER_LOADS; ++u)
         if (c0 + 32 * u < chunks) wv[u] = ldg_nc(wr + (c0 + 32 * u) * 8);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < ROUTER_LOADS; ++u) {
         const int c = c0 + 32 * u;
         if (c >= chunks) break;
         const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv[u]);
