@@ -302,6 +302,11 @@ def run_ours(args):
     torch.cuda.synchronize()
     act_bytes = {T: L * (T * H * 2 * 2 + T * K_TOP * 8 + E * H * 2) for T in RAGGED}  # x, y, ids+w, router
     weight_bytes = {T: distinct[T] * BYTES_PER_EXPERT for T in RAGGED}
+    # DRAM bytes (read + write) over algorithmic weight bytes in the ncu captures: the GEMV at T = 32
+    # (profiles/expert_gemv_q8_0_cfg2_t32.md: 371.6 / 367.7 MB gate/up, 188.5 / 183.8 MB down) and the
+    # tcgen05 GEMM at T = 256 (profiles/expert_gemm_tc_q8_0_cfg2_t256.md: 446.9 / 427.8 MB, 227.5 / 213.9 MB)
+    gemv_ratio, gemm_ratio = (371.6 + 188.5) / (367.7 + 183.8), (446.9 + 227.5) / (427.8 + 213.9)
+    traffic_per_step = sum(weight_bytes[T] * (gemm_ratio if T * K_TOP >= 8 * E else gemv_ratio) for T in RAGGED)
 
     # ---- stage timing: the same step with events around plan / gate-up / down / combine ---------
     nev = len(RAGGED) * L
@@ -423,7 +428,9 @@ def run_ours(args):
                                    "above (gate/up+SwiGLU and down*weight, Q8_0 units)", "bound": "hbm",
                          "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "peak_source": peak_kind,
-                         "traffic": None,
+                         "traffic": round(traffic_per_step),
+                         "traffic_unit": "DRAM bytes per step, the step's algorithmic bytes scaled by the "
+                                         "DRAM/algorithmic ratio of each path's ncu capture (profiles/)",
                          "algorithmic_bytes": "5,013,504 B per distinct expert per layer (Q8_0 gate+up+down)"},
             "stage_ms_per_step": {k: round(v, 3) for k, v in stage.items()},
             "per_batch": per_batch,
