@@ -1,25 +1,28 @@
-// expert_gemm_tc.cu — prefill-size grouped expert GEMM on the 5th-generation tensor cores.
+// expert_gemm_tc.cu — grouped expert GEMM on the 5th-generation tensor cores: prefill-size
+// batches (Q4_K / FP8 / Q8_0) and decode batches of 8 or more tokens per expert (Q8_0).
 //
 // Reference: the fork's grouped MoE kernels behind MoEExperts::forward, driven by
 // PrefillStream::dispatch (src/moe/prefill_stream.rs:1178-1216) and forward_batched (:2080-2102),
 // with the expert math of run_expert (src/moe/stages/gpu.rs:162-167).
 //
-// A work item is one (expert, 128-row weight tile, <=128-token tile) block of
+// A work item is one (expert, 128-row weight tile, <= BN-token tile) block of
 //   gate/up:  H[tok, n] = SwiGLU over the tile's 64 gate and 64 up rows of X_e W^T
 //   down:     Ypair[pair, n] = w_pair * (h_e W^T)[tok, n]
 // computed as D[128 x N] (TMEM, f32) = A[128 x K] (weights, TMEM) * B[K x N] (tokens, shared memory)
-// with tcgen05.mma kind::f16. The kernel is persistent (one CTA per SM walking the items) and
-// warp-specialised. Per 128-column K chunk:
+// with tcgen05.mma kind::f16. The kernel is persistent (one or two CTAs per SM walking the items)
+// and warp-specialised. Per 128-column K chunk:
 //   * the token tile arrives by 2-D TMA loads (64 columns x 32 rows per box, SWIZZLE_128B) from the
 //     gathered, f16-converted activations;
-//   * the weight tile streams into a shared-memory ring by 1-D bulk copies; 16 warps dequantise it
-//     (Q4_K: nibble -> f16 by the 0x6400 exponent trick, then d*sc*q - dmin*m in f16; FP8 e4m3: cvt
-//     to f16 times the 128x128 block scale) and write the f16 operand straight into tensor memory
-//     with tcgen05.st, so the dequantised weights never touch shared memory;
+//   * the weight tile streams into a shared-memory ring by 1-D bulk copies; 8 or 16 warps dequantise
+//     it (Q4_K: nibble -> f16 by the 0x6400 exponent trick, then d*sc*q - dmin*m in f16; FP8 e4m3:
+//     cvt to f16 times the 128x128 block scale; Q8_0: byte -> f16 by the same trick, times the block
+//     scale) and write the f16 operand straight into tensor memory with tcgen05.st, so the
+//     dequantised weights never touch shared memory;
 //   * one thread issues 8 MMAs (K = 16 each).
-// Two accumulators let the epilogue of one item overlap the main loop of the next.
-// Every wait is bounded: a wait that runs out sets MOE_ERR_TIMEOUT in the error word, the CTA
-// stops issuing work, waits (bounded) for its own MMAs, frees its TMEM and returns.
+// With two accumulators the epilogue of one item overlaps the main loop of the next; with one, the
+// CTA's other resident CTA covers it. Every wait is bounded: a wait that runs out sets
+// MOE_ERR_TIMEOUT in the error word, the CTA stops issuing work, waits (bounded) for its own MMAs,
+// frees its TMEM and returns.
 //
 // Weight layouts in HBM (tile-major, built by the repack kernels below):
 //   FP8:  per (expert, 128-row tile, 128-column chunk) 16 KB of e4m3, rows of 128 B with 16-byte
