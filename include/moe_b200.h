@@ -291,6 +291,10 @@ void moe_cpu_experts_destroy(moe_cpu_experts* cpu);
  * skipping MOE_ID_NONE and weight-0 slots, of w * down(silu(gate x) * up x); x [T, H] bf16 host. */
 moe_status moe_cpu_forward(const moe_cpu_experts* cpu, const uint16_t* x, const uint32_t* ids, const float* weights,
                            int T, int width, const uint8_t* select, float* y);
+/* The instruction set moe_cpu_forward's row dot products use on this host: "avx512", "avx2" or
+ * "scalar" (the widest the host reports, chosen at the first call; the environment variable
+ * MOE_CPU_ISA=scalar|avx2 caps it, for testing each build). */
+const char* moe_cpu_isa(void);
 /* An executor runs moe_cpu_forward jobs FIFO on a worker thread and publishes each result ([T, H]
  * f32) into `result_ring` (a host -> device ring whose slots hold max T * H * 4 bytes, used by this
  * executor alone). submit copies its inputs, returns at once, and gives the ring slot the result

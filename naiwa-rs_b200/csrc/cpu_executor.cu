@@ -26,31 +26,12 @@
 #include <thread>
 #include <vector>
 
+#include "cpu_kernels.h"
 #include "moe_internal.cuh"
 
 using namespace moe;
 
 namespace {
-
-inline float f16_bits_to_f32(uint16_t h) {
-  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
-  uint32_t exp = (h >> 10) & 0x1f, man = h & 0x3ffu, bits;
-  if (exp == 0) {
-    if (man == 0) bits = sign;
-    else {  // subnormal: renormalise
-      int e = -1;
-      do {
-        man <<= 1;
-        ++e;
-      } while (!(man & 0x400u));
-      bits = sign | ((uint32_t)(127 - 15 - e) << 23) | ((man & 0x3ffu) << 13);
-    }
-  } else if (exp == 31) bits = sign | 0x7f800000u | (man << 13);
-  else bits = sign | ((exp + 127 - 15) << 23) | (man << 13);
-  float f;
-  std::memcpy(&f, &bits, 4);
-  return f;
-}
 
 inline float bf16_bits_to_f32(uint16_t h) {
   const uint32_t b = (uint32_t)h << 16;
@@ -104,41 +85,18 @@ struct moe_executor {
   moe_status error_status = MOE_OK;
 };
 
-// Row r of expert e's [N, K] projection, dequantised to f32.
-static void dequant_row(const moe_cpu_experts* c, const std::vector<uint8_t>& stack, int N, int K, int e, int r,
-                        float* out) {
+// Row r of expert e's [N, K] projection (GGML bytes) times nx f32 vectors: out[j] = row . xs[j].
+static void row_dots(const moe_cpu_experts* c, const std::vector<uint8_t>& stack, int N, int K, int e, int r,
+                     const float* const* xs, int nx, float* out) {
   const uint8_t* row = stack.data() + ((int64_t)e * N + r) * c->row_bytes(K);
-  if (c->wdtype == MOE_DTYPE_Q8_0) {
-    for (int b = 0; b < K / 32; ++b) {
-      const uint8_t* blk = row + b * 34;
-      uint16_t dh;
-      std::memcpy(&dh, blk, 2);
-      const float d = f16_bits_to_f32(dh);
-      const int8_t* q = reinterpret_cast<const int8_t*>(blk + 2);
-      for (int i = 0; i < 32; ++i) out[b * 32 + i] = d * (float)q[i];
-    }
-  } else {
-    const uint16_t* w = reinterpret_cast<const uint16_t*>(row);
-    for (int i = 0; i < K; ++i) out[i] = bf16_bits_to_f32(w[i]);
-  }
+  if (c->wdtype == MOE_DTYPE_Q8_0) cpu_dot_q8_0(row, xs, nx, K, out);
+  else cpu_dot_bf16(reinterpret_cast<const uint16_t*>(row), xs, nx, K, out);
 }
 
-static inline float dot_f32(const float* a, const float* b, int n) {
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-  int i = 0;
-  for (; i + 4 <= n; i += 4) {
-    s0 += a[i] * b[i];
-    s1 += a[i + 1] * b[i + 1];
-    s2 += a[i + 2] * b[i + 2];
-    s3 += a[i + 3] * b[i + 3];
-  }
-  for (; i < n; ++i) s0 += a[i] * b[i];
-  return (s0 + s1) + (s2 + s3);
-}
-
-// Two passes over the selected pairs grouped by expert, so every weight row is dequantised once per
-// call however many of the call's tokens use the expert: pass 1 h = silu(gate x) * (up x) per pair,
-// pass 2 ypair = w * (down h) per pair; then y[t] sums the token's pairs in slot order.
+// Two passes over the selected pairs grouped by expert, so every weight row is read once per call
+// however many of the call's tokens use the expert (the row dots take the expert's vectors
+// together): pass 1 h = silu(gate x) * (up x) per pair, pass 2 ypair = w * (down h) per pair; then
+// y[t] sums the token's pairs in slot order.
 static moe_status cpu_forward_impl(const moe_cpu_experts* c, const uint16_t* x_bf16, const uint32_t* ids,
                                    const float* w, int T, int width, const uint8_t* select, float* y) {
   const int H = c->H, I = c->I, E = c->E;
@@ -164,26 +122,27 @@ static moe_status cpu_forward_impl(const moe_cpu_experts* c, const uint16_t* x_b
   parallel_for(n_seg * gu_blocks, c->threads, [&](int task) {
     const int sg = task / gu_blocks, r0 = (task % gu_blocks) * RB, r1 = std::min(I, r0 + RB);
     const int e = (int)ids[pairs[seg_start[sg]]];
-    std::vector<float> gw(H), uw(H);
+    const int i0 = seg_start[sg], n = seg_start[sg + 1] - i0;
+    std::vector<const float*> xs(n);
+    for (int j = 0; j < n; ++j) xs[j] = xf.data() + (size_t)(pairs[i0 + j] / width) * H;
+    std::vector<float> g(n), u(n);
     for (int r = r0; r < r1; ++r) {
-      dequant_row(c, c->gate, I, H, e, r, gw.data());
-      dequant_row(c, c->up, I, H, e, r, uw.data());
-      for (int i = seg_start[sg]; i < seg_start[sg + 1]; ++i) {
-        const float* xt = xf.data() + (size_t)(pairs[i] / width) * H;
-        const float g = dot_f32(gw.data(), xt, H), u = dot_f32(uw.data(), xt, H);
-        h[(size_t)i * I + r] = g / (1.0f + std::exp(-g)) * u;
-      }
+      row_dots(c, c->gate, I, H, e, r, xs.data(), n, g.data());
+      row_dots(c, c->up, I, H, e, r, xs.data(), n, u.data());
+      for (int j = 0; j < n; ++j) h[(size_t)(i0 + j) * I + r] = g[j] / (1.0f + std::exp(-g[j])) * u[j];
     }
   });
   // pass 2
   parallel_for(n_seg * dn_blocks, c->threads, [&](int task) {
     const int sg = task / dn_blocks, r0 = (task % dn_blocks) * RB, r1 = std::min(H, r0 + RB);
     const int e = (int)ids[pairs[seg_start[sg]]];
-    std::vector<float> dw(I);
+    const int i0 = seg_start[sg], n = seg_start[sg + 1] - i0;
+    std::vector<const float*> hs(n);
+    for (int j = 0; j < n; ++j) hs[j] = h.data() + (size_t)(i0 + j) * I;
+    std::vector<float> v(n);
     for (int r = r0; r < r1; ++r) {
-      dequant_row(c, c->down, H, I, e, r, dw.data());
-      for (int i = seg_start[sg]; i < seg_start[sg + 1]; ++i)
-        ypair[(size_t)i * H + r] = w[pairs[i]] * dot_f32(dw.data(), h.data() + (size_t)i * I, I);
+      row_dots(c, c->down, H, I, e, r, hs.data(), n, v.data());
+      for (int j = 0; j < n; ++j) ypair[(size_t)(i0 + j) * H + r] = w[pairs[i0 + j]] * v[j];
     }
   });
   // y[t]: the token's pairs in slot order
@@ -262,6 +221,8 @@ moe_status moe_cpu_experts_create(const moe_layer_desc* d, int n_threads, moe_cp
 }
 
 void moe_cpu_experts_destroy(moe_cpu_experts* c) { delete c; }
+
+const char* moe_cpu_isa(void) { return cpu_dot_isa(); }
 
 moe_status moe_cpu_forward(const moe_cpu_experts* c, const uint16_t* x, const uint32_t* ids, const float* weights,
                            int T, int width, const uint8_t* select, float* y) {

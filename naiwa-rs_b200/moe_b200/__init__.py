@@ -14,5 +14,5 @@ from .layer import (  # noqa: F401
 )
 from .ep import ExpertParallelMoE, PeerExpertParallelMoE, ep_combine, ep_dispatch, ep_pack_rows  # noqa: F401,E402
 from .doorbell import Ring  # noqa: F401,E402
-from .cpu import CpuExperts, Executor, add_f32_into_bf16  # noqa: F401,E402
+from .cpu import CpuExperts, Executor, add_f32_into_bf16, cpu_isa  # noqa: F401,E402
 from .paged import PagedMoE  # noqa: F401,E402

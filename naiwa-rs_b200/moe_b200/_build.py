@@ -28,7 +28,8 @@ def _nvcc() -> str:
 
 
 def sources():
-    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
+    # .cu files (device and host code) and plain host .cpp files, all compiled by nvcc
+    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cpp")))
 
 
 def _stale(lib: str) -> bool:
@@ -41,7 +42,7 @@ def _stale(lib: str) -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
-    """Compile every .cu under csrc/ and link libmoe_b200.so (static cudart)."""
+    """Compile every .cu and .cpp under csrc/ and link libmoe_b200.so (static cudart)."""
     if not force and not _stale(LIB):
         return LIB
     os.makedirs(OBJ, exist_ok=True)
@@ -49,7 +50,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     objs = []
 
     def one(src):
-        obj = os.path.join(OBJ, os.path.basename(src)[:-3] + ".o")
+        obj = os.path.join(OBJ, os.path.splitext(os.path.basename(src))[0] + ".o")
         cmd = [nvcc, *NVCC_FLAGS, "-c", src, "-o", obj]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:

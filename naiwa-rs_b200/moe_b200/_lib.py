@@ -106,6 +106,7 @@ def lib():
             "moe_cpu_experts_create": (i, [ctypes.POINTER(LayerDesc), i, ctypes.POINTER(ctypes.c_void_p)]),
             "moe_cpu_experts_destroy": (None, [P]),
             "moe_cpu_forward": (i, [P, P, P, P, i, i, P, P]),
+            "moe_cpu_isa": (ctypes.c_char_p, []),
             "moe_executor_create": (i, [P, P, ctypes.POINTER(ctypes.c_void_p)]),
             "moe_executor_submit": (i, [P, P, P, P, i, i, P, ctypes.POINTER(ctypes.c_uint32)]),
             "moe_executor_drain": (i, [P]),

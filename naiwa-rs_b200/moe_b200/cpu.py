@@ -18,6 +18,11 @@ def _np_ptr(a):
     return ctypes.c_void_p(a.ctypes.data) if a is not None else None
 
 
+def cpu_isa() -> str:
+    """The instruction set of the CPU expert path's row dot products on this host (moe_cpu_isa)."""
+    return lib().moe_cpu_isa().decode()
+
+
 class CpuExperts:
     """Host copy of a layer's Q8_0 / BF16 stacks (numpy uint8, GGML layout) and the CPU expert path."""
 
