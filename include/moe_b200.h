@@ -285,8 +285,9 @@ void moe_ring_counters(const moe_ring* ring, uint32_t* seq, uint32_t* consumed);
  * 330-378). The CPU experts keep a host copy of Q8_0 or BF16 GGML stacks (desc with host pointers). */
 typedef struct moe_cpu_experts moe_cpu_experts;
 typedef struct moe_executor moe_executor;
-/* n_threads (0: all hardware threads) includes the calling thread; the other n_threads - 1 start here
- * and serve every moe_cpu_forward on this object until destroy. Calls on one object take turns. */
+/* n_threads (0: all hardware threads) includes the calling thread; the other n_threads - 1 belong to
+ * a worker pool shared by every CPU-experts object with the same n_threads, started by the first
+ * such create and kept until the process exits. Calls that share a pool take turns. */
 moe_status moe_cpu_experts_create(const moe_layer_desc* desc, int n_threads, moe_cpu_experts** out);
 void moe_cpu_experts_destroy(moe_cpu_experts* cpu);
 /* Synchronous: y [T, H] f32 (host) = sum over the routed pairs with select[p] != 0 (select NULL: all),

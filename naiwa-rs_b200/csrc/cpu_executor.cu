@@ -21,7 +21,7 @@
 #include <cstring>
 #include <deque>
 #include <functional>
-#include <memory>
+#include <map>
 #include <mutex>
 #include <string>
 #include <thread>
@@ -41,10 +41,9 @@ inline float bf16_bits_to_f32(uint16_t h) {
   return f;
 }
 
-// Worker threads started with the CPU experts and reused by every call (starting threads per call
-// cost ~0.4 ms of a 1.3 ms decode call). run(n, f) runs f(i) for i in [0, n) on the workers and the
-// calling thread and returns when every worker has finished its share. One run at a time per pool:
-// concurrent callers take turns.
+// Worker threads reused by every call (starting threads per call cost ~0.4 ms of a 1.3 ms decode
+// call). run(n, f) runs f(i) for i in [0, n) on the workers and the calling thread and returns when
+// every worker has finished its share. One run at a time per pool: concurrent callers take turns.
 class ThreadPool {
  public:
   explicit ThreadPool(int threads) {
@@ -103,12 +102,24 @@ class ThreadPool {
   bool stop_ = false;
 };
 
+// One pool per thread count, shared by every CPU-experts object of the process (a model has one per
+// layer and runs them one at a time). The pools are created on first use and kept until the
+// process exits: idle workers only wait on a condition variable.
+ThreadPool* shared_pool(int threads) {
+  static std::mutex m;
+  static std::map<int, ThreadPool*>* pools = new std::map<int, ThreadPool*>();
+  std::lock_guard<std::mutex> l(m);
+  ThreadPool*& pool = (*pools)[threads];
+  if (!pool) pool = new ThreadPool(threads);
+  return pool;
+}
+
 }  // namespace
 
 struct moe_cpu_experts {
   int E = 0, k = 0, H = 0, I = 0, wdtype = 0, threads = 1;
   std::vector<uint8_t> gate, up, down;  // GGML bytes, [E, N, K] stacked
-  std::unique_ptr<ThreadPool> pool;     // threads - 1 workers plus the calling thread
+  ThreadPool* pool = nullptr;           // shared: threads - 1 workers plus the calling thread
 
   int64_t row_bytes(int K) const { return wdtype == MOE_DTYPE_Q8_0 ? (int64_t)K / 32 * 34 : (int64_t)K * 2; }
 };
@@ -261,7 +272,7 @@ moe_status moe_cpu_experts_create(const moe_layer_desc* d, int n_threads, moe_cp
   c->I = d->inter;
   c->wdtype = d->wdtype;
   c->threads = n_threads > 0 ? n_threads : (int)std::max(1u, std::thread::hardware_concurrency());
-  c->pool.reset(new ThreadPool(c->threads));
+  c->pool = shared_pool(c->threads);
   const int64_t gu = c->row_bytes(c->H) * c->I * c->E, dn = c->row_bytes(c->I) * c->H * c->E;
   c->gate.assign(static_cast<const uint8_t*>(d->gate), static_cast<const uint8_t*>(d->gate) + gu);
   c->up.assign(static_cast<const uint8_t*>(d->up), static_cast<const uint8_t*>(d->up) + gu);
