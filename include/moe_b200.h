@@ -327,7 +327,9 @@ moe_status moe_select_ids(const uint32_t* ids, int64_t n, int E, const uint32_t*
  * kernels that store rows straight into the peers' memory (CUDA IPC mappings, plain loads/stores,
  * no multicast). Each rank creates one peer object (cap_rows = the most tokens one rank sends per
  * call), exports its handle, gathers every rank's handle by any host channel and connects. Per call
- * (epoch = 1, 2, ... identical on every rank), on one stream:
+ * (epoch = 1, 2, ... identical on every rank; or epoch = 0 in all five calls, which takes the epoch
+ * after the last one whose combine waited on this rank from device memory, so that a captured CUDA
+ * graph of whole steps can be replayed), on one stream:
  *   moe_ep_dispatch_plan (above) -> moe_ep_peer_dispatch -> moe_ep_peer_receive -> moe_forward of the
  *   local layer on moe_ep_peer_recv_rows (world * cap_rows rows) -> moe_ep_peer_return ->
  *   moe_ep_peer_combine.
@@ -357,8 +359,14 @@ moe_status moe_ep_peer_return(moe_ep_peer* peer, const void* y_local, uint32_t e
  * token's returned rows in rank order, f32, rounded once (rank_counts / token_rows of the plan). */
 moe_status moe_ep_peer_combine(moe_ep_peer* peer, uint32_t epoch, int T, const int32_t* rank_counts,
                                const int32_t* token_rows, const void* y_add, void* y, void* stream);
-/* Synchronises `stream`, then reads and clears the peer status: MOE_OK or MOE_ERR_TIMEOUT. */
+/* Synchronises `stream`, then reads and clears the peer status: MOE_OK, MOE_ERR_TIMEOUT (a wait for
+ * another rank ran out on this rank, or a destination this rank's rows went to reported that its own
+ * receive ran out; that epoch's combine then added no returned row) or MOE_ERR_INVALID (a dispatch
+ * plan sent more than cap_rows rows to one rank; the extra rows were dropped). */
 moe_status moe_ep_peer_check(moe_ep_peer* peer, void* stream);
+/* Sets how long the peer's device-side waits for other ranks last (default five seconds), for the
+ * launches issued after this call. No counterpart in the reference. */
+moe_status moe_ep_peer_set_wait_limit(moe_ep_peer* peer, int64_t timeout_us);
 
 /* Library version string. */
 const char* moe_version(void);

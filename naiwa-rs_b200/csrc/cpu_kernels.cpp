@@ -4,9 +4,15 @@
 // + FMA + F16C, AVX2 + FMA + F16C, and portable scalar code, so the library loads on any x86-64 host.
 // The vector builds widen each Q8_0 block's 32 int8 once (2 x 16 or 4 x 8 lanes) and multiply them
 // into every activation vector of the call, then scale the block's partial sums by d in one FMA.
+// On hosts other than x86-64 (an aarch64 Grace host, say) only the scalar build is compiled.
 #include "cpu_kernels.h"
 
+#if defined(__x86_64__)
+#define MOE_CPU_X86 1
 #include <immintrin.h>
+#else
+#define MOE_CPU_X86 0
+#endif
 
 #include <cstdlib>
 #include <cstring>
@@ -71,6 +77,7 @@ void dot_bf16_scalar(const uint16_t* row, const float* const* xs, int nx, int K,
   }
 }
 
+#if MOE_CPU_X86
 __attribute__((target("avx2,fma"))) inline float hsum(__m256 v) {
   __m128 s = _mm_add_ps(_mm256_castps256_ps128(v), _mm256_extractf128_ps(v, 1));
   s = _mm_add_ps(s, _mm_movehl_ps(s, s));
@@ -200,9 +207,12 @@ __attribute__((target("avx2,fma"))) void dot_bf16_avx2_any(const uint16_t* row, 
   }
 }
 
+#endif  // MOE_CPU_X86
+
 // 2: AVX-512 (F, BW, VL) + FMA + F16C; 1: AVX2 + FMA + F16C; 0: scalar
 int host_isa() {
   static const int isa = [] {
+#if MOE_CPU_X86
     __builtin_cpu_init();
     const bool avx2 =
         __builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma") && __builtin_cpu_supports("f16c");
@@ -214,6 +224,9 @@ int host_isa() {
       else if (std::strcmp(cap, "avx2") == 0 && isa > 1) isa = 1;
     }
     return isa;
+#else
+    return 0;
+#endif
   }();
   return isa;
 }
@@ -224,9 +237,14 @@ void cpu_dot_q8_0(const uint8_t* row, const float* const* xs, int nx, int K, flo
   for (int j0 = 0; j0 < nx; j0 += CPU_DOT_MAX_X) {  // the row stays in cache across the chunks
     const int n = nx - j0 < CPU_DOT_MAX_X ? nx - j0 : CPU_DOT_MAX_X;
     const int isa = host_isa();
+#if MOE_CPU_X86
     if (isa == 2) dot_q8_0_avx512_any(row, xs + j0, n, K, out + j0);
     else if (isa == 1) dot_q8_0_avx2_any(row, xs + j0, n, K, out + j0);
     else dot_q8_0_scalar(row, xs + j0, n, K, out + j0);
+#else
+    (void)isa;
+    dot_q8_0_scalar(row, xs + j0, n, K, out + j0);
+#endif
   }
 }
 
@@ -234,9 +252,14 @@ void cpu_dot_bf16(const uint16_t* row, const float* const* xs, int nx, int K, fl
   for (int j0 = 0; j0 < nx; j0 += CPU_DOT_MAX_X) {
     const int n = nx - j0 < CPU_DOT_MAX_X ? nx - j0 : CPU_DOT_MAX_X;
     const int isa = host_isa();
+#if MOE_CPU_X86
     if (isa == 2) dot_bf16_avx512_any(row, xs + j0, n, K, out + j0);
     else if (isa == 1) dot_bf16_avx2_any(row, xs + j0, n, K, out + j0);
     else dot_bf16_scalar(row, xs + j0, n, K, out + j0);
+#else
+    (void)isa;
+    dot_bf16_scalar(row, xs + j0, n, K, out + j0);
+#endif
   }
 }
 

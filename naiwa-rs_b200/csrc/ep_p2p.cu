@@ -8,8 +8,9 @@
 //     recv_meta [W][cap][2k] int32  their (local id, weight bits) slots
 //     ret_y     [W][cap][H] bf16    my rows' outputs, region d written back by destination rank d
 //     disp_flag [W] u64             (epoch << 32 | row count) from source s, written by s
-//     ret_flag  [W] u64             (epoch << 32 | 0) from destination d, written by d
-//   and, local only: recv_count [W], two last-block counters, a status word.
+//     ret_flag  [W] u64             (epoch << 32 | failed) from destination d, written by d
+//   and, local only: recv_count [W], two last-block counters, a status word, the last epoch whose
+//   receive completed, the last epoch whose return failed and the last epoch whose combine waited.
 //
 //   moe_ep_peer_dispatch (source): rows of the dispatch plan (sorted by destination rank, then token)
 //     go to destination r's region [my rank] at their position within r's section, with 16-byte
@@ -20,17 +21,26 @@
 //     [W * cap, k] with MOE_ID_NONE for rows past a source's count (the plan skips them), so
 //     moe_forward runs on recv_x as it lies.
 //   moe_ep_peer_return (destination): each source's rows of the local output go back into that
-//     source's ret_y region [my rank]; last block publishes the return flags.
+//     source's ret_y region [my rank]; last block publishes the return flags, with the failed bit
+//     set when this epoch's receive did not complete (its rows were never computed).
 //   moe_ep_peer_combine (source): one block waits, bounded, for all W return flags of this epoch;
-//     then y[t] = y_add[t] + sum over ranks of ret_y[r][position of (t, r)], f32, rounded once.
+//     then y[t] = y_add[t] + sum over ranks of ret_y[r][position of (t, r)], f32, rounded once. When
+//     the wait ran out or any destination flagged a failure, the epoch is marked failed: the
+//     status word records MOE_ERR_TIMEOUT and the combine adds no returned row (y = y_add or 0).
 //
 // Reuse is safe without resets: a source issues epoch n + 1's dispatch only after its combine of
 // epoch n, which waited for every destination's return, which each destination issued after its
 // forward had read recv_x; a destination's return of epoch n + 1 follows its receive of that epoch,
-// which follows the source's combine of epoch n. Every wait is bounded (RING-style %globaltimer
-// limit): one that runs out records MOE_ERR_TIMEOUT in the status word (moe_ep_peer_check) and the
-// kernel returns without reading the regions. No multicast: peers are reached by plain stores and
-// loads through IPC mappings only.
+// which follows the source's combine of epoch n.
+//
+// Epochs are either given by the host (1, 2, ... identical on every rank) or, with epoch 0, held on
+// the device: each call then uses the epoch after the last one whose return-wait completed on this
+// rank, so a captured CUDA graph of a whole step can be replayed any number of times. Every wait is bounded (RING-style %globaltimer
+// limit, five seconds unless moe_ep_peer_set_wait_limit changes it): one that runs out records
+// MOE_ERR_TIMEOUT in the status word (moe_ep_peer_check) and the kernel returns without reading the
+// regions. A failure travels with the return flag, so every rank whose rows went through the failed
+// destination sees it too. No multicast: peers are reached by plain stores and loads through IPC
+// mappings only.
 #include <cstring>
 
 #include "moe_internal.cuh"
@@ -38,11 +48,13 @@
 namespace moe {
 
 constexpr int P2P_THREADS = 256;
-constexpr uint64_t P2P_WAIT_NS = 5ull * 1000ull * 1000ull * 1000ull;  // 5 s
+constexpr uint64_t P2P_WAIT_NS_DEFAULT = 5ull * 1000ull * 1000ull * 1000ull;  // 5 s
 constexpr int P2P_MAX_WORLD = 64;
+constexpr uint64_t P2P_FLAG_FAILED = 1;  // low word of a return flag: the destination's receive failed
 
 struct PeerLayout {
-  size_t recv_x, recv_meta, ret_y, disp_flag, ret_flag, recv_count, counters, status, total;
+  size_t recv_x, recv_meta, ret_y, disp_flag, ret_flag, recv_count, counters, status, recv_ok_epoch, fail_epoch,
+      done_epoch, total;
 };
 
 static PeerLayout peer_layout(int W, int cap, int H, int k) {
@@ -61,6 +73,9 @@ static PeerLayout peer_layout(int W, int cap, int H, int k) {
   l.recv_count = take((size_t)W * 4);
   l.counters = take(2 * 4);
   l.status = take(4);
+  l.recv_ok_epoch = take(4);
+  l.fail_epoch = take(4);
+  l.done_epoch = take(4);
   l.total = o;
   return l;
 }
@@ -83,6 +98,14 @@ __device__ __forceinline__ void st_release_sys64(uint64_t* p, uint64_t v) {
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
+// The epoch of a call: the host's, or (epoch_arg 0) the one after this rank's last completed
+// return-wait, which the kernels of one call all read before the call's own return-wait advances it
+// (same stream, launched in order); `ahead` is 1 before that advance and 0 after it.
+__device__ __forceinline__ uint32_t call_epoch(const unsigned char* mine, const PeerLayout& L, uint32_t epoch_arg,
+                                               uint32_t ahead) {
+  return epoch_arg ? epoch_arg : *reinterpret_cast<const volatile uint32_t*>(mine + L.done_epoch) + ahead;
+}
+
 // Rank r's section of the send rows: [start[r], start[r] + counts[r]).
 __device__ __forceinline__ int rank_of_row(const int* start, int W, int row) {
   int r = 0;
@@ -92,7 +115,7 @@ __device__ __forceinline__ int rank_of_row(const int* start, int W, int row) {
 
 // Source: rows -> peers' recv regions; last block publishes the flags.
 __global__ void __launch_bounds__(P2P_THREADS) peer_dispatch_kernel(PeerPtrs peers, PeerLayout L, int me, int W, int cap,
-                                                                    int H, int k, uint32_t epoch,
+                                                                    int H, int k, uint32_t epoch_arg,
                                                                     const uint4* __restrict__ x,
                                                                     const int32_t* __restrict__ rank_counts,
                                                                     const int32_t* __restrict__ send_token,
@@ -100,6 +123,7 @@ __global__ void __launch_bounds__(P2P_THREADS) peer_dispatch_kernel(PeerPtrs pee
                                                                     const float* __restrict__ send_w) {
   __shared__ int start[P2P_MAX_WORLD + 1];
   __shared__ int s_last;
+  const uint32_t epoch = call_epoch(peers.base[me], L, epoch_arg, 1);
   if (threadIdx.x == 0) {
     int run = 0;
     for (int r = 0; r < W; ++r) {
@@ -114,7 +138,7 @@ __global__ void __launch_bounds__(P2P_THREADS) peer_dispatch_kernel(PeerPtrs pee
   const int warps = gridDim.x * (P2P_THREADS / 32);
   for (int row = blockIdx.x * (P2P_THREADS / 32) + (threadIdx.x >> 5); row < n; row += warps) {
     const int r = rank_of_row(start, W, row), pos = row - start[r];
-    if (pos >= cap) continue;  // cannot happen: a source sends each token at most once per rank
+    if (pos >= cap) continue;  // past the destination's region: dropped, the flag says cap, status latched
     unsigned char* dst = peers.base[r];
     uint4* dx = reinterpret_cast<uint4*>(dst + L.recv_x) + ((size_t)me * cap + pos) * H16;
     const uint4* sx = x + (size_t)send_token[row] * H16;
@@ -133,27 +157,37 @@ __global__ void __launch_bounds__(P2P_THREADS) peer_dispatch_kernel(PeerPtrs pee
   if (s_last) {
     __threadfence_system();
     for (int r = threadIdx.x; r < W; r += P2P_THREADS) {
+      int n_r = start[r + 1] - start[r];
+      if (n_r > cap) {  // a malformed plan: never publish more rows than the region holds
+        n_r = cap;
+        atomicExch(reinterpret_cast<int32_t*>(peers.base[me] + L.status), (int32_t)MOE_ERR_INVALID);
+      }
       uint64_t* f = reinterpret_cast<uint64_t*>(peers.base[r] + L.disp_flag) + me;
-      st_release_sys64(f, ((uint64_t)epoch << 32) | (uint32_t)(start[r + 1] - start[r]));
+      st_release_sys64(f, ((uint64_t)epoch << 32) | (uint32_t)n_r);
     }
     if (threadIdx.x == 0) done[0] = 0;  // every block has counted: ready for the next epoch
   }
 }
 
-// Waits (thread 0, bounded) until flags[0..W) all carry `epoch`; false after the time limit.
-__device__ bool wait_flags(const uint64_t* flags, int W, uint32_t epoch, int32_t* status) {
+// Waits (thread 0, bounded by wait_ns) until flags[0..W) all carry `epoch`; false after the time
+// limit or when a flag of this epoch has its failed bit set.
+__device__ bool wait_flags(const uint64_t* flags, int W, uint32_t epoch, int32_t* status, uint64_t wait_ns) {
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
     const uint64_t t0 = p2p_now();
     int ok = 0;
     for (;;) {
-      int all = 1;
-      for (int r = 0; r < W && all; ++r) all = (uint32_t)(ld_acquire_sys64(flags + r) >> 32) == epoch;
+      int all = 1, failed = 0;
+      for (int r = 0; r < W && all; ++r) {
+        const uint64_t f = ld_acquire_sys64(flags + r);
+        all = (uint32_t)(f >> 32) == epoch;
+        failed |= all && (f & P2P_FLAG_FAILED);
+      }
       if (all) {
-        ok = 1;
+        ok = !failed;
         break;
       }
-      if (p2p_now() - t0 > P2P_WAIT_NS) break;
+      if (p2p_now() - t0 > wait_ns) break;
       __nanosleep(128);
     }
     if (!ok) atomicExch(status, (int32_t)MOE_ERR_TIMEOUT);
@@ -165,23 +199,27 @@ __device__ bool wait_flags(const uint64_t* flags, int W, uint32_t epoch, int32_t
 
 // Destination: wait for every source of this epoch, then ids/weights for the local forward.
 __global__ void __launch_bounds__(P2P_THREADS) peer_receive_kernel(PeerPtrs peers, PeerLayout L, int me, int W, int cap,
-                                                                   int k, uint32_t epoch, uint32_t* __restrict__ ids,
-                                                                   float* __restrict__ w) {
+                                                                   int k, uint32_t epoch_arg, uint64_t wait_ns,
+                                                                   uint32_t* __restrict__ ids, float* __restrict__ w) {
   unsigned char* mine = peers.base[me];
+  const uint32_t epoch = call_epoch(mine, L, epoch_arg, 1);
   const uint64_t* flags = reinterpret_cast<const uint64_t*>(mine + L.disp_flag);
   int32_t* counts = reinterpret_cast<int32_t*>(mine + L.recv_count);
   int32_t* status = reinterpret_cast<int32_t*>(mine + L.status);
+  uint32_t* recv_ok = reinterpret_cast<uint32_t*>(mine + L.recv_ok_epoch);
   __shared__ int cnt[P2P_MAX_WORLD];
-  if (!wait_flags(flags, W, epoch, status)) {
+  if (!wait_flags(flags, W, epoch, status, wait_ns)) {
     // sources that did not arrive: run nothing (all slots empty), so the forward reads no region
     for (size_t i = threadIdx.x; i < (size_t)W * cap * k; i += P2P_THREADS) ids[i] = MOE_ID_NONE;
     for (int r = threadIdx.x; r < W; r += P2P_THREADS) counts[r] = 0;
     return;
   }
   for (int r = threadIdx.x; r < W; r += P2P_THREADS) {
-    cnt[r] = (int)(uint32_t)(ld_acquire_sys64(flags + r) & 0xffffffffu);
+    const int c = (int)(uint32_t)(ld_acquire_sys64(flags + r) & 0xffffffffu);
+    cnt[r] = c < cap ? c : cap;  // a flag never names more rows than the region holds
     counts[r] = cnt[r];
   }
+  if (threadIdx.x == 0) *recv_ok = epoch;  // read by this epoch's return (same stream, later launch)
   __syncthreads();
   const int32_t* meta = reinterpret_cast<const int32_t*>(mine + L.recv_meta);
   for (size_t i = threadIdx.x; i < (size_t)W * cap * k; i += P2P_THREADS) {
@@ -199,9 +237,10 @@ __global__ void __launch_bounds__(P2P_THREADS) peer_receive_kernel(PeerPtrs peer
 
 // Destination: each source's output rows back into its ret_y region; last block publishes.
 __global__ void __launch_bounds__(P2P_THREADS) peer_return_kernel(PeerPtrs peers, PeerLayout L, int me, int W, int cap,
-                                                                  int H, uint32_t epoch, const uint4* __restrict__ y) {
+                                                                  int H, uint32_t epoch_arg, const uint4* __restrict__ y) {
   __shared__ int s_last;
   unsigned char* mine = peers.base[me];
+  const uint32_t epoch = call_epoch(mine, L, epoch_arg, 1);
   const int32_t* counts = reinterpret_cast<const int32_t*>(mine + L.recv_count);
   const int H16 = H / 8, lane = threadIdx.x & 31;
   const int warps = gridDim.x * (P2P_THREADS / 32);
@@ -219,9 +258,12 @@ __global__ void __launch_bounds__(P2P_THREADS) peer_return_kernel(PeerPtrs peers
   __syncthreads();
   if (s_last) {
     __threadfence_system();
+    // a receive that did not complete this epoch computed none of the sources' rows: say so
+    const uint64_t failed =
+        *reinterpret_cast<const volatile uint32_t*>(mine + L.recv_ok_epoch) == epoch ? 0 : P2P_FLAG_FAILED;
     for (int s = threadIdx.x; s < W; s += P2P_THREADS) {
       uint64_t* f = reinterpret_cast<uint64_t*>(peers.base[s] + L.ret_flag) + me;
-      st_release_sys64(f, (uint64_t)epoch << 32);
+      st_release_sys64(f, ((uint64_t)epoch << 32) | failed);
     }
     if (threadIdx.x == 0) *done = 0;
   }
@@ -229,14 +271,20 @@ __global__ void __launch_bounds__(P2P_THREADS) peer_return_kernel(PeerPtrs peers
 
 // Source: wait for every destination's return of this epoch (one block), then the combine.
 __global__ void __launch_bounds__(P2P_THREADS) peer_wait_return_kernel(PeerPtrs peers, PeerLayout L, int me, int W,
-                                                                       uint32_t epoch) {
+                                                                       uint32_t epoch_arg, uint64_t wait_ns) {
   unsigned char* mine = peers.base[me];
-  (void)wait_flags(reinterpret_cast<const uint64_t*>(mine + L.ret_flag), W, epoch,
-                   reinterpret_cast<int32_t*>(mine + L.status));
+  const uint32_t epoch = call_epoch(mine, L, epoch_arg, 1);
+  const bool ok = wait_flags(reinterpret_cast<const uint64_t*>(mine + L.ret_flag), W, epoch,
+                             reinterpret_cast<int32_t*>(mine + L.status), wait_ns);
+  if (threadIdx.x == 0) {
+    if (!ok) *reinterpret_cast<uint32_t*>(mine + L.fail_epoch) = epoch;  // this epoch's combine adds no returned row
+    *reinterpret_cast<uint32_t*>(mine + L.done_epoch) = epoch;  // the next device-held epoch follows it
+  }
 }
 
 // y[t] = y_add[t] + sum_r ret_y[r][token_rows[t, r] - start[r]] (rows < 0 skipped); one warp per token.
 __global__ void peer_combine_kernel(PeerPtrs peers, PeerLayout L, int me, int W, int cap, int T, int H,
+                                    uint32_t epoch_arg,
                                     const int32_t* __restrict__ rank_counts, const int32_t* __restrict__ token_rows,
                                     const uint4* __restrict__ y_add, uint4* __restrict__ y) {
   __shared__ int start[P2P_MAX_WORLD];
@@ -248,8 +296,8 @@ __global__ void peer_combine_kernel(PeerPtrs peers, PeerLayout L, int me, int W,
     }
   }
   __syncthreads();
-  const int32_t* status = reinterpret_cast<const int32_t*>(peers.base[me] + L.status);
-  const bool failed = *reinterpret_cast<const volatile int32_t*>(status) != 0;
+  const uint32_t epoch = call_epoch(peers.base[me], L, epoch_arg, 0);  // the return-wait before it advanced it
+  const bool failed = *reinterpret_cast<const volatile uint32_t*>(peers.base[me] + L.fail_epoch) == epoch;
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (t >= T) return;
   const int H8 = H / 8;
@@ -271,7 +319,7 @@ __global__ void peer_combine_kernel(PeerPtrs peers, PeerLayout L, int me, int W,
     }
     for (int r = 0; r < W && !failed; ++r) {
       const int row = token_rows[(size_t)t * W + r];
-      if (row < 0) continue;
+      if (row < 0 || row - start[r] >= cap) continue;  // rows past the region were never sent
       const uint4 v = __ldcg(ret + ((size_t)r * cap + (row - start[r])) * H8 + c);  // peer-written
       const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
 #pragma unroll
@@ -297,6 +345,7 @@ struct moe_ep_peer {
   PeerPtrs peers{};
   bool opened[P2P_MAX_WORLD] = {};
   int grid = 0;
+  uint64_t wait_ns = P2P_WAIT_NS_DEFAULT;
 };
 
 extern "C" {
@@ -388,7 +437,6 @@ moe_status moe_ep_peer_dispatch(moe_ep_peer* p, const void* x, int T, const int3
                                 uint32_t epoch, void* stream) {
   MOE_TRY(peer_ready(p, "moe_ep_peer_dispatch"));
   if (T > p->cap) return fail(MOE_ERR_INVALID, "moe_ep_peer_dispatch: T exceeds cap_rows");
-  if (epoch == 0) return fail(MOE_ERR_INVALID, "moe_ep_peer_dispatch: epochs start at 1");
   DeviceGuard guard(p->dev);
   peer_dispatch_kernel<<<p->grid, P2P_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
       p->peers, p->L, p->rank, p->world, p->cap, p->H, p->k, epoch, static_cast<const uint4*>(x), rank_counts,
@@ -401,8 +449,8 @@ moe_status moe_ep_peer_receive(moe_ep_peer* p, uint32_t epoch, uint32_t* ids, fl
   MOE_TRY(peer_ready(p, "moe_ep_peer_receive"));
   if (!ids || !weights) return fail(MOE_ERR_INVALID, "moe_ep_peer_receive: null output");
   DeviceGuard guard(p->dev);
-  peer_receive_kernel<<<1, P2P_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(p->peers, p->L, p->rank, p->world,
-                                                                               p->cap, p->k, epoch, ids, weights);
+  peer_receive_kernel<<<1, P2P_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      p->peers, p->L, p->rank, p->world, p->cap, p->k, epoch, p->wait_ns, ids, weights);
   MOE_CUDA_TRY(cudaGetLastError());
   return MOE_OK;
 }
@@ -423,13 +471,13 @@ moe_status moe_ep_peer_combine(moe_ep_peer* p, uint32_t epoch, int T, const int3
   if (T < 0 || !rank_counts || (T && (!token_rows || !y))) return fail(MOE_ERR_INVALID, "moe_ep_peer_combine: bad arguments");
   DeviceGuard guard(p->dev);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  peer_wait_return_kernel<<<1, 32, 0, st>>>(p->peers, p->L, p->rank, p->world, epoch);
+  peer_wait_return_kernel<<<1, 32, 0, st>>>(p->peers, p->L, p->rank, p->world, epoch, p->wait_ns);
   MOE_CUDA_TRY(cudaGetLastError());
   if (T == 0) return MOE_OK;
   const int threads = 256;
   peer_combine_kernel<<<(unsigned)(((int64_t)T * 32 + threads - 1) / threads), threads, 0, st>>>(
-      p->peers, p->L, p->rank, p->world, p->cap, T, p->H, rank_counts, token_rows, static_cast<const uint4*>(y_add),
-      static_cast<uint4*>(y));
+      p->peers, p->L, p->rank, p->world, p->cap, T, p->H, epoch, rank_counts, token_rows,
+      static_cast<const uint4*>(y_add), static_cast<uint4*>(y));
   MOE_CUDA_TRY(cudaGetLastError());
   return MOE_OK;
 }
@@ -442,8 +490,18 @@ moe_status moe_ep_peer_check(moe_ep_peer* p, void* stream) {
   MOE_CUDA_TRY(cudaMemcpy(&st, p->local + p->L.status, 4, cudaMemcpyDeviceToHost));
   if (st != 0) {
     MOE_CUDA_TRY(cudaMemset(p->local + p->L.status, 0, 4));
-    return fail((moe_status)st, "moe_ep_peer: a wait for another rank ran out (a peer stopped or fell behind)");
+    if (st == MOE_ERR_INVALID)
+      return fail(MOE_ERR_INVALID, "moe_ep_peer: a dispatch plan sent more rows to one rank than cap_rows");
+    return fail((moe_status)st, "moe_ep_peer: a wait for another rank ran out, or a destination reported that its "
+                                "receive did (a peer stopped or fell behind)");
   }
+  return MOE_OK;
+}
+
+moe_status moe_ep_peer_set_wait_limit(moe_ep_peer* p, int64_t timeout_us) {
+  if (!p) return fail(MOE_ERR_INVALID, "moe_ep_peer_set_wait_limit: null peer");
+  if (timeout_us <= 0) return fail(MOE_ERR_INVALID, "moe_ep_peer_set_wait_limit: the limit must be positive");
+  p->wait_ns = (uint64_t)timeout_us * 1000ull;
   return MOE_OK;
 }
 

@@ -13,6 +13,8 @@ struct RouteParams {
   int T, H, E, k, mode, n_group, topk_group;
   float routed_scale;
 };
+// Argument checks of route_tokens alone (shape, mode, pointers, alignment); enqueues nothing.
+moe_status route_validate(const RouteParams& p);
 moe_status route_tokens(const RouteParams& p, void* ws, size_t ws_bytes, cudaStream_t st);
 size_t route_workspace_bytes(int T, int E);
 

@@ -58,7 +58,10 @@ extern "C" moe_status moe_route_tokens_noalloc(const void* x, const void* w_rout
                                      std::to_string((size_t)MOE_ROUTE_NOALLOC_MAX_BYTES) + ")");
   RouteParams p{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w_router), bias, ids,
                 weights, T, H, E, k, mode, n_group, topk_group, routed_scale};
-  if (T == 0) return route_tokens(p, nullptr, 0, static_cast<cudaStream_t>(stream));
+  // every argument is checked before anything is enqueued, so a rejected call leaves the stream
+  // (and a capture in progress on it) untouched
+  MOE_TRY(route_validate(p));
+  if (T == 0) return MOE_OK;
   void* scratch = nullptr;
   MOE_TRY(scratch_address(&scratch));
   cudaStream_t st = static_cast<cudaStream_t>(stream);

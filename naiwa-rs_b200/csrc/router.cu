@@ -252,7 +252,7 @@ static moe_status launch_route(const RouteParams& p, float* logits, unsigned* co
   return MOE_OK;
 }
 
-moe_status route_tokens(const RouteParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
+moe_status route_validate(const RouteParams& p) {
   if (p.T < 0 || p.H <= 0 || p.E <= 0 || p.k <= 0 || p.k > p.E || p.k > 32)
     return fail(MOE_ERR_INVALID, "moe_route: need T >= 0, 0 < k <= min(E, 32)");
   if (p.H % 8 != 0) return fail(MOE_ERR_INVALID, "moe_route: hidden must be a multiple of 8");
@@ -270,6 +270,11 @@ moe_status route_tokens(const RouteParams& p, void* ws, size_t ws_bytes, cudaStr
     return fail(MOE_ERR_INVALID, "moe_route: x and router weight must be 16-byte aligned");
   if (((uintptr_t)p.ids | (uintptr_t)p.weights | (uintptr_t)p.bias) & 3)
     return fail(MOE_ERR_INVALID, "moe_route: ids, weights and bias must be 4-byte aligned");
+  return MOE_OK;
+}
+
+moe_status route_tokens(const RouteParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
+  MOE_TRY(route_validate(p));
   if (p.T == 0) return MOE_OK;
   if (!ws || ws_bytes < route_workspace_bytes(p.T, p.E) || ((uintptr_t)ws & 15))
     return fail(MOE_ERR_INVALID,

@@ -125,6 +125,7 @@ def lib():
             "moe_ep_peer_return": (i, [P, P, ctypes.c_uint32, P]),
             "moe_ep_peer_combine": (i, [P, ctypes.c_uint32, i, P, P, P, P, P]),
             "moe_ep_peer_check": (i, [P, P]),
+            "moe_ep_peer_set_wait_limit": (i, [P, ctypes.c_int64]),
             "moe_ring_create": (i, [i, i, ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
             "moe_ring_destroy": (None, [P]),
             "moe_ring_slot_bytes": (ctypes.c_size_t, [P]),

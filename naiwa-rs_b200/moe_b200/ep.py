@@ -175,7 +175,7 @@ class PeerExpertParallelMoE:
     `local` must be built with max_tokens >= world * max_tokens (the rows it may receive)."""
 
     def __init__(self, local, rank: int, world: int, experts_per_rank: int, max_tokens: int, group=None,
-                 shared=None):
+                 shared=None, wait_limit_us: Optional[int] = None):
         torch = _torch()
         import torch.distributed as dist
 
@@ -185,6 +185,8 @@ class PeerExpertParallelMoE:
         h = ctypes.c_void_p()
         check(lib().moe_ep_peer_create(local.device, rank, world, self.cap, self.H, self.k, ctypes.byref(h)))
         self._h = h
+        if wait_limit_us is not None:
+            self.set_wait_limit(wait_limit_us)
         nb = int(lib().moe_ep_peer_handle_bytes())
         mine = (ctypes.c_ubyte * nb)()
         check(lib().moe_ep_peer_export(self._h, ctypes.cast(mine, ctypes.c_void_p)))
@@ -199,40 +201,67 @@ class PeerExpertParallelMoE:
         self.recv_w = torch.empty((R, self.k), dtype=torch.float32, device=dev)
         self.y_local = torch.empty((R, self.H), dtype=torch.bfloat16, device=dev)
         self.recv_rows = lib().moe_ep_peer_recv_rows(self._h)
-        self.epoch = 0
+        # the dispatch plan's buffers, sized for cap tokens (moe_ep_dispatch_plan)
+        rows = self.cap * min(world, self.k)
+        self.plan = {
+            "rank_counts": torch.empty(world, dtype=torch.int32, device=dev),
+            "n_send": torch.empty(1, dtype=torch.int32, device=dev),
+            "token_rows": torch.empty((self.cap, world), dtype=torch.int32, device=dev),
+            "send_token": torch.empty(rows, dtype=torch.int32, device=dev),
+            "send_ids": torch.empty((rows, self.k), dtype=torch.int32, device=dev),
+            "send_w": torch.empty((rows, self.k), dtype=torch.float32, device=dev),
+            "error_word": torch.zeros(1, dtype=torch.int32, device=dev),
+        }
+        self.shared_w = torch.ones((self.cap, 1), dtype=torch.float32, device=dev)
+        self.shared_ids = torch.zeros((self.cap, 1), dtype=torch.int32, device=dev)
 
-    def forward(self, xs, topk_weights, topk_ids, stream=None):
+    def forward(self, xs, topk_weights, topk_ids, out=None, stream=None):
+        """[T, H] bf16 of this rank's T <= max_tokens tokens, global ids [T, k]. Every rank calls it the
+        same number of times, in the same order. The epoch is held on the device (epoch 0 in the C
+        calls), so a captured graph of calls can be replayed; nothing is allocated but the output when
+        `out` is not given."""
         torch = _torch()
         T, H = xs.shape
         if T > self.cap:
             raise ValueError("PeerExpertParallelMoE.forward: T exceeds max_tokens")
-        self.epoch += 1
-        e = self.epoch
         st = ctypes.c_void_p(_stream(stream))
         xs = xs.contiguous()
-        plan = ep_dispatch(topk_ids, topk_weights, self.epr, self.world, stream=stream)
-        check(lib().moe_ep_peer_dispatch(self._h, _ptr(xs), T, _ptr(plan["rank_counts"]), _ptr(plan["send_token"]),
-                                         _ptr(plan["send_ids"]), _ptr(plan["send_w"]), e, st))
+        ids = topk_ids if topk_ids.dtype == torch.int32 else topk_ids.to(torch.int32)
+        ids = ids.contiguous()
+        w = topk_weights if topk_weights.dtype == torch.float32 else topk_weights.to(torch.float32)
+        w = w.contiguous()
+        P = self.plan
+        L = lib()
+        check(L.moe_ep_dispatch_plan(_ptr(ids), _ptr(w), T, self.k, self.epr, self.world, _ptr(P["rank_counts"]),
+                                     _ptr(P["n_send"]), _ptr(P["token_rows"]), _ptr(P["send_token"]),
+                                     _ptr(P["send_ids"]), _ptr(P["send_w"]), _ptr(P["error_word"]), st))
+        check(L.moe_ep_peer_dispatch(self._h, _ptr(xs), T, _ptr(P["rank_counts"]), _ptr(P["send_token"]),
+                                     _ptr(P["send_ids"]), _ptr(P["send_w"]), 0, st))
         y_shared = None
         if self.shared is not None:
-            ones = torch.ones((T, 1), dtype=torch.float32, device=xs.device)
-            zeros = torch.zeros((T, 1), dtype=torch.int32, device=xs.device)
-            y_shared = self.shared.forward(xs, ones, zeros, stream=stream)
-        check(lib().moe_ep_peer_receive(self._h, e, _ptr(self.recv_ids), _ptr(self.recv_w), st))
+            y_shared = self.shared.forward(xs, self.shared_w[:T], self.shared_ids[:T], stream=stream)
+        check(L.moe_ep_peer_receive(self._h, 0, _ptr(self.recv_ids), _ptr(self.recv_w), st))
         R = self.world * self.cap
-        check(lib().moe_forward(self.local._h, ctypes.c_void_p(self.recv_rows), R, _ptr(self.recv_ids),
-                                _ptr(self.recv_w), self.k, _ptr(self.y_local), st))
-        check(lib().moe_ep_peer_return(self._h, _ptr(self.y_local), e, st))
-        y = torch.empty((T, H), dtype=torch.bfloat16, device=xs.device)
-        check(lib().moe_ep_peer_combine(self._h, e, T, _ptr(plan["rank_counts"]), _ptr(plan["token_rows"]),
-                                        _ptr(y_shared), _ptr(y), st))
+        check(L.moe_forward(self.local._h, ctypes.c_void_p(self.recv_rows), R, _ptr(self.recv_ids),
+                            _ptr(self.recv_w), self.k, _ptr(self.y_local), st))
+        check(L.moe_ep_peer_return(self._h, _ptr(self.y_local), 0, st))
+        y = out if out is not None else torch.empty((T, H), dtype=torch.bfloat16, device=xs.device)
+        check(L.moe_ep_peer_combine(self._h, 0, T, _ptr(P["rank_counts"]), _ptr(P["token_rows"]),
+                                    _ptr(y_shared), _ptr(y), st))
         return y
 
     __call__ = forward
 
+    def set_wait_limit(self, timeout_us: int):
+        """How long the device-side waits for other ranks last (default five seconds)."""
+        check(lib().moe_ep_peer_set_wait_limit(self._h, int(timeout_us)))
+
     def check(self, stream=None):
         check(lib().moe_ep_peer_check(self._h, ctypes.c_void_p(_stream(stream))))
         self.local.check()
+        if int(self.plan["error_word"].item()) != 0:
+            self.plan["error_word"].zero_()
+            check(5)  # MOE_ERR_BAD_IDS: a routed id beyond experts_per_rank * world
 
     def close(self):
         if getattr(self, "_h", None) is not None and self._h.value:

@@ -590,6 +590,187 @@ void orc_moe_forward_f32(const float* x, const uint32_t* ids, const float* w, in
   free(acc);
 }
 
+/* The same dequantised reference over quantised stacks, computed expert by expert on n_threads so
+ * that full-size layers (config 3's 512-token chunks, config 5's 7168 x 2048 FP8 experts) can be
+ * checked on every token: only one expert's f32 weights exist at a time, and the token sums run in
+ * double. Per token the experts are added in expert order instead of slot order, which moves the
+ * double sum by far less than one f32 ulp of the result. Returns -1 on bad arguments. */
+typedef struct {
+  int dtype, E, H, I, T, k;
+  const uint8_t *gate, *up, *down;
+  const float *gs, *us, *ds;
+  const float* x;
+  const float* w;
+  int e;                 /* current expert */
+  const int* pairs;      /* its pairs (t * k + j), in pair order */
+  int np;
+  float *fg, *fu, *fd;   /* its dequantised [I, H], [I, H], [H, I] */
+  double* h;             /* [np, I] */
+  double* yp;            /* [np, H] */
+  double* acc;           /* [T, H] */
+  atomic_int next;
+  int phase;
+} ref_job;
+
+static void dequant_rows(int dtype, const uint8_t* q, const float* scales, int N, int K, int r0, int r1, float* out) {
+  const int64_t row_bytes = orc_block_bytes(dtype, K);
+  if (dtype == 3) { /* FP8: the block scale of (row, column) */
+    const int kb = K / 128;
+    for (int r = r0; r < r1; ++r)
+      for (int c = 0; c < K; ++c)
+        out[(int64_t)r * K + c] = orc_fp8e4m3_to_f32(q[(int64_t)r * K + c]) * scales[(r / 128) * kb + c / 128];
+    return;
+  }
+  for (int r = r0; r < r1; ++r) {
+    const uint8_t* src = q + (int64_t)r * row_bytes;
+    float* dst = out + (int64_t)r * K;
+    if (dtype == 0) {
+      for (int c = 0; c < K; ++c) {
+        uint16_t b;
+        memcpy(&b, src + 2 * c, 2);
+        dst[c] = orc_bf16_to_f32(b);
+      }
+    } else if (dtype == 1) {
+      orc_q8_0_dequantize(src, K, dst);
+    } else {
+      orc_q4_k_dequantize(src, K, dst);
+    }
+  }
+}
+
+static double dot_f64(const float* a, const double* b, int n) {
+  double s[4] = {0, 0, 0, 0};
+  int i = 0;
+  for (; i + 4 <= n; i += 4)
+    for (int l = 0; l < 4; ++l) s[l] += (double)a[i + l] * b[i + l];
+  for (; i < n; ++i) s[0] += (double)a[i] * b[i];
+  return (s[0] + s[1]) + (s[2] + s[3]);
+}
+
+static double dot_f32x(const float* a, const float* b, int n) {
+  double s[4] = {0, 0, 0, 0};
+  int i = 0;
+  for (; i + 4 <= n; i += 4)
+    for (int l = 0; l < 4; ++l) s[l] += (double)a[i + l] * b[i + l];
+  for (; i < n; ++i) s[0] += (double)a[i] * b[i];
+  return (s[0] + s[1]) + (s[2] + s[3]);
+}
+
+static void* ref_worker(void* arg) {
+  ref_job* J = (ref_job*)arg;
+  const int CH = 32;
+  const int e = J->e, H = J->H, I = J->I;
+  if (J->phase == 0) { /* dequantise the expert: items are 32-row chunks of the three matrices */
+    const int gi = (I + CH - 1) / CH, di = (H + CH - 1) / CH;
+    for (;;) {
+      int it = atomic_fetch_add(&J->next, 1);
+      if (it >= 2 * gi + di) break;
+      const int64_t gub = orc_block_bytes(J->dtype, (int64_t)I * H);
+      const int scn = J->dtype == 3 ? (I / 128) * (H / 128) : 0;
+      if (it < 2 * gi) {
+        const int which = it / gi, r0 = (it % gi) * CH, r1 = r0 + CH < I ? r0 + CH : I;
+        const uint8_t* src = (which ? J->up : J->gate) + (int64_t)e * gub;
+        const float* sc = J->dtype == 3 ? (which ? J->us : J->gs) + (int64_t)e * scn : NULL;
+        dequant_rows(J->dtype, src, sc, I, H, r0, r1, which ? J->fu : J->fg);
+      } else {
+        const int r0 = (it - 2 * gi) * CH, r1 = r0 + CH < H ? r0 + CH : H;
+        const float* sc = J->dtype == 3 ? J->ds + (int64_t)e * scn : NULL;
+        dequant_rows(J->dtype, J->down + (int64_t)e * gub, sc, H, I, r0, r1, J->fd);
+      }
+    }
+  } else if (J->phase == 1) { /* h = silu(gate x) * (up x) per pair, in double */
+    const int per = (I + CH - 1) / CH;
+    for (;;) {
+      int it = atomic_fetch_add(&J->next, 1);
+      if (it >= J->np * per) break;
+      const int q = it / per, n0 = (it % per) * CH, n1 = n0 + CH < I ? n0 + CH : I;
+      const float* xt = J->x + (int64_t)(J->pairs[q] / J->k) * H;
+      for (int n = n0; n < n1; ++n) {
+        const double sg = dot_f32x(J->fg + (int64_t)n * H, xt, H);
+        const double su = dot_f32x(J->fu + (int64_t)n * H, xt, H);
+        J->h[(int64_t)q * I + n] = sg / (1.0 + exp(-sg)) * su;
+      }
+    }
+  } else if (J->phase == 2) { /* down per pair */
+    const int per = (H + CH - 1) / CH;
+    for (;;) {
+      int it = atomic_fetch_add(&J->next, 1);
+      if (it >= J->np * per) break;
+      const int q = it / per, n0 = (it % per) * CH, n1 = n0 + CH < H ? n0 + CH : H;
+      for (int n = n0; n < n1; ++n) J->yp[(int64_t)q * H + n] = dot_f64(J->fd + (int64_t)n * I, J->h + (int64_t)q * I, I);
+    }
+  } else { /* weighted sum into the tokens, pairs in order, by column chunk */
+    const int per = (H + CH - 1) / CH;
+    for (;;) {
+      int it = atomic_fetch_add(&J->next, 1);
+      if (it >= per) break;
+      const int n0 = it * CH, n1 = n0 + CH < H ? n0 + CH : H;
+      for (int q = 0; q < J->np; ++q) {
+        const int p = J->pairs[q];
+        const double wt = J->w[p];
+        double* at = J->acc + (int64_t)(p / J->k) * H;
+        for (int n = n0; n < n1; ++n) at[n] += wt * J->yp[(int64_t)q * H + n];
+      }
+    }
+  }
+  return NULL;
+}
+
+int orc_moe_forward_ref(int dtype, const uint8_t* gate, const uint8_t* up, const uint8_t* down, const float* gs,
+                        const float* us, const float* ds, const float* x, const uint32_t* ids, const float* w, int T,
+                        int k, int E, int H, int I, int n_threads, float* y) {
+  if (dtype < 0 || dtype > 3 || T < 0 || k <= 0 || E <= 0 || H <= 0 || I <= 0) return -1;
+  if ((dtype == 3 && (H % 128 || I % 128 || !gs || !us || !ds)) || (dtype == 1 && (H % 32 || I % 32)) ||
+      (dtype == 2 && (H % 256 || I % 256)))
+    return -1;
+  if (n_threads < 1) n_threads = 1;
+  const int n = T * k;
+  int* count = calloc((size_t)E, sizeof(int));
+  for (int p = 0; p < n; ++p)
+    if (ids[p] < (uint32_t)E) count[ids[p]]++;
+  int maxc = 0;
+  for (int e = 0; e < E; ++e) maxc = count[e] > maxc ? count[e] : maxc;
+  ref_job J;
+  memset(&J, 0, sizeof(J));
+  J.dtype = dtype; J.E = E; J.H = H; J.I = I; J.T = T; J.k = k;
+  J.gate = gate; J.up = up; J.down = down; J.gs = gs; J.us = us; J.ds = ds; J.x = x; J.w = w;
+  int* pairs = malloc(sizeof(int) * (size_t)(maxc > 0 ? maxc : 1));
+  J.pairs = pairs;
+  J.fg = malloc(sizeof(float) * (size_t)I * H);
+  J.fu = malloc(sizeof(float) * (size_t)I * H);
+  J.fd = malloc(sizeof(float) * (size_t)H * I);
+  J.h = malloc(sizeof(double) * (size_t)(maxc > 0 ? maxc : 1) * I);
+  J.yp = malloc(sizeof(double) * (size_t)(maxc > 0 ? maxc : 1) * H);
+  J.acc = calloc((size_t)T * H + 1, sizeof(double));
+  pthread_t* th = malloc(sizeof(pthread_t) * (size_t)n_threads);
+  for (int e = 0; e < E; ++e) {
+    if (!count[e]) continue;
+    int np = 0;
+    for (int p = 0; p < n; ++p)
+      if (ids[p] == (uint32_t)e) pairs[np++] = p;
+    J.e = e;
+    J.np = np;
+    for (int phase = 0; phase < 4; ++phase) {
+      J.phase = phase;
+      atomic_store(&J.next, 0);
+      for (int i = 1; i < n_threads; ++i) pthread_create(&th[i], NULL, ref_worker, &J);
+      ref_worker(&J);
+      for (int i = 1; i < n_threads; ++i) pthread_join(th[i], NULL);
+    }
+  }
+  for (int64_t i = 0; i < (int64_t)T * H; ++i) y[i] = (float)J.acc[i];
+  free(th);
+  free(pairs);
+  free(J.fg);
+  free(J.fu);
+  free(J.fd);
+  free(J.h);
+  free(J.yp);
+  free(J.acc);
+  free(count);
+  return 0;
+}
+
 /* ------------------------------------------------------------------------------------------ */
 /* timed CPU baseline                                                                          */
 /* ------------------------------------------------------------------------------------------ */

@@ -72,6 +72,11 @@ int orc_permute(const uint32_t* ids, int n_pairs, int E, int32_t* counts, int32_
 /* gate, up: [E, I, H] f32; down: [E, H, I] f32; x: [T, H] f32; ids/w: [T, k]; y: [T, H] f32. */
 void orc_moe_forward_f32(const float* x, const uint32_t* ids, const float* w, int T, int k, int E, int H,
                          int I, const float* gate, const float* up, const float* down, float* y);
+/* orc_moe_forward_f32 over quantised stacks (dtype codes of include/moe_b200.h; FP8 block scales in
+ * gs/us/ds), expert by expert on n_threads; ids >= E are skipped. */
+int orc_moe_forward_ref(int dtype, const uint8_t* gate, const uint8_t* up, const uint8_t* down, const float* gs,
+                        const float* us, const float* ds, const float* x, const uint32_t* ids, const float* w, int T,
+                        int k, int E, int H, int I, int n_threads, float* y);
 
 /* ---- timed CPU baseline: two-pass fused decode over Q8_0 stacks -------------------------- */
 /* gate/up/down are GGML Q8_0 stacks [E, I, H], [E, I, H], [E, H, I]. x f32 [T, H]. */

@@ -31,7 +31,9 @@ def build() -> str:
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(_LIB_PATH):
+        srcs = [os.path.join(_HERE, f) for f in ("moe_oracle.c", "moe_oracle.h", "Makefile")]
+        if not os.path.exists(_LIB_PATH) or any(
+                os.path.exists(f) and os.path.getmtime(f) > os.path.getmtime(_LIB_PATH) for f in srcs):
             build()
         L = ctypes.CDLL(_LIB_PATH)
         P = ctypes.c_void_p
@@ -63,6 +65,7 @@ def lib():
             "orc_route": (i, [P, P, i, i, i, i, i, i, f, P, P]),
             "orc_permute": (i, [P, i, i, P, P, P, P, P]),
             "orc_moe_forward_f32": (None, [P, P, P, i, i, i, i, i, P, P, P, P]),
+            "orc_moe_forward_ref": (i, [i, P, P, P, P, P, P, P, P, P, i, i, i, i, i, i, P]),
             "orc_fused_moe_decode_q8_0": (i, [P, P, P, P, P, P, i, i, i, i, i, i, P]),
         }
         for name, (res, args) in sig.items():
@@ -266,6 +269,25 @@ def moe_forward_f32(x, ids, w, gate, up, down):
     E, I = gate.shape[0], gate.shape[1]
     y = np.empty((T, H), dtype=np.float32)
     lib().orc_moe_forward_f32(_p(x), _p(ids), _p(w), T, k, E, H, I, _p(gate), _p(up), _p(down), _p(y))
+    return y
+
+
+def moe_forward_ref(dtype: int, q, x, ids, w, E: int, H: int, I: int, scales=None, threads: int = 0):
+    """moe_forward_f32 of the dequantised stacks, from the quantised stacks q = (gate, up, down) and,
+    for FP8, their block scales, on `threads` host threads (0: all); x [T, H] f32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    ids = np.ascontiguousarray(ids, dtype=np.uint32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    T, k = ids.shape
+    qs = [np.ascontiguousarray(a).reshape(-1) for a in q]
+    sc = [None] * 3 if scales is None else [np.ascontiguousarray(a, dtype=np.float32).reshape(-1) for a in scales]
+    y = np.empty((T, H), dtype=np.float32)
+    n = threads or (len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count() or 1)
+    rc = lib().orc_moe_forward_ref(dtype, _p(qs[0]), _p(qs[1]), _p(qs[2]), None if sc[0] is None else _p(sc[0]),
+                                   None if sc[1] is None else _p(sc[1]), None if sc[2] is None else _p(sc[2]),
+                                   _p(x), _p(ids), _p(w), T, k, E, H, I, n, _p(y))
+    if rc != 0:
+        raise ValueError("orc_moe_forward_ref: bad arguments")
     return y
 
 

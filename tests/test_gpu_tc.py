@@ -2,22 +2,17 @@
 
 Weights are dequantised to f16 inside the kernel; activations are staged as f16 with a
 power-of-two row scale. Outputs must stay within max |y - ref| / max |ref| <= 1e-2 of the oracle's
-double-accumulated dequantised reference.
+double-accumulated dequantised reference and within the elementwise bound
+of tests/tolerance.py on every token.
 """
 import numpy as np
 import pytest
 
 from oracle import oracle as O
+from tolerance import assert_close
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
-
-REL_TOL = 1e-2
-
-
-def rel_err(got, ref):
-    return float(np.abs(np.asarray(got, np.float64) - ref).max() / max(np.abs(ref).max(), 1e-30))
-
 
 def bf16_tensor(a_u16):
     return torch.from_numpy(np.ascontiguousarray(a_u16).view(np.int16)).view(torch.bfloat16).cuda()
@@ -73,7 +68,7 @@ def test_tc_layer_matches_dequantised_reference(dtype, H, I, T):
     ids, ws = random_routing(rng, T, E, k, skew=1.1 if T > 50 else 0.0)
     got = run(layer, x, ids, ws)
     want = O.moe_forward_f32(O.bf16_to_f32(x).reshape(T, H), ids, ws, *d)
-    assert rel_err(got, want) < REL_TOL
+    assert_close(got, want)
 
 
 def test_tc_weight_zero_padding_and_bad_ids():
@@ -89,32 +84,42 @@ def test_tc_weight_zero_padding_and_bad_ids():
     assert np.array_equal(run(layer, x, pad_i, pad_w), base)
 
 
+def fast_stacks(rng, E, H, I, dtype, std=0.02):
+    """Quantised stacks (and FP8 block scales) of seeded N(0, std) weights, without dequantised copies."""
+    qs, ss = [], []
+    for shape in ((E, I, H), (E, I, H), (E, H, I)):
+        w = rng.standard_normal(shape, dtype=np.float32)
+        w *= np.float32(std)
+        q, s = O.quantize(dtype, w)
+        del w
+        qs.append(q)
+        ss.append(s)
+    return qs, ss
+
+
 def test_config3_shaped_q4k_prefill_chunk():
-    """the config-2 layer in Q4_K, a 512-token prefill chunk, Zipf(1.1) routing.
-    Checked on 24 sampled tokens against the dequantised reference."""
+    """the config-2 layer in Q4_K, a full 512-token prefill chunk, Zipf(1.1) routing,
+    every token against the dequantised reference."""
     rng = np.random.default_rng(3)
     E, k, H, I, T = 128, 8, 2048, 768, 512
-    q, s, d = quant_stacks(rng, E, H, I, O.DT_Q4_K)
+    q, s = fast_stacks(rng, E, H, I, O.DT_Q4_K)
     layer = build(q, s, E, k, H, I, O.DT_Q4_K, max_tokens=T)
     x = O.f32_to_bf16(rng.normal(0, 1, (T, H)).astype(np.float32))
     ids, ws = random_routing(rng, T, E, k, skew=1.1)
     got = run(layer, x, ids, ws)
-    sample = rng.choice(T, 24, replace=False)
-    xs = O.bf16_to_f32(x).reshape(T, H)[sample]
-    want = O.moe_forward_f32(xs, ids[sample].copy(), ws[sample].copy(), *d)
-    assert rel_err(got[sample], want) < REL_TOL
+    want = O.moe_forward_ref(O.DT_Q4_K, q, O.bf16_to_f32(x).reshape(T, H), ids, ws, E, H, I)
+    assert_close(got, want, what="config 3, 512-token chunk")
 
 
-def test_config5_shaped_fp8_layer():
-    """BASELINE config 5 shapes (H 7168, I 2048, FP8 e4m3 128x128) with 16 local experts, the per-GPU
-    expert count of a 16-way split; 96 tokens of top-8. Checked on 12 sampled tokens."""
+def test_config5_shaped_fp8_shard():
+    """BASELINE config 5 shapes (H 7168, I 2048, FP8 e4m3 128x128): one GPU's shard of an 8-way split,
+    32 local experts, 128 tokens of top-8; every token against the dequantised reference."""
     rng = np.random.default_rng(5)
-    E, k, H, I, T = 16, 8, 7168, 2048, 96
-    q, s, d = quant_stacks(rng, E, H, I, O.DT_FP8)
+    E, k, H, I, T = 32, 8, 7168, 2048, 128
+    q, s = fast_stacks(rng, E, H, I, O.DT_FP8)
     layer = build(q, s, E, k, H, I, O.DT_FP8, max_tokens=T)
     x = O.f32_to_bf16(rng.normal(0, 1, (T, H)).astype(np.float32))
     ids, ws = random_routing(rng, T, E, k)
     got = run(layer, x, ids, ws)
-    sample = rng.choice(T, 12, replace=False)
-    want = O.moe_forward_f32(O.bf16_to_f32(x).reshape(T, H)[sample], ids[sample].copy(), ws[sample].copy(), *d)
-    assert rel_err(got[sample], want) < REL_TOL
+    want = O.moe_forward_ref(O.DT_FP8, q, O.bf16_to_f32(x).reshape(T, H), ids, ws, E, H, I, scales=s)
+    assert_close(got, want, what="config 5, E32 shard")
