@@ -368,6 +368,34 @@ moe_status moe_ep_peer_check(moe_ep_peer* peer, void* stream);
  * launches issued after this call. No counterpart in the reference. */
 moe_status moe_ep_peer_set_wait_limit(moe_ep_peer* peer, int64_t timeout_us);
 
+/* ---- GGUF expert stacks (on-disk model files) ---------------------------------------------
+ * The reference reads its weights from GGUF shards through candle (src/load.rs:414-450) and hands
+ * the provider each MoE block's blk.{L}.ffn_{gate,up,down}_exps.weight as stacked [E, N, K] GGML
+ * tensors (provider.rs:367), sliced per expert by byte range (expert.rs:123-145). moe_gguf_open maps
+ * a GGUF v2/v3 file read-only and parses its header, metadata and tensor table (every read bounds-
+ * checked; a malformed file fails with MOE_ERR_INVALID and a message). Pointers it returns point
+ * into the mapping and stay valid until moe_gguf_close. */
+typedef struct moe_gguf moe_gguf;
+moe_status moe_gguf_open(const char* path, moe_gguf** out);
+void moe_gguf_close(moe_gguf* file);
+int moe_gguf_tensor_count(const moe_gguf* file);
+const char* moe_gguf_tensor_name(const moe_gguf* file, int i);
+/* A tensor by name: GGML type id, dims[4] (dims[0] fastest; unused dims 1), n_dims, its bytes in the
+ * mapping and their count (-1 for a type whose block size this library does not know). */
+moe_status moe_gguf_tensor(const moe_gguf* file, const char* name, int* ggml_type, int64_t* dims, int* n_dims,
+                           const void** data, int64_t* nbytes);
+/* Integer (or bool) metadata value; MOE_ERR_INVALID when absent or not an integer. */
+moe_status moe_gguf_get_int(const moe_gguf* file, const char* key, int64_t* value);
+/* String metadata value copied into buf (n bytes with the terminator); returns its length, 0 if absent. */
+size_t moe_gguf_get_str(const moe_gguf* file, const char* key, char* buf, size_t n);
+/* Fills desc from MoE layer `layer` of the file: num_experts, hidden, inter and wdtype from the
+ * expert stacks (Q8_0, Q4_K or BF16, one type for all three projections), gate/up/down as host
+ * pointers into the mapping (weights_on_device = 0), top_k from {general.architecture}.expert_used_count
+ * when present, and router_weight from blk.{L}.ffn_gate_inp.weight (bf16 as stored; f32 / f16
+ * converted to bf16 into memory the file object owns), NULL when the file has none. Other fields
+ * (device, max_tokens, router mode, cache_slots, ...) are left as the caller set them. */
+moe_status moe_gguf_layer_desc(moe_gguf* file, int layer, moe_layer_desc* desc);
+
 /* Library version string. */
 const char* moe_version(void);
 

@@ -10,9 +10,10 @@ from ._lib import (  # noqa: F401
     ROUTER_SOFTMAX, ROUTER_SOFTMAX_RENORM, lib,
 )
 from .layer import (  # noqa: F401
-    ExpertLoadContext, MoeConfig, RoutedExperts, RoutedExpertsProvider, plan_pairs, route_tokens,
+    ExpertLoadContext, MoeConfig, RoutedExperts, RoutedExpertsProvider, Router, plan_pairs, route_tokens,
 )
 from .ep import ExpertParallelMoE, PeerExpertParallelMoE, ep_combine, ep_dispatch, ep_pack_rows  # noqa: F401,E402
 from .doorbell import Ring  # noqa: F401,E402
 from .cpu import CpuExperts, Executor, add_f32_into_bf16, cpu_isa  # noqa: F401,E402
 from .paged import PagedMoE  # noqa: F401,E402
+from .gguf import GGUFFile  # noqa: F401,E402

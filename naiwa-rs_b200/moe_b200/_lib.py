@@ -136,6 +136,16 @@ def lib():
             "moe_ring_device_take": (i, [P, ctypes.c_uint32, P, ctypes.c_size_t, P]),
             "moe_ring_check": (i, [P, P]),
             "moe_ring_counters": (None, [P, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)]),
+            "moe_gguf_open": (i, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+            "moe_gguf_close": (None, [P]),
+            "moe_gguf_tensor_count": (i, [P]),
+            "moe_gguf_tensor_name": (ctypes.c_char_p, [P, i]),
+            "moe_gguf_tensor": (i, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int64),
+                                    ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_void_p),
+                                    ctypes.POINTER(ctypes.c_int64)]),
+            "moe_gguf_get_int": (i, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int64)]),
+            "moe_gguf_get_str": (ctypes.c_size_t, [P, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]),
+            "moe_gguf_layer_desc": (i, [P, i, ctypes.POINTER(LayerDesc)]),
             "moe_version": (ctypes.c_char_p, []),
         }
         for name, (res, args) in sigs.items():

@@ -215,11 +215,14 @@ class PeerExpertParallelMoE:
         self.shared_w = torch.ones((self.cap, 1), dtype=torch.float32, device=dev)
         self.shared_ids = torch.zeros((self.cap, 1), dtype=torch.int32, device=dev)
 
-    def forward(self, xs, topk_weights, topk_ids, out=None, stream=None):
+    def forward(self, xs, topk_weights, topk_ids, out=None, stream=None, layer=None, marks=None):
         """[T, H] bf16 of this rank's T <= max_tokens tokens, global ids [T, k]. Every rank calls it the
         same number of times, in the same order. The epoch is held on the device (epoch 0 in the C
         calls), so a captured graph of calls can be replayed; nothing is allocated but the output when
-        `out` is not given."""
+        `out` is not given. `layer` runs this call's local experts instead of the constructor's (one
+        exchange object can serve every layer of a stack: calls are ordered on the stream). `marks`:
+        five CUDA events recorded after the dispatch, the receive, the local forward, the return and
+        the combine (per-stage timing)."""
         torch = _torch()
         T, H = xs.shape
         if T > self.cap:
@@ -232,22 +235,32 @@ class PeerExpertParallelMoE:
         w = w.contiguous()
         P = self.plan
         L = lib()
+        local = layer if layer is not None else self.local
+
+        def mark(i):
+            if marks is not None:
+                marks[i].record(stream if stream is not None else torch.cuda.current_stream())
         check(L.moe_ep_dispatch_plan(_ptr(ids), _ptr(w), T, self.k, self.epr, self.world, _ptr(P["rank_counts"]),
                                      _ptr(P["n_send"]), _ptr(P["token_rows"]), _ptr(P["send_token"]),
                                      _ptr(P["send_ids"]), _ptr(P["send_w"]), _ptr(P["error_word"]), st))
         check(L.moe_ep_peer_dispatch(self._h, _ptr(xs), T, _ptr(P["rank_counts"]), _ptr(P["send_token"]),
                                      _ptr(P["send_ids"]), _ptr(P["send_w"]), 0, st))
+        mark(0)
         y_shared = None
         if self.shared is not None:
             y_shared = self.shared.forward(xs, self.shared_w[:T], self.shared_ids[:T], stream=stream)
         check(L.moe_ep_peer_receive(self._h, 0, _ptr(self.recv_ids), _ptr(self.recv_w), st))
+        mark(1)
         R = self.world * self.cap
-        check(L.moe_forward(self.local._h, ctypes.c_void_p(self.recv_rows), R, _ptr(self.recv_ids),
+        check(L.moe_forward(local._h, ctypes.c_void_p(self.recv_rows), R, _ptr(self.recv_ids),
                             _ptr(self.recv_w), self.k, _ptr(self.y_local), st))
+        mark(2)
         check(L.moe_ep_peer_return(self._h, _ptr(self.y_local), 0, st))
+        mark(3)
         y = out if out is not None else torch.empty((T, H), dtype=torch.bfloat16, device=xs.device)
         check(L.moe_ep_peer_combine(self._h, 0, T, _ptr(P["rank_counts"]), _ptr(P["token_rows"]),
                                     _ptr(y_shared), _ptr(y), st))
+        mark(4)
         return y
 
     __call__ = forward

@@ -284,6 +284,36 @@ def route_tokens(x, w_router, k: int, mode: int, bias=None, n_group: int = 1, to
     return ids, w
 
 
+class Router:
+    """The router of one MoE block on its own (the gate linear + top-k upstream of RoutedExperts.forward),
+    for callers whose experts are not one local layer: an expert-parallel rank routes its tokens over
+    all experts while holding only its share. Holds the gate, the bias and a workspace sized for
+    max_tokens, so each call allocates nothing (and can be captured in a CUDA graph)."""
+
+    def __init__(self, w_router, k: int, mode: int, max_tokens: int, bias=None, n_group: int = 1,
+                 topk_group: int = 1, routed_scale: float = 1.0):
+        torch = _torch()
+        self.w = w_router.contiguous()
+        self.E, self.H = self.w.shape
+        self.k, self.mode, self.bias = int(k), int(mode), bias
+        self.n_group, self.topk_group, self.scale = int(n_group), int(topk_group), float(routed_scale)
+        self.max_tokens = int(max_tokens)
+        self.ws_bytes = int(lib().moe_route_workspace_bytes(self.max_tokens, self.E))
+        self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=self.w.device)  # counters start at 0
+
+    def route(self, x, out_ids=None, out_weights=None, stream=None):
+        torch = _torch()
+        T = x.shape[0]
+        if T > self.max_tokens:
+            raise MoeError(_lib.MOE_ERR_INVALID, "Router.route: T exceeds max_tokens")
+        ids = out_ids if out_ids is not None else torch.empty((T, self.k), dtype=torch.int32, device=x.device)
+        w = out_weights if out_weights is not None else torch.empty((T, self.k), dtype=torch.float32, device=x.device)
+        check(lib().moe_route_tokens(_ptr(x), _ptr(self.w), _ptr(self.bias), T, self.H, self.E, self.k, self.mode,
+                                     self.n_group, self.topk_group, self.scale, _ptr(ids), _ptr(w), _ptr(self.ws),
+                                     self.ws_bytes, ctypes.c_void_p(_stream(stream))))
+        return ids, w
+
+
 def plan_pairs(ids, num_experts: int, stream=None):
     """Histogram + stable permutation of routed pairs -> (counts, offsets, perm, active, error_word)."""
     torch = _torch()

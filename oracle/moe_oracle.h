@@ -84,6 +84,12 @@ int orc_fused_moe_decode_q8_0(const uint8_t* gate, const uint8_t* up, const uint
                               const uint32_t* ids, const float* w, int T, int k, int E, int H, int I,
                               int n_threads, float* y);
 
+/* ---- timed CPU baseline, fast restatement (cpu_baseline.c): same result as
+ * orc_fused_moe_decode_q8_0 up to summation order; AVX2, persistent thread pool ------------------ */
+int orc_baseline_decode_q8_0(const uint8_t* gate, const uint8_t* up, const uint8_t* down, const float* x,
+                             const uint32_t* ids, const float* w, int T, int k, int E, int H, int I, int n_threads,
+                             float* y);
+
 #ifdef __cplusplus
 }
 #endif

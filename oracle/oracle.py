@@ -31,7 +31,7 @@ def build() -> str:
 def lib():
     global _lib
     if _lib is None:
-        srcs = [os.path.join(_HERE, f) for f in ("moe_oracle.c", "moe_oracle.h", "Makefile")]
+        srcs = [os.path.join(_HERE, f) for f in ("moe_oracle.c", "cpu_baseline.c", "moe_oracle.h", "Makefile")]
         if not os.path.exists(_LIB_PATH) or any(
                 os.path.exists(f) and os.path.getmtime(f) > os.path.getmtime(_LIB_PATH) for f in srcs):
             build()
@@ -67,6 +67,7 @@ def lib():
             "orc_moe_forward_f32": (None, [P, P, P, i, i, i, i, i, P, P, P, P]),
             "orc_moe_forward_ref": (i, [i, P, P, P, P, P, P, P, P, P, i, i, i, i, i, i, P]),
             "orc_fused_moe_decode_q8_0": (i, [P, P, P, P, P, P, i, i, i, i, i, i, P]),
+            "orc_baseline_decode_q8_0": (i, [P, P, P, P, P, P, i, i, i, i, i, i, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -301,6 +302,21 @@ def fused_moe_decode_q8_0(gate_q, up_q, down_q, x, ids, w, E, H, I, threads):
                                          threads, _p(y))
     if rc != 0:
         raise ValueError("fused decode: bad arguments")
+    return y
+
+
+def baseline_decode_q8_0(gate_q, up_q, down_q, x, ids, w, E, H, I, threads):
+    """The timed CPU baseline (cpu_baseline.c): fused_moe_decode_q8_0's result, vectorised, with each
+    active expert's weights read once per call."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    ids = np.ascontiguousarray(ids, dtype=np.uint32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    T, k = ids.shape
+    y = np.empty((T, H), dtype=np.float32)
+    rc = lib().orc_baseline_decode_q8_0(_p(gate_q), _p(up_q), _p(down_q), _p(x), _p(ids), _p(w), T, k, E, H, I,
+                                        threads, _p(y))
+    if rc != 0:
+        raise ValueError("baseline decode: bad arguments")
     return y
 
 

@@ -267,3 +267,22 @@ def test_fused_cpu_decode_matches_dequantised_reference():
     # a swapped weight moves the output far beyond the tolerance (the test has teeth)
     bad = O.moe_forward_f32(x, ids, ws[:, ::-1].copy(), gd, ud, dd)
     assert np.abs(bad - want).max() > 0.1
+
+
+# ---- the timed CPU baseline (oracle/cpu_baseline.c) against the strict-order oracle ---------------
+
+@pytest.mark.parametrize("T", [1, 5, 33])
+def test_cpu_baseline_matches_strict_oracle(T):
+    """bench.py's reference arm times orc_baseline_decode_q8_0; it must compute the strict oracle's
+    fused decode (up to f32 summation order), including weight-0 slots and a repeated expert."""
+    rng = np.random.default_rng(40 + T)
+    E, k, H, I = 16, 4, 256, 128
+    q = [O.quantize(O.DT_Q8_0, rng.normal(0, 0.02, s).astype(np.float32))[0] for s in ((E, I, H), (E, I, H), (E, H, I))]
+    x = rng.normal(0, 1, (T, H)).astype(np.float32)
+    ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.uint32)
+    w = rng.dirichlet(np.ones(k), T).astype(np.float32)
+    w[0, -1] = 0.0           # weight-0 padding is skipped
+    ids[-1, 1] = ids[-1, 0]  # a repeated expert: one pair, the weights summed
+    want = O.fused_moe_decode_q8_0(q[0], q[1], q[2], x, ids, w, E, H, I, 2)
+    got = O.baseline_decode_q8_0(q[0], q[1], q[2], x, ids, w, E, H, I, 3)
+    assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
