@@ -975,8 +975,11 @@ def run_stack(args):
         cpu = M.CpuExperts(E, K_TOP, H, I, M.DTYPE_Q8_0, g, u, d, threads=ncpu)
         layer.cache_upload(range(SLOTS))  # the fill thread's first pass
         layers.append(layer)
-        paged.append(M.PagedMoE(layer, cpu=cpu, pcie_frac=1.0, max_tokens=SEQS))
+        paged.append(M.PagedMoE(layer, cpu=cpu, pcie_frac=args.pcie_frac, max_tokens=SEQS, staging_slots=16,
+                                lookahead=not args.no_lookahead))
         del g, u, d
+    for a, b in zip(paged, paged[1:]):  # each layer's activation predicts the next layer's experts
+        a.set_next(b)
     torch.cuda.synchronize()
     gen = torch.Generator(device=dev)
     gen.manual_seed(44)
@@ -1012,6 +1015,9 @@ def run_stack(args):
     pairs = sum(p.stats["pairs"] - b["pairs"] for p, b in zip(paged, base_p))
     hits = sum(p.stats["hits"] - b["hits"] for p, b in zip(paged, base_p))
     cpu_pairs = sum(p.stats["cpu_pairs"] - b["cpu_pairs"] for p, b in zip(paged, base_p))
+    delta = {key: sum(p.stats[key] - b[key] for p, b in zip(paged, base_p))
+             for key in ("staged_pairs", "staged_experts", "lookahead_passes", "lookahead_loads", "lookahead_swaps",
+                         "lookahead_dropped", "predicted")}
     p50 = stats_mod.median(times) * 1e3
     print(json.dumps({
         "metric": "p50 TPOT (ms) of a 32-sequence decode step through a 48-layer MoE stack with a 25% expert cache",
@@ -1024,8 +1030,13 @@ def run_stack(args):
                                "in pinned host memory; 32 sequences per decode step, residual stream "
                                "x += moe(rmsnorm(x)) carried across steps",
                    "layers": L, "cache_slots": SLOTS, "sequences": SEQS, "cpu_threads": ncpu,
-                   "miss_policy": "streamed_misses(frac 1.0, cap 32) into free LRU slots, the rest on the CPU"},
+                   "miss_policy": f"streamed_misses(frac {args.pcie_frac}, cap 16) into 16 staging slots per layer, "
+                                  "resident experts first; the rest on the CPU executor",
+                   "lookahead": ("off" if args.no_lookahead else
+                                 "each layer's activation predicts the next layer's experts on the lookahead thread "
+                                 "(CPU router, union by votes, 1 swap per row)")},
         "tokens_per_s": SEQS / (p50 / 1e3), "hit_rate": hits / max(pairs, 1), "cpu_pair_share": cpu_pairs / max(pairs, 1),
+        "staged_pair_share": delta["staged_pairs"] / max(pairs, 1), "paged_stats": delta,
         "h2d_gbs": up_bytes / sum(times) / 1e9, "p90_ms": sorted(times)[int(0.9 * (len(times) - 1))] * 1e3,
         "e2e": {"value": p50, "unit": "ms", "h2d_bytes_per_step": up_bytes // max(len(times), 1),
                 "d2h_bytes_per_step": 0},
@@ -1046,6 +1057,9 @@ def main():
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--pcie-frac", type=float, default=1.0,
+                    help="stack workload: share of each call's missed experts streamed into staging slots")
+    ap.add_argument("--no-lookahead", action="store_true", help="stack workload: no next-layer prefetch")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the nested config-3 prefill record of the default (decode) run")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep", "stack"],

@@ -368,6 +368,54 @@ moe_status moe_ep_peer_check(moe_ep_peer* peer, void* stream);
  * launches issued after this call. No counterpart in the reference. */
 moe_status moe_ep_peer_set_wait_limit(moe_ep_peer* peer, int64_t timeout_us);
 
+/* ---- paged decode and prefill through an expert cache ---------------------------------------
+ * Replaces the reference's CachedLayer call path: the decode split of one layer call between resident
+ * slots, streamed misses and the CPU (src/moe/decode.rs:224-378, stages/route.rs:19-158,
+ * stages/dma_miss.rs:80-160, stages/cpu_miss.rs:21-54, staging.rs:23-183), the lookahead prefetch of
+ * the next layer's predicted experts (stages/preload.rs:18-195, cached_layer.rs:1236-1337) and the
+ * ring-batched, upload-overlapped prefill (rings.rs:68-156, prefill_stream.rs:1066, :1362-1694).
+ * One moe_paged per cached layer (cache_slots > 0); calls on one layer come from one host thread, on
+ * one stream. A process-wide lookahead thread runs the predictions: it reads a layer's router on the
+ * host and enqueues copies on that layer's copy stream; every forward of the layer waits for them. */
+typedef struct moe_paged moe_paged;
+typedef struct {
+  int staging_slots;       /* device slots past the cache slots for streamed misses and prefill waves (16) */
+  float pcie_frac;         /* streamed_misses fraction of the missed experts copied per call (1.0) */
+  int stream_cap;          /* at most this many experts streamed per call, <= staging_slots (16) */
+  int lookahead;           /* 1: predict and prefetch the next layer (moe_paged_set_next) from each call's activation */
+  int lookahead_swaps;     /* slots a prediction may take from other experts, per activation row (1) */
+  int max_tokens;          /* largest T of one moe_paged_forward (<= the layer's max_tokens) (256) */
+  int64_t host_timeout_us; /* how long the host waits for the router's top-k and the CPU rows (5 s) */
+} moe_paged_opts;
+typedef struct {
+  int64_t calls, pairs, hits, staged_experts, staged_pairs, cpu_pairs;
+  int64_t lookahead_passes, lookahead_loads, lookahead_swaps, lookahead_dropped, lookahead_errors, predicted;
+  int64_t prefill_calls, prefill_waves, prefill_uploads;
+} moe_paged_stats;
+void moe_paged_default_opts(moe_paged_opts* opts);
+/* cpu: the CPU expert path for misses that are not streamed (NULL: every miss must fit the staging
+ * slots). opts NULL: the defaults. Reserves the staging slots in the layer (synchronises the device). */
+moe_status moe_paged_create(moe_layer* layer, moe_cpu_experts* cpu, const moe_paged_opts* opts, moe_paged** out);
+void moe_paged_destroy(moe_paged* paged);
+/* The layer whose experts this layer's calls predict (the next MoE layer of the model), or NULL. */
+moe_status moe_paged_set_next(moe_paged* paged, moe_paged* next);
+/* RoutedExperts::forward through the cache: x, y [T, H] bf16 device, ids/weights [T, width] device,
+ * width <= 2 * top_k. Waits on the host for this call's top-k (behind the router only). */
+moe_status moe_paged_forward(moe_paged* paged, const void* x, int T, const uint32_t* ids, const float* weights,
+                             int width, void* y, void* stream);
+/* A prompt through the cache: chunks of the layer's scratch; per chunk the resident experts first,
+ * then the missing ones in waves of staging_slots / 2, balanced by routed pairs, each wave's upload
+ * overlapping the previous wave's compute; the waves' outputs summed in f32, rounded once. */
+moe_status moe_paged_prefill(moe_paged* paged, const void* x, int T, const uint32_t* ids, const float* weights,
+                             int width, void* y, void* stream);
+/* Fills empty cache slots with the most-routed experts not resident (fill_candidate), now. */
+moe_status moe_paged_fill(moe_paged* paged, void* stream);
+moe_status moe_paged_get_stats(moe_paged* paged, moe_paged_stats* out);
+/* Waits until the lookahead thread has no queued or running prediction. */
+moe_status moe_paged_drain_lookahead(void);
+/* Synchronises `stream`; reports latched errors of the layer, its rings, its CPU jobs and its lookahead. */
+moe_status moe_paged_check(moe_paged* paged, void* stream);
+
 /* ---- GGUF expert stacks (on-disk model files) ---------------------------------------------
  * The reference reads its weights from GGUF shards through candle (src/load.rs:414-450) and hands
  * the provider each MoE block's blk.{L}.ffn_{gate,up,down}_exps.weight as stacked [E, N, K] GGML

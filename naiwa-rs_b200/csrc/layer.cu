@@ -13,7 +13,7 @@
 
 #include <vector>
 
-#include "moe_internal.cuh"
+#include "layer_internal.cuh"
 #include <cmath>
 
 namespace moe {
@@ -46,72 +46,6 @@ moe_status cuda_fail(cudaError_t e, const char* what) {
 }  // namespace moe
 
 using namespace moe;
-
-struct moe_layer {
-  moe_layer_desc d{};
-  int dev = 0;
-  int sms = 148;
-  // weights (device layout)
-  uint8_t* gu_q = nullptr;
-  uint8_t* gu_s = nullptr;
-  uint8_t* dn_q = nullptr;
-  uint8_t* dn_s = nullptr;
-  int64_t gu_q_stride = 0, gu_s_stride = 0, dn_q_stride = 0, dn_s_stride = 0;
-  __nv_bfloat16* router_w = nullptr;
-  float* router_b = nullptr;
-  // scratch
-  int cap_pairs = 0;
-  int cap_tokens = 0;
-  int32_t* counts = nullptr;
-  int32_t* offsets = nullptr;
-  int32_t* perm = nullptr;
-  int32_t* active = nullptr;
-  int32_t* n_active = nullptr;
-  int32_t* err = nullptr;
-  void* plan_ws = nullptr;
-  size_t plan_ws_bytes = 0;
-  float* h = nullptr;
-  float* ypair = nullptr;
-  void* route_ws = nullptr;
-  size_t route_ws_bytes = 0;
-  // tensor-core path (Q4_K / FP8 / Q8_0 at 128-multiples): tile-major weights, f16 staging, TMA maps
-  bool tc = false;
-  bool q8_tiles = false;  // Q8_0 in units: GEMV or tcgen05 per call (q8_uses_gemm)
-  float* gu_scale = nullptr;
-  float* dn_scale = nullptr;
-  void* x16 = nullptr;
-  float* xscale = nullptr;
-  void* h16 = nullptr;
-  float* hscale = nullptr;
-  int32_t* tile_list = nullptr;
-  int32_t* n_tiles = nullptr;
-  alignas(128) unsigned char tmap_x[128];
-  alignas(128) unsigned char tmap_h[128];
-  int64_t weight_bytes = 0;
-  int64_t scratch_bytes = 0;
-  // expert cache (cache_slots > 0): every expert in pinned host memory in the device layout, `slots`
-  // of them in the device banks above; slot_of maps expert -> slot (-1: not resident)
-  int slots = 0;
-  uint8_t* hs_gu_q = nullptr;
-  uint8_t* hs_gu_s = nullptr;
-  uint8_t* hs_dn_q = nullptr;
-  uint8_t* hs_dn_s = nullptr;
-  float* hs_gu_scale = nullptr;
-  float* hs_dn_scale = nullptr;
-  int64_t gu_scale_stride = 0, dn_scale_stride = 0;  // floats per expert (tensor-core FP8 scales)
-  int32_t* slot_of = nullptr;                         // device [E]
-  std::vector<int> slot_expert;                       // [slots], -1 empty
-  std::vector<uint64_t> last_use;                     // [slots]
-  std::vector<int> slot_of_host;                      // [E]
-  std::vector<uint64_t> hit_counts;                   // [E] routed pairs seen per expert
-  uint64_t tick = 0;
-  cudaStream_t copy_stream = nullptr;
-  cudaEvent_t last_read = nullptr;    // recorded after every forward: the slots' readers
-  cudaEvent_t copies_done = nullptr;  // recorded after the latest uploads
-  bool copies_pending = false;
-  int64_t stat_hits = 0, stat_misses = 0, stat_uploads = 0, stat_upload_bytes = 0;
-};
-
 
 static void free_scratch(moe_layer* L) {
   cudaFree(L->counts);
@@ -191,15 +125,15 @@ static moe_status alloc_scratch(moe_layer* L, int max_tokens) {
   return MOE_OK;
 }
 
-// Device slot-map edits carried in the launch arguments (no host buffer to race with).
-struct SlotEdits {
-  int n;
-  int expert[64];
-  int slot[64];
-};
-
 __global__ void slot_edit_kernel(int32_t* __restrict__ slot_of, SlotEdits ed) {
   if ((int)threadIdx.x < ed.n) slot_of[ed.expert[threadIdx.x]] = ed.slot[threadIdx.x];
+}
+
+moe_status moe::launch_slot_edits(int32_t* slot_of, const SlotEdits& ed, cudaStream_t st) {
+  if (ed.n <= 0) return MOE_OK;
+  slot_edit_kernel<<<1, 64, 0, st>>>(slot_of, ed);
+  MOE_CUDA_TRY(cudaGetLastError());
+  return MOE_OK;
 }
 
 static void free_cache(moe_layer* L) {
@@ -258,6 +192,7 @@ static moe_status setup_cache(moe_layer* L, int64_t* acct) {
   MOE_CUDA_TRY(cudaEventCreateWithFlags(&L->last_read, cudaEventDisableTiming));
   MOE_CUDA_TRY(cudaEventCreateWithFlags(&L->copies_done, cudaEventDisableTiming));
   L->slot_expert.assign(S, -1);
+  L->slot_state.assign(S, SLOT_EMPTY);
   L->last_use.assign(S, 0);
   L->slot_of_host.assign(E, -1);
   L->hit_counts.assign(E, 0);
@@ -468,7 +403,7 @@ static int pick_rowt(int tiles, int tpp, double est_active, int sms) {
 }
 
 static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_t* ids, const float* weights,
-                               int width, void* y, void* stream, void* const* events);
+                               int width, void* y, void* stream, void* const* events, bool combine = true);
 
 // A Q8_0 unit-layout layer runs the tcgen05 GEMM once the batch averages 8 or more tokens per
 // expert (below that the GEMV streams the weights faster: it splits K across warps, so few experts
@@ -511,11 +446,11 @@ static moe_status mark(void* const* events, int i, cudaStream_t st) {
 }
 
 static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_t* ids, const float* weights,
-                               int width, void* y, void* stream, void* const* events) {
+                               int width, void* y, void* stream, void* const* events, bool combine) {
   if (!L) return fail(MOE_ERR_INVALID, "moe_forward: null layer");
   if (T < 0 || width <= 0) return fail(MOE_ERR_INVALID, "moe_forward: need T >= 0 and width > 0");
   if (T == 0) return MOE_OK;
-  if (!x || !ids || !weights || !y) return fail(MOE_ERR_INVALID, "moe_forward: null pointer");
+  if (!x || !ids || !weights || (combine && !y)) return fail(MOE_ERR_INVALID, "moe_forward: null pointer");
   if ((uintptr_t)x & 15) return fail(MOE_ERR_INVALID, "moe_forward: x must be 16-byte aligned");
   if (((uintptr_t)ids | (uintptr_t)weights) & 3)
     return fail(MOE_ERR_INVALID, "moe_forward: ids and weights must be 4-byte aligned");
@@ -529,9 +464,12 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   const int n_pairs = (int)n64;
   const int E = L->d.num_experts, H = L->d.hidden, I = L->d.inter;
   const int32_t* slot_of = L->slots ? L->slot_of : nullptr;
-  if (L->slots && L->copies_pending) {  // uploads issued since the last forward land first
-    MOE_CUDA_TRY(cudaStreamWaitEvent(st, L->copies_done, 0));
-    L->copies_pending = false;
+  if (L->slots) {  // uploads issued since the last forward land first
+    std::lock_guard<std::recursive_mutex> lock(L->cache_mu);
+    if (L->copies_pending) {
+      MOE_CUDA_TRY(cudaStreamWaitEvent(st, L->copies_done, 0));
+      L->copies_pending = false;
+    }
   }
   PlanOut po{L->counts, L->offsets, L->perm, L->active, L->n_active, L->err, slot_of};
   MOE_TRY(mark(events, 0, st));
@@ -580,7 +518,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
     da.tmap = L->tmap_h;
     MOE_TRY(tc_gemm(w, da, st));
     MOE_TRY(mark(events, 3, st));
-    MOE_TRY(launch_combine(L->ypair, ids, T, width, H, E, y, st, slot_of));
+    if (combine) MOE_TRY(launch_combine(L->ypair, ids, T, width, H, E, y, st, slot_of));
     if (L->slots) MOE_CUDA_TRY(cudaEventRecord(L->last_read, st));  // the slots' readers
     return mark(events, 4, st);
   }
@@ -627,7 +565,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   dp.out = L->ypair;
   MOE_TRY(launch_expert_gemv(L->d.wdtype, dp, max_active, rowt_of(dp), st));
   MOE_TRY(mark(events, 3, st));
-  MOE_TRY(launch_combine(L->ypair, ids, T, width, H, E, y, st, slot_of));
+  if (combine) MOE_TRY(launch_combine(L->ypair, ids, T, width, H, E, y, st, slot_of));
   if (L->slots) MOE_CUDA_TRY(cudaEventRecord(L->last_read, st));  // the slots' readers
   return mark(events, 4, st);
 }
@@ -703,6 +641,7 @@ moe_status moe_cache_split(moe_layer* L, const uint32_t* ids, int n_pairs, uint8
   for (int p = 0; p < n_pairs; ++p)
     if (ids[p] != MOE_ID_NONE && ids[p] >= (uint32_t)E)
       return fail(MOE_ERR_BAD_IDS, "moe_cache_split: routed expert id " + std::to_string(ids[p]) + " >= num_experts");
+  std::lock_guard<std::recursive_mutex> lock(L->cache_mu);
   const uint64_t tick = ++L->tick;
   for (int p = 0; p < n_pairs; ++p) {
     const uint32_t id = ids[p];
@@ -712,7 +651,7 @@ moe_status moe_cache_split(moe_layer* L, const uint32_t* ids, int n_pairs, uint8
     }
     L->hit_counts[id] += 1;
     const int s = L->slot_of_host[id];
-    if (s >= 0) {
+    if (s >= 0 && L->slot_state[s] == SLOT_PUBLISHED) {  // a slot still loading is a miss
       L->last_use[s] = tick;
       hit[p] = 1;
       ++L->stat_hits;
@@ -736,22 +675,21 @@ moe_status moe_cache_upload(moe_layer* L, const uint32_t* experts, int n, const 
     if (experts[i] >= (uint32_t)E) return fail(MOE_ERR_BAD_IDS, "moe_cache_upload: expert id >= num_experts");
   DeviceGuard guard(L->dev);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  std::lock_guard<std::recursive_mutex> lock(L->cache_mu);
   // experts to keep: the caller's protect list and everything this call brings in
   std::vector<int> keep;
   keep.reserve((size_t)(n + n_protect));
   for (int i = 0; i < n_protect; ++i)
     if (protect[i] < (uint32_t)E) keep.push_back((int)protect[i]);
   for (int i = 0; i < n; ++i) keep.push_back((int)experts[i]);
-  std::vector<int> published(L->slots, 1);
+  std::vector<int> published(L->slots);  // a slot still loading (lookahead pass) is never a victim
+  for (int s = 0; s < L->slots; ++s) published[s] = L->slot_state[s] == SLOT_PUBLISHED;
   SlotEdits ed{};
   bool waited = false;
   int loaded = 0;
   auto flush = [&]() -> moe_status {
-    if (ed.n) {
-      slot_edit_kernel<<<1, 64, 0, st>>>(L->slot_of, ed);
-      MOE_CUDA_TRY(cudaGetLastError());
-      ed.n = 0;
-    }
+    MOE_TRY(launch_slot_edits(L->slot_of, ed, st));
+    ed.n = 0;
     return MOE_OK;
   };
   for (int i = 0; i < n; ++i) {
@@ -769,6 +707,7 @@ moe_status moe_cache_upload(moe_layer* L, const uint32_t* experts, int n, const 
                                    (int)keep.size(), &victim);
       if (slot < 0) break;  // every slot holds an expert this call needs
       L->slot_of_host[victim] = -1;
+      published[slot] = 0;
       if (ed.n == 64) MOE_TRY(flush());
       ed.expert[ed.n] = victim;
       ed.slot[ed.n++] = -1;
@@ -777,28 +716,15 @@ moe_status moe_cache_upload(moe_layer* L, const uint32_t* experts, int n, const 
       MOE_CUDA_TRY(cudaStreamWaitEvent(L->copy_stream, L->last_read, 0));
       waited = true;
     }
-    auto copy = [&](void* bank, const void* store, int64_t stride) -> moe_status {
-      if (!bank || !stride) return MOE_OK;
-      MOE_CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(bank) + (int64_t)slot * stride,
-                                   static_cast<const uint8_t*>(store) + (int64_t)e * stride, (size_t)stride,
-                                   cudaMemcpyHostToDevice, L->copy_stream));
-      L->stat_upload_bytes += stride;
-      return MOE_OK;
-    };
-    MOE_TRY(copy(L->gu_q, L->hs_gu_q, L->gu_q_stride));
-    MOE_TRY(copy(L->gu_s, L->hs_gu_s, L->gu_s_stride));
-    MOE_TRY(copy(L->dn_q, L->hs_dn_q, L->dn_q_stride));
-    MOE_TRY(copy(L->dn_s, L->hs_dn_s, L->dn_s_stride));
-    MOE_TRY(copy(L->gu_scale, L->hs_gu_scale, L->gu_scale_stride * 4));
-    MOE_TRY(copy(L->dn_scale, L->hs_dn_scale, L->dn_scale_stride * 4));
+    MOE_TRY(cache_copy_expert(L, e, slot));
     L->slot_expert[slot] = e;
+    L->slot_state[slot] = SLOT_PUBLISHED;  // copies_done covers it: the next forward waits on it
     L->last_use[slot] = L->tick;
     L->slot_of_host[e] = slot;
     if (ed.n == 64) MOE_TRY(flush());
     ed.expert[ed.n] = e;
     ed.slot[ed.n++] = slot;
     ++loaded;
-    ++L->stat_uploads;
   }
   if (loaded) {
     MOE_CUDA_TRY(cudaEventRecord(L->copies_done, L->copy_stream));
@@ -811,6 +737,7 @@ moe_status moe_cache_upload(moe_layer* L, const uint32_t* experts, int n, const 
 
 int moe_cache_slots(const moe_layer* L, int32_t* slot_expert) {
   if (!L || !L->slots) return 0;
+  std::lock_guard<std::recursive_mutex> lock(const_cast<moe_layer*>(L)->cache_mu);
   if (slot_expert)
     for (int s = 0; s < L->slots; ++s) slot_expert[s] = L->slot_expert[s];
   return L->slots;
@@ -819,6 +746,7 @@ int moe_cache_slots(const moe_layer* L, int32_t* slot_expert) {
 moe_status moe_cache_stats(const moe_layer* L, int64_t* hits, int64_t* misses, int64_t* uploads,
                            int64_t* upload_bytes, uint64_t* hit_counts) {
   if (!L) return fail(MOE_ERR_INVALID, "moe_cache_stats: null layer");
+  std::lock_guard<std::recursive_mutex> lock(const_cast<moe_layer*>(L)->cache_mu);
   if (hits) *hits = L->stat_hits;
   if (misses) *misses = L->stat_misses;
   if (uploads) *uploads = L->stat_uploads;
@@ -844,4 +772,78 @@ extern "C" moe_status moe_forward_chunked(moe_layer* L, const void* x, int T, co
                          stream, nullptr));
   }
   return MOE_OK;
+}
+
+// ---- cache internals shared with the paged runtime -------------------------------------------------
+
+moe_status moe::cache_copy_expert(moe_layer* L, int e, int slot) {
+  auto copy = [&](void* bank, const void* store, int64_t stride) -> moe_status {
+    if (!bank || !stride) return MOE_OK;
+    MOE_CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(bank) + (int64_t)slot * stride,
+                                 static_cast<const uint8_t*>(store) + (int64_t)e * stride, (size_t)stride,
+                                 cudaMemcpyHostToDevice, L->copy_stream));
+    L->stat_upload_bytes += stride;
+    return MOE_OK;
+  };
+  MOE_TRY(copy(L->gu_q, L->hs_gu_q, L->gu_q_stride));
+  MOE_TRY(copy(L->gu_s, L->hs_gu_s, L->gu_s_stride));
+  MOE_TRY(copy(L->dn_q, L->hs_dn_q, L->dn_q_stride));
+  MOE_TRY(copy(L->dn_s, L->hs_dn_s, L->dn_s_stride));
+  MOE_TRY(copy(L->gu_scale, L->hs_gu_scale, L->gu_scale_stride * 4));
+  MOE_TRY(copy(L->dn_scale, L->hs_dn_scale, L->dn_scale_stride * 4));
+  ++L->stat_uploads;
+  return MOE_OK;
+}
+
+moe_status moe::cache_reserve_staging(moe_layer* L, int n) {
+  if (!L->slots) return fail(MOE_ERR_INVALID, "staging slots need a layer with an expert cache");
+  if (n <= L->staging) return MOE_OK;
+  DeviceGuard guard(L->dev);
+  MOE_CUDA_TRY(cudaDeviceSynchronize());
+  const int old_total = L->slots + L->staging, total = L->slots + n;
+  int64_t acct = L->weight_bytes;
+  auto grow = [&](uint8_t** bank, int64_t stride) -> moe_status {
+    if (!*bank || !stride) return MOE_OK;
+    uint8_t* nb = nullptr;
+    cudaError_t e = cudaMalloc(&nb, (size_t)(stride * total));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(staging slots)");
+    e = cudaMemcpy(nb, *bank, (size_t)(stride * old_total), cudaMemcpyDeviceToDevice);
+    if (e != cudaSuccess) {
+      cudaFree(nb);
+      return cuda_fail(e, "cudaMemcpy(staging slots)");
+    }
+    cudaFree(*bank);
+    *bank = nb;
+    acct += stride * (total - old_total);
+    return MOE_OK;
+  };
+  MOE_TRY(grow(&L->gu_q, L->gu_q_stride));
+  MOE_TRY(grow(&L->gu_s, L->gu_s_stride));
+  MOE_TRY(grow(&L->dn_q, L->dn_q_stride));
+  MOE_TRY(grow(&L->dn_s, L->dn_s_stride));
+  uint8_t* gs = reinterpret_cast<uint8_t*>(L->gu_scale);
+  uint8_t* ds = reinterpret_cast<uint8_t*>(L->dn_scale);
+  MOE_TRY(grow(&gs, L->gu_scale_stride * 4));
+  MOE_TRY(grow(&ds, L->dn_scale_stride * 4));
+  L->gu_scale = reinterpret_cast<float*>(gs);
+  L->dn_scale = reinterpret_cast<float*>(ds);
+  L->staging = n;
+  L->weight_bytes = acct;
+  return MOE_OK;
+}
+
+moe_status moe::layer_forward(moe_layer* L, const void* x, int T, const uint32_t* ids, const float* weights, int width,
+                              void* y, cudaStream_t st) {
+  return forward_impl(L, x, T, ids, weights, width, y, st, nullptr);
+}
+
+moe_status moe::layer_experts(moe_layer* L, const void* x, int T, const uint32_t* ids, const float* weights, int width,
+                              cudaStream_t st) {
+  return forward_impl(L, x, T, ids, weights, width, nullptr, st, nullptr, false);
+}
+
+moe_status moe::layer_combine(moe_layer* L, int T, const uint32_t* ids, int width, void* y, cudaStream_t st) {
+  if ((int64_t)T * width > L->cap_pairs) return fail(MOE_ERR_INVALID, "layer_combine: T * width exceeds the scratch");
+  DeviceGuard guard(L->dev);
+  return launch_combine(L->ypair, ids, T, width, L->d.hidden, L->d.num_experts, y, st, L->slots ? L->slot_of : nullptr);
 }

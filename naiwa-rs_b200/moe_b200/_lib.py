@@ -136,6 +136,16 @@ def lib():
             "moe_ring_device_take": (i, [P, ctypes.c_uint32, P, ctypes.c_size_t, P]),
             "moe_ring_check": (i, [P, P]),
             "moe_ring_counters": (None, [P, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)]),
+            "moe_paged_default_opts": (None, [P]),
+            "moe_paged_create": (i, [P, P, P, ctypes.POINTER(ctypes.c_void_p)]),
+            "moe_paged_destroy": (None, [P]),
+            "moe_paged_set_next": (i, [P, P]),
+            "moe_paged_forward": (i, [P, P, i, P, P, i, P, P]),
+            "moe_paged_prefill": (i, [P, P, i, P, P, i, P, P]),
+            "moe_paged_fill": (i, [P, P]),
+            "moe_paged_get_stats": (i, [P, P]),
+            "moe_paged_drain_lookahead": (i, []),
+            "moe_paged_check": (i, [P, P]),
             "moe_gguf_open": (i, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
             "moe_gguf_close": (None, [P]),
             "moe_gguf_tensor_count": (i, [P]),

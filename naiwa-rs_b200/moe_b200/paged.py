@@ -1,157 +1,126 @@
-"""Decode through an expert cache: the reference's split of one MoE layer call between resident GPU
-slots, PCIe-streamed misses and the CPU.
+"""Decode and prefill through an expert cache: the reference's CachedLayer call path (libmoe_b200's
+moe_paged_*, csrc/paged.cu).
 
 Reference flow (naiwa-rs src/moe/decode.rs:224-378, stages/route.rs:19-158, stages/dma_miss.rs,
-stages/cpu_miss.rs): the router's top-k reach the host thread through the top-k doorbell (no stream
-sync), the route split marks each pair resident or missed, `streamed_misses` picks the missed
-experts worth uploading now, the rest run on the CPU from the host stacks while the GPU computes the
-resident pairs, and the CPU rows come back through the result doorbell and are added to the GPU's.
-
-Per call, with the library's pieces:
-  1. top-k ring (device -> host): ids and weights; activation ring (device -> host): x (bf16),
-     both published on the compute stream right after the router;
-  2. `RoutedExperts.cache_split` (a2) on the host copy of the ids;
-  3. `policy.streamed_misses` over the missed pairs, `RoutedExperts.cache_upload` (a8) of those
-     experts, protecting this call's hits;
-  4. pairs still missing go to the CPU `Executor` (a11) with a selection mask;
-  5. the GPU forward runs the resident pairs (the slot map skips the others);
-  6. the result ring (host -> device) brings the CPU rows back; they are added to the output.
+stages/cpu_miss.rs, stages/preload.rs, staging.rs, rings.rs, prefill_stream.rs): the router's top-k
+reach the host through the top-k doorbell (no stream sync); the route split marks each pair resident
+or missed; `streamed_misses` picks the missed experts worth copying now into staging slots; the rest
+run on the CPU from the host stacks while the GPU computes the resident pairs, then the staged ones;
+the CPU rows come back through the result doorbell. Each call's activation feeds the next layer's
+prediction on a background thread, which prefetches that layer's predicted experts. All of it runs
+in the library; this class only holds the handle.
 """
 from __future__ import annotations
 
-import numpy as np
+import ctypes
 
-from . import policy
-from .cpu import CpuExperts, Executor, add_f32_into_bf16
-from .doorbell import Ring
-from .layer import _torch
+from ._lib import check, lib
+from .layer import _ptr, _stream, _torch
+
+
+class PagedOpts(ctypes.Structure):
+    _fields_ = [
+        ("staging_slots", ctypes.c_int),
+        ("pcie_frac", ctypes.c_float),
+        ("stream_cap", ctypes.c_int),
+        ("lookahead", ctypes.c_int),
+        ("lookahead_swaps", ctypes.c_int),
+        ("max_tokens", ctypes.c_int),
+        ("host_timeout_us", ctypes.c_int64),
+    ]
+
+
+class PagedStats(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int64) for n in (
+        "calls", "pairs", "hits", "staged_experts", "staged_pairs", "cpu_pairs", "lookahead_passes",
+        "lookahead_loads", "lookahead_swaps", "lookahead_dropped", "lookahead_errors", "predicted", "prefill_calls",
+        "prefill_waves", "prefill_uploads")]
 
 
 class PagedMoE:
-    def __init__(self, layer, cpu: CpuExperts | None = None, pcie_frac: float = 1.0, stream_cap: int | None = None,
-                 max_tokens: int | None = None, host_timeout_us: int = 5_000_000):
-        torch = _torch()
+    """One cached layer's calls (a RoutedExperts built with cache_slots > 0).
+
+    cpu: a CpuExperts for the misses that are not streamed (None: every miss must fit the staging
+    slots). pcie_frac / stream_cap: the share and number of missed experts copied per call into the
+    layer's staging slots. lookahead: predict the next layer's experts from each call's activation
+    (set the next layer with `set_next`)."""
+
+    def __init__(self, layer, cpu=None, pcie_frac: float = 1.0, stream_cap: int | None = None,
+                 max_tokens: int | None = None, staging_slots: int = 16, lookahead: bool = True,
+                 lookahead_swaps: int = 1, host_timeout_us: int = 5_000_000):
         if not layer.cache_slots:
             raise ValueError("PagedMoE needs a layer built with cache_slots > 0")
         self.layer = layer
         self.cpu = cpu
-        self.pcie_frac = float(pcie_frac)
-        self.stream_cap = layer.cache_slots if stream_cap is None else int(stream_cap)
-        self.T_max = int(max_tokens or layer.max_tokens)
-        self.k = layer.top_k
-        self.H = layer.hidden
-        self.timeout = host_timeout_us
-        dev = layer.device
-        self.topk_ring = Ring(dev, 4, self.T_max * self.k * 8)
-        self.act_ring = Ring(dev, 4, self.T_max * self.H * 2) if cpu is not None else None
-        self.result_ring = Ring(dev, 4, self.T_max * self.H * 4) if cpu is not None else None
-        self.executor = Executor(cpu, self.result_ring) if cpu is not None else None
-        self.cpu_rows = torch.empty(self.T_max * self.H, dtype=torch.float32, device=f"cuda:{dev}")
-        self.stats = {"calls": 0, "pairs": 0, "hits": 0, "streamed": 0, "cpu_pairs": 0}
+        o = PagedOpts()
+        lib().moe_paged_default_opts(ctypes.byref(o))
+        o.staging_slots = int(staging_slots)
+        o.pcie_frac = float(pcie_frac)
+        o.stream_cap = int(staging_slots if stream_cap is None else stream_cap)
+        o.lookahead = 1 if lookahead else 0
+        o.lookahead_swaps = int(lookahead_swaps)
+        o.max_tokens = int(max_tokens or layer.max_tokens)
+        o.host_timeout_us = int(host_timeout_us)
+        self.T_max = o.max_tokens
+        h = ctypes.c_void_p()
+        check(lib().moe_paged_create(layer._h, cpu._h if cpu is not None else None, ctypes.byref(o), ctypes.byref(h)))
+        self._h = h
 
-    def forward(self, xs, topk_weights, topk_ids, stream=None):
+    def set_next(self, nxt: "PagedMoE | None"):
+        """The next MoE layer, whose experts this layer's calls predict and prefetch."""
+        check(lib().moe_paged_set_next(self._h, nxt._h if nxt is not None else None))
+
+    def forward(self, xs, topk_weights, topk_ids, out=None, stream=None):
+        torch = _torch()
         T = xs.shape[0]
-        k = topk_ids.shape[1]
-        if T > self.T_max or k != self.k:
-            raise ValueError("PagedMoE.forward: T exceeds max_tokens or width != top_k")
-        ids_d = topk_ids.to(_torch().int32).contiguous()
-        w_d = topk_weights.to(_torch().float32).contiguous()
-        seq = self.topk_ring.publish_from_device(ids_d, w_d, stream=stream)
-        aseq = self.act_ring.publish_from_device(xs.contiguous(), stream=stream) if self.cpu is not None else 0
-        buf = np.empty(T * k * 2, np.uint32)
-        self.topk_ring.host_take(seq, buf, timeout_us=self.timeout)  # waits for the router, not the stream
-        ids = buf[:T * k].reshape(T, k)
-        w = buf[T * k:].view(np.float32).reshape(T, k)
-        hit = self.layer.cache_split(ids)
-        flat = ids.reshape(-1)
-        miss_rows = [[(int(ids[t, j]), float(w[t, j])) for j in range(k) if hit[t * k + j] == 0] for t in range(T)]
-        streamed = policy.streamed_misses(miss_rows, self.pcie_frac, self.stream_cap)
-        if streamed:
-            self.layer.cache_upload(streamed, protect=sorted(set(flat[hit == 1].tolist())), stream=stream)
-        resident = self.layer.cache_resident()
-        is_res = np.zeros(self.layer.num_experts + 1, bool)
-        is_res[resident[resident >= 0]] = True
-        live = flat != 0xFFFFFFFF
-        now_res = np.where(live, is_res[np.where(live, flat, self.layer.num_experts)], False)
-        cpu_sel = (live & ~now_res).astype(np.uint8)
-        target = 0
-        if self.cpu is not None:
-            x_h = np.empty(T * self.H, np.uint16)
-            self.act_ring.host_take(aseq, x_h, timeout_us=self.timeout)
-            if cpu_sel.any():
-                target = self.executor.submit(x_h.reshape(T, self.H), ids, w, cpu_sel)
-        elif cpu_sel.any():
-            raise RuntimeError("PagedMoE: missed experts with no CPU path and no slot to stream them into")
-        y = self.layer.forward(xs, w_d, ids_d, stream=stream)
-        if target:
-            rows = self.cpu_rows[:T * self.H]
-            self.result_ring.device_take(target, rows, stream=stream)
-            add_f32_into_bf16(y, rows, stream=stream)
-        s = self.stats
-        s["calls"] += 1
-        s["pairs"] += int(live.sum())
-        s["hits"] += int((hit == 1).sum())
-        s["streamed"] += len(streamed)
-        s["cpu_pairs"] += int(cpu_sel.sum())
+        ids = topk_ids if topk_ids.dtype == torch.int32 else topk_ids.to(torch.int32)
+        w = topk_weights if topk_weights.dtype == torch.float32 else topk_weights.to(torch.float32)
+        ids, w, xs = ids.contiguous(), w.contiguous(), xs.contiguous()
+        y = out if out is not None else torch.empty_like(xs)
+        check(lib().moe_paged_forward(self._h, _ptr(xs), T, _ptr(ids), _ptr(w), ids.shape[1], _ptr(y),
+                                      ctypes.c_void_p(_stream(stream))))
         return y
 
     __call__ = forward
 
-    def prefill(self, xs, topk_weights, topk_ids, chunk: int | None = None, stream=None):
-        """A prompt through the cached layer (PrefillStream::forward, prefill_stream.rs:1362-1694): chunks
-        of at most `chunk` tokens (default: what the layer's scratch holds); per chunk, its distinct
-        experts in waves of at most `slots` (resident ones first, so they need no upload); each wave
-        uploads its experts, runs the forward on ids restricted to them (moe_select_ids) and the wave
-        outputs are summed per token in f32 and rounded once (moe_ep_combine). All on the GPU."""
-        import ctypes
-
-        from ._lib import check, lib
-        from .ep import ep_combine
-        from .layer import _ptr, _stream
-
+    def prefill(self, xs, topk_weights, topk_ids, out=None, stream=None):
+        """A prompt through the cached layer (PrefillStream::forward, prefill_stream.rs:1362-1694)."""
         torch = _torch()
-        T, H = xs.shape
-        k = topk_ids.shape[1]
-        chunk = int(chunk or max(1, self.layer.max_tokens))
-        ids_all = topk_ids.to(torch.int32).contiguous()
-        w_all = topk_weights.to(torch.float32).contiguous()
-        ids_host = ids_all.cpu().numpy().view(np.uint32)
-        y = torch.empty_like(xs)
-        S = self.layer.cache_slots
-        for c0 in range(0, T, chunk):
-            c1 = min(T, c0 + chunk)
-            n = c1 - c0
-            ids_c, w_c, x_c = ids_all[c0:c1], w_all[c0:c1], xs[c0:c1]
-            flat = ids_host[c0:c1].reshape(-1)
-            distinct = sorted(set(flat[flat != 0xFFFFFFFF].tolist()))
-            res = set(int(e) for e in self.layer.cache_resident() if e >= 0)
-            order = [e for e in distinct if e in res] + [e for e in distinct if e not in res]
-            waves = [order[i:i + S] for i in range(0, len(order), S)] or [[]]
-            outs = []
-            for wave in waves:
-                self.layer.cache_upload(wave, protect=wave, stream=stream)
-                sel = torch.empty_like(ids_c)
-                ev = np.ascontiguousarray(np.asarray(wave, dtype=np.uint32))
-                check(lib().moe_select_ids(_ptr(ids_c), ids_c.numel(), self.layer.num_experts,
-                                           ctypes.c_void_p(ev.ctypes.data if ev.size else None), ev.size, _ptr(sel),
-                                           ctypes.c_void_p(_stream(stream))))
-                outs.append(self.layer.forward(x_c, w_c, sel, stream=stream))
-            rows = torch.arange(n, device=xs.device, dtype=torch.int32)
-            token_rows = torch.stack([rows + i * n for i in range(len(outs))], dim=1).contiguous()
-            y[c0:c1] = ep_combine(torch.cat(outs), token_rows, n, stream=stream)
+        T = xs.shape[0]
+        ids = topk_ids.to(torch.int32).contiguous()
+        w = topk_weights.to(torch.float32).contiguous()
+        xs = xs.contiguous()
+        y = out if out is not None else torch.empty_like(xs)
+        check(lib().moe_paged_prefill(self._h, _ptr(xs), T, _ptr(ids), _ptr(w), ids.shape[1], _ptr(y),
+                                      ctypes.c_void_p(_stream(stream))))
         return y
 
+    def fill(self, stream=None):
+        """Fill empty slots with the most-routed experts not resident (fill_candidate)."""
+        check(lib().moe_paged_fill(self._h, ctypes.c_void_p(_stream(stream))))
+
+    @property
+    def stats(self) -> dict:
+        s = PagedStats()
+        check(lib().moe_paged_get_stats(self._h, ctypes.byref(s)))
+        d = {n: int(getattr(s, n)) for n, _ in PagedStats._fields_}
+        d["streamed"] = d["staged_experts"]
+        return d
+
+    @staticmethod
+    def drain_lookahead():
+        check(lib().moe_paged_drain_lookahead())
+
     def check(self, stream=None):
-        self.layer.check()
-        self.topk_ring.check(stream)
-        if self.cpu is not None:
-            self.act_ring.check(stream)
-            self.result_ring.check(stream)
-            self.executor.drain()
+        check(lib().moe_paged_check(self._h, ctypes.c_void_p(_stream(stream))))
 
     def close(self):
-        if self.executor is not None:
-            self.executor.close()
-        for r in (self.topk_ring, self.act_ring, self.result_ring):
-            if r is not None:
-                r.close()
+        if getattr(self, "_h", None) is not None and self._h.value:
+            lib().moe_paged_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
