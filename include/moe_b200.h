@@ -127,6 +127,13 @@ void moe_layer_destroy(moe_layer* layer);
  * src/moe/slot.rs:76-111 extended to scratch. */
 int64_t moe_layer_device_bytes(const moe_layer* layer);
 
+/* The share of a forward's id slots expected to be live (not MOE_ID_NONE), default 1. The layer picks
+ * its kernels (decode GEMV or tcgen05 GEMM, token tile sizes) from the live pairs it expects; a caller
+ * whose ids are mostly empty slots says so here (an expert-parallel rank runs world * T received rows
+ * of which about 1 / world of the slots are its own). Results do not depend on it. No counterpart in
+ * the reference. */
+moe_status moe_layer_set_live_hint(moe_layer* layer, float live_fraction);
+
 /* Reads and clears the device-side error word of the layer (bad ids seen by a forward).
  * Synchronises `stream`. Returns MOE_OK or the latched status. */
 moe_status moe_layer_check(moe_layer* layer, void* stream);

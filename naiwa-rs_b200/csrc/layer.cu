@@ -6,6 +6,7 @@
 // expert is resident in HBM (180 GB holds every config of this path), so the per-call work is:
 // plan (histogram + stable permute) -> gate/up+SwiGLU -> down*weight -> combine, all on the
 // caller's stream with no host synchronisation, so a sequence of calls captures into one CUDA graph.
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -476,10 +477,13 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   MOE_TRY(plan_pairs(ids, n_pairs, E, po, L->plan_ws, L->plan_ws_bytes, st));
   MOE_TRY(mark(events, 1, st));
   const int max_active = n_pairs < E ? n_pairs : E;
-  const double est = (double)E * (1.0 - std::pow(1.0 - 1.0 / E, (double)n_pairs));
-  if (L->tc && (!L->q8_tiles || q8_uses_gemm(n_pairs, E))) {
+  // the kernel-path choices below follow the pairs expected to be live (moe_layer_set_live_hint);
+  // grid bounds keep using every slot
+  const int n_live = L->live_hint < 1.0f ? std::max(1, (int)((double)n_pairs * L->live_hint)) : n_pairs;
+  const double est = (double)E * (1.0 - std::pow(1.0 - 1.0 / E, (double)n_live));
+  if (L->tc && (!L->q8_tiles || q8_uses_gemm(n_live, E))) {
     const int w = L->d.wdtype;
-    const int bn = tc_token_tile(n_pairs, E);
+    const int bn = tc_token_tile(n_live, E);
     MOE_TRY(tc_tile_list(L->counts, L->active, L->n_active, bn, L->tile_list, L->n_tiles, st));
     MOE_TRY(tc_gather(x, nullptr, H, width, L->perm, n_pairs, L->offsets + E, L->x16, L->xscale, st, bn < 128));
     TcArgs ga{};
@@ -533,7 +537,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   gp.tiles = 2 * I / 16;
   gp.kb_count = H / 32;
   gp.phase = 0;
-  gp.tpp = choose_tpp(H, n_pairs / (est > 1.0 ? est : 1.0));
+  gp.tpp = choose_tpp(H, n_live / (est > 1.0 ? est : 1.0));
   gp.width = width;
   gp.n_pairs = n_pairs;
   gp.x = static_cast<const __nv_bfloat16*>(x);
@@ -558,7 +562,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   dp.tiles = H / 16;
   dp.kb_count = I / 32;
   dp.phase = 1;
-  dp.tpp = choose_tpp(I, n_pairs / (est > 1.0 ? est : 1.0));
+  dp.tpp = choose_tpp(I, n_live / (est > 1.0 ? est : 1.0));
   dp.x = nullptr;
   dp.h_in = L->h;
   dp.route_w = weights;
@@ -583,6 +587,14 @@ void moe_layer_destroy(moe_layer* L) {
 }
 
 int64_t moe_layer_device_bytes(const moe_layer* L) { return L ? L->weight_bytes + L->scratch_bytes : 0; }
+
+moe_status moe_layer_set_live_hint(moe_layer* L, float live_fraction) {
+  if (!L) return fail(MOE_ERR_INVALID, "moe_layer_set_live_hint: null layer");
+  if (!(live_fraction > 0.0f && live_fraction <= 1.0f))
+    return fail(MOE_ERR_INVALID, "moe_layer_set_live_hint: the fraction must be in (0, 1]");
+  L->live_hint = live_fraction;
+  return MOE_OK;
+}
 
 moe_status moe_layer_check(moe_layer* L, void* stream) {
   if (!L) return fail(MOE_ERR_INVALID, "moe_layer_check: null layer");

@@ -61,6 +61,7 @@ struct moe_layer {
   alignas(128) unsigned char tmap_h[128];
   int64_t weight_bytes = 0;
   int64_t scratch_bytes = 0;
+  float live_hint = 1.0f;  // expected share of a forward's id slots that are live (kernel-path choice only)
   // expert cache (cache_slots > 0): every expert in pinned host memory in the device layout, `slots`
   // of them (plus `staging` streamed ones) in the device banks above; slot_of maps expert -> slot
   // (-1: not resident)

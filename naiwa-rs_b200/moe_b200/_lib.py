@@ -85,6 +85,7 @@ def lib():
             "moe_layer_destroy": (None, [P]),
             "moe_layer_device_bytes": (ctypes.c_int64, [P]),
             "moe_layer_check": (i, [P, P]),
+            "moe_layer_set_live_hint": (i, [P, f]),
             "moe_last_error": (ctypes.c_size_t, [ctypes.c_char_p, ctypes.c_size_t]),
             "moe_route_tokens": (i, [P, P, P, i, i, i, i, i, i, i, f, P, P, P, ctypes.c_size_t, P]),
             "moe_route_workspace_bytes": (ctypes.c_size_t, [i, i]),

@@ -212,6 +212,8 @@ class PeerExpertParallelMoE:
             "send_w": torch.empty((rows, self.k), dtype=torch.float32, device=dev),
             "error_word": torch.zeros(1, dtype=torch.int32, device=dev),
         }
+        # the local forward runs world * cap received rows, about 1 / world of whose slots are live
+        local.set_live_hint(1.0 / world)
         self.shared_w = torch.ones((self.cap, 1), dtype=torch.float32, device=dev)
         self.shared_ids = torch.zeros((self.cap, 1), dtype=torch.int32, device=dev)
 

@@ -193,6 +193,10 @@ class RoutedExperts:
         check(lib().moe_layer_warmup(self._h, int(max_tokens)))
         self.max_tokens = max(self.max_tokens, int(max_tokens))
 
+    def set_live_hint(self, live_fraction: float):
+        """Expected share of live (non-empty) id slots per forward: steers the kernel-path choice only."""
+        check(lib().moe_layer_set_live_hint(self._h, float(live_fraction)))
+
     def device_bytes(self) -> int:
         return int(lib().moe_layer_device_bytes(self._h))
 
