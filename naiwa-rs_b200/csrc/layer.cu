@@ -419,6 +419,21 @@ static bool q8_uses_gemm(int n_pairs, int E) {
   return (int64_t)n_pairs >= 8ll * E;
 }
 
+// Below the tcgen05 threshold a Q8_0 unit layer streams its weights either through registers (the
+// decode GEMV, expert_decode.cu) or through a shared-memory ring (expert_stream.cu); both give the
+// same bits. MOE_DECODE=stream|gemv pins the choice.
+static bool decode_uses_stream(int n_pairs, int E) {
+  static const int forced = [] {
+    const char* v = std::getenv("MOE_DECODE");
+    if (!v) return 0;
+    return std::string(v) == "stream" ? 1 : std::string(v) == "gemv" ? -1 : 0;
+  }();
+  if (forced) return forced > 0;
+  (void)n_pairs;
+  (void)E;
+  return false;
+}
+
 moe_status moe_forward(moe_layer* L, const void* x, int T, const uint32_t* ids, const float* weights, int width,
                        void* y, void* stream) {
   return forward_impl(L, x, T, ids, weights, width, y, stream, nullptr);
@@ -548,8 +563,11 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   gp.n_active = L->n_active;
   gp.slot_of = slot_of;
   gp.tile_major = L->q8_tiles ? 1 : 0;
+  gp.err = L->err;
   auto rowt_of = [&](const ExpertParams& q) { return pick_rowt(q.tiles, q.tpp, est, L->sms); };
-  MOE_TRY(launch_expert_gemv(L->d.wdtype, gp, max_active, rowt_of(gp), st));
+  const bool use_stream = L->q8_tiles && decode_uses_stream(n_live, E);
+  if (use_stream) MOE_TRY(launch_expert_stream(gp, max_active, L->sms, st));
+  else MOE_TRY(launch_expert_gemv(L->d.wdtype, gp, max_active, rowt_of(gp), st));
   MOE_TRY(mark(events, 2, st));
 
   ExpertParams dp = gp;
@@ -567,7 +585,8 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   dp.h_in = L->h;
   dp.route_w = weights;
   dp.out = L->ypair;
-  MOE_TRY(launch_expert_gemv(L->d.wdtype, dp, max_active, rowt_of(dp), st));
+  if (use_stream) MOE_TRY(launch_expert_stream(dp, max_active, L->sms, st));
+  else MOE_TRY(launch_expert_gemv(L->d.wdtype, dp, max_active, rowt_of(dp), st));
   MOE_TRY(mark(events, 3, st));
   if (combine) MOE_TRY(launch_combine(L->ypair, ids, T, width, H, E, y, st, slot_of));
   if (L->slots) MOE_CUDA_TRY(cudaEventRecord(L->last_read, st));  // the slots' readers
@@ -578,6 +597,7 @@ extern "C" {
 
 void moe_layer_destroy(moe_layer* L) {
   if (!L) return;
+  paged_detach_all(L);
   DeviceGuard guard(L->dev);
   cudaDeviceSynchronize();
   free_weights(L);

@@ -90,6 +90,9 @@ struct moe_layer {
   // runtime's lookahead thread (the reference's per-layer Mutex, cached_layer.rs:494); recursive so
   // the paged runtime can call the layer's own entry points while it holds it.
   std::recursive_mutex cache_mu;
+  // Paged runtimes built on this layer (paged.cu); destroying the layer detaches them first, so no
+  // lookahead job can reach a freed layer.
+  std::vector<struct moe_paged*> paged;
 };
 
 namespace moe {
@@ -109,6 +112,10 @@ moe_status cache_copy_expert(moe_layer* L, int e, int slot);
 // Grows the device banks by n staging slots past the cache slots (synchronises the device; the
 // existing slots keep their contents). No-op when the layer already has at least n.
 moe_status cache_reserve_staging(moe_layer* L, int n);
+
+// Detaches every paged runtime of L before L is destroyed: their queued lookahead jobs are dropped,
+// a running one is waited for, and their later calls fail instead of touching the freed layer.
+void paged_detach_all(moe_layer* L);
 
 // moe_forward on an explicit stream, for the paged runtime.
 moe_status layer_forward(moe_layer* L, const void* x, int T, const uint32_t* ids, const float* weights, int width,

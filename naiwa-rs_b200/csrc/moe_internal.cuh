@@ -55,8 +55,13 @@ struct ExpertParams {
   int units_per_expert;
   const int32_t* slot_of;     // [E] cache slot of each expert, or null: weights indexed by expert id
   int tile_major;             // Q8_0 only: weights in 128 x 128 units (repack_q8_units)
+  int32_t* err;               // [1] error word (a bounded wait that ran out), or null
 };
 moe_status launch_expert_gemv(int wdtype, ExpertParams p, int max_active, int rowt, cudaStream_t st);
+// The Q8_0 unit-layout pass through a shared-memory weight stream (expert_stream.cu): same results
+// as launch_expert_gemv, one persistent CTA per SM.
+moe_status launch_expert_stream(ExpertParams p, int max_active, int sms, cudaStream_t st);
+int stream_stages(int K, int tpp);
 moe_status launch_combine(const float* ypair, const uint32_t* ids, int T, int width, int H, int E, void* y,
                           cudaStream_t st, const int32_t* slot_of = nullptr);
 int choose_tpp(int K, double mean_tokens_per_expert);

@@ -92,6 +92,7 @@ struct Lookahead {
   std::condition_variable cv, idle_cv;
   std::deque<LookJob> jobs;
   moe_paged* running = nullptr;
+  std::vector<moe_paged*> live;  // every paged runtime not yet destroyed
   std::thread worker;
   bool started = false;
 
@@ -105,6 +106,7 @@ struct Lookahead {
   void loop();
   void push(LookJob&& j, moe_paged* p) {
     std::lock_guard<std::mutex> l(m);
+    if (std::find(live.begin(), live.end(), p) == live.end() || !p->L) return;  // target gone or detached
     start();
     if (jobs.size() >= LOOKAHEAD_DEPTH) {
       std::lock_guard<std::mutex> s(p->stats_mu);
@@ -114,11 +116,22 @@ struct Lookahead {
     jobs.push_back(std::move(j));
     cv.notify_one();
   }
-  // Drops the queued jobs of `p` and waits until none of them runs.
-  void forget(moe_paged* p) {
+  // Drops the queued jobs of `p` and waits until none of them runs; with `remove`, p also leaves
+  // the live set and every other runtime's link to it is cut.
+  void forget(moe_paged* p, bool remove, bool detach = false) {
     std::unique_lock<std::mutex> l(m);
     for (auto it = jobs.begin(); it != jobs.end();) it = it->target == p ? jobs.erase(it) : it + 1;
     idle_cv.wait(l, [&] { return running != p; });
+    if (detach) p->L = nullptr;  // under the lock: push() refuses p from now on
+    if (remove) {
+      live.erase(std::remove(live.begin(), live.end(), p), live.end());
+      for (moe_paged* q : live)
+        if (q->next == p) q->next = nullptr;
+    }
+  }
+  void add(moe_paged* p) {
+    std::lock_guard<std::mutex> l(m);
+    live.push_back(p);
   }
   // Waits until the queue is empty and no job runs.
   void drain() {
@@ -240,6 +253,7 @@ void Lookahead::loop() {
       cv.wait(l, [&] { return !jobs.empty(); });
       job = std::move(jobs.front());
       jobs.pop_front();
+      if (!job.target->L) continue;  // its layer was destroyed
       running = job.target;
     }
     const std::vector<int> predicted = predict(job.target, job.x.data(), job.rows);
@@ -272,7 +286,12 @@ void moe_paged_default_opts(moe_paged_opts* o) {
 
 void moe_paged_destroy(moe_paged* p) {
   if (!p) return;
-  lookahead().forget(p);
+  lookahead().forget(p, true);
+  if (p->L) {
+    std::lock_guard<std::recursive_mutex> lock(p->L->cache_mu);
+    auto& v = p->L->paged;
+    v.erase(std::remove(v.begin(), v.end(), p), v.end());
+  }
   if (p->ex) moe_executor_destroy(p->ex);
   moe_ring_destroy(p->topk_ring);
   moe_ring_destroy(p->act_ring);
@@ -345,12 +364,30 @@ moe_status moe_paged_create(moe_layer* L, moe_cpu_experts* cpu, const moe_paged_
     p->router.resize(bf.size());
     for (size_t i = 0; i < bf.size(); ++i) p->router[i] = bf16_bits_to_f32(bf[i]);
   }
+  {
+    std::lock_guard<std::recursive_mutex> lock(L->cache_mu);
+    L->paged.push_back(p);
+  }
+  lookahead().add(p);
   *out = p;
   return MOE_OK;
 }
 
+}  // extern "C"
+
+void moe::paged_detach_all(moe_layer* L) {
+  std::vector<moe_paged*> ps;
+  {
+    std::lock_guard<std::recursive_mutex> lock(L->cache_mu);
+    ps.swap(L->paged);
+  }
+  for (moe_paged* p : ps) lookahead().forget(p, false, true);  // no job of p runs on L; later calls fail
+}
+
+extern "C" {
+
 moe_status moe_paged_set_next(moe_paged* p, moe_paged* next) {
-  if (!p) return fail(MOE_ERR_INVALID, "moe_paged_set_next: null paged layer");
+  if (!p || !p->L) return fail(MOE_ERR_INVALID, "moe_paged_set_next: null paged layer or its layer was destroyed");
   if (next && next->router.empty())
     return fail(MOE_ERR_INVALID, "moe_paged_set_next: the next layer has no router to predict with");
   if (next && next->H != p->H) return fail(MOE_ERR_INVALID, "moe_paged_set_next: hidden sizes differ");
@@ -362,7 +399,7 @@ moe_status moe_paged_set_next(moe_paged* p, moe_paged* next) {
 
 moe_status moe_paged_forward(moe_paged* p, const void* x, int T, const uint32_t* ids, const float* weights, int width,
                              void* y, void* stream) {
-  if (!p) return fail(MOE_ERR_INVALID, "moe_paged_forward: null paged layer");
+  if (!p || !p->L) return fail(MOE_ERR_INVALID, "moe_paged_forward: null paged layer or its layer was destroyed");
   if (T < 0 || width <= 0 || width > 2 * p->k) return fail(MOE_ERR_INVALID, "moe_paged_forward: bad T or width");
   if (T == 0) return MOE_OK;
   if (T > p->o.max_tokens) return fail(MOE_ERR_INVALID, "moe_paged_forward: T exceeds the paged max_tokens");
@@ -391,7 +428,17 @@ moe_status moe_paged_forward(moe_paged* p, const void* x, int T, const uint32_t*
     std::lock_guard<std::recursive_mutex> lock(L->cache_mu);
     // 2. the route split (stages/route.rs:19-158) and the streamed misses (cached_layer.rs:385-398)
     std::vector<uint8_t> hit((size_t)n);
-    MOE_TRY(moe_cache_split(L, ids_h, n, hit.data()));
+    const moe_status split = moe_cache_split(L, ids_h, n, hit.data());
+    if (split != MOE_OK) {  // name the ring state with the bad id, so a malformed hand-off is visible
+      uint32_t rseq = 0, rcons = 0;
+      moe_ring_counters(p->topk_ring, &rseq, &rcons);
+      std::string msg;
+      for (int i = 0; i < n && i < 8; ++i) msg += " " + std::to_string(ids_h[i]);
+      return fail(split, "moe_paged_forward: " + last_error_message() + " (top-k slot " + std::to_string(seq) +
+                             ", ring seq " + std::to_string(rseq) + ", consumed " + std::to_string(rcons) +
+                             ", T " + std::to_string(T) + ", width " + std::to_string(width) + "; first ids" + msg +
+                             ")");
+    }
     std::vector<uint32_t> miss_ids;
     std::vector<float> miss_w;
     std::vector<int32_t> row_lens((size_t)T, 0);
@@ -499,7 +546,7 @@ moe_status moe_paged_forward(moe_paged* p, const void* x, int T, const uint32_t*
 
 moe_status moe_paged_prefill(moe_paged* p, const void* x, int T, const uint32_t* ids, const float* weights, int width,
                              void* y, void* stream) {
-  if (!p) return fail(MOE_ERR_INVALID, "moe_paged_prefill: null paged layer");
+  if (!p || !p->L) return fail(MOE_ERR_INVALID, "moe_paged_prefill: null paged layer or its layer was destroyed");
   if (T < 0 || width <= 0) return fail(MOE_ERR_INVALID, "moe_paged_prefill: bad T or width");
   if (T == 0) return MOE_OK;
   if (!x || !ids || !weights || !y) return fail(MOE_ERR_INVALID, "moe_paged_prefill: null pointer");
@@ -621,7 +668,7 @@ moe_status moe_paged_get_stats(moe_paged* p, moe_paged_stats* out) {
 }
 
 moe_status moe_paged_fill(moe_paged* p, void* stream) {
-  if (!p) return fail(MOE_ERR_INVALID, "moe_paged_fill: null paged layer");
+  if (!p || !p->L) return fail(MOE_ERR_INVALID, "moe_paged_fill: null paged layer or its layer was destroyed");
   moe_layer* L = p->L;
   std::lock_guard<std::recursive_mutex> lock(L->cache_mu);
   for (;;) {  // the reference's spawn_fill loop (cached_layer.rs:1303-1337), synchronous here
@@ -640,7 +687,7 @@ moe_status moe_paged_drain_lookahead(void) {
 }
 
 moe_status moe_paged_check(moe_paged* p, void* stream) {
-  if (!p) return fail(MOE_ERR_INVALID, "moe_paged_check: null paged layer");
+  if (!p || !p->L) return fail(MOE_ERR_INVALID, "moe_paged_check: null paged layer or its layer was destroyed");
   MOE_TRY(moe_layer_check(p->L, stream));
   MOE_TRY(moe_ring_check(p->topk_ring, stream));
   MOE_TRY(moe_ring_check(p->act_ring, stream));

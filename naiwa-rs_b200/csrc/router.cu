@@ -144,10 +144,13 @@ __device__ void select_token(const RouteParams& p, float* l, float* a, uint32_t*
   __syncwarp();
 }
 
-// grid (ceil(T/TB), ceil(E/EB)); ws_logits [T, E] f32; ws_count [ceil(T/TB)] u32 (zero between calls)
+// grid (ceil(T/TB), ceil(E/EB)); ws_logits [T, E] f32; the arrival counter of token block b is
+// ws_count_end[-1 - b], the end of the workspace counting down: its address does not depend on T, so
+// a workspace reused with another T keeps every counter at zero between calls (at the front, after
+// the logits, a shorter call's counters would land on a longer call's logits)
 template <int TB>
 __global__ void __launch_bounds__(ROUTER_THREADS) route_kernel(RouteParams p, float* __restrict__ ws_logits,
-                                                               unsigned* __restrict__ ws_count) {
+                                                               unsigned* __restrict__ ws_count_end) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ int s_last;
   const int H = p.H, E = p.E;
@@ -209,7 +212,7 @@ __global__ void __launch_bounds__(ROUTER_THREADS) route_kernel(RouteParams p, fl
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(&ws_count[blockIdx.x], 1u);
+    const unsigned prev = atomicAdd(&ws_count_end[-1 - (int)blockIdx.x], 1u);
     s_last = prev == gridDim.y - 1;
   }
   __syncthreads();
@@ -223,7 +226,7 @@ __global__ void __launch_bounds__(ROUTER_THREADS) route_kernel(RouteParams p, fl
   __syncthreads();
   for (int t = warp; t < nt; t += ROUTER_WARPS)
     select_token(p, lg + t * E, aux + t * auxw, taken + t * ((E + 31) / 32), t0 + t, lane);
-  if (threadIdx.x == 0) ws_count[blockIdx.x] = 0u;  // ready for the next call on this stream
+  if (threadIdx.x == 0) ws_count_end[-1 - (int)blockIdx.x] = 0u;  // ready for the next call on this stream
 }
 
 static size_t route_smem(int TB, int H, int E) {
@@ -280,8 +283,8 @@ moe_status route_tokens(const RouteParams& p, void* ws, size_t ws_bytes, cudaStr
     return fail(MOE_ERR_INVALID,
                 "moe_route: workspace missing, misaligned or smaller than moe_route_workspace_bytes");
   float* logits = static_cast<float*>(ws);
-  unsigned* counts =
-      reinterpret_cast<unsigned*>(static_cast<char*>(ws) + ((size_t)p.T * p.E * 4 + 255) / 256 * 256);
+  // counters count down from the (4-byte aligned) end: T-independent addresses past every logit
+  unsigned* counts = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + (ws_bytes & ~(size_t)3));
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

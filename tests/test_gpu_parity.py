@@ -70,6 +70,24 @@ def test_router_softmax_bit_exact(T, H, E, k, mode):
     assert np.array_equal(wt.cpu().numpy().view(np.uint32), rw.view(np.uint32))
 
 
+def test_router_workspace_reused_across_batch_sizes():
+    """One layer (and one Router workspace) routes batches that grow and shrink: every call's ids and
+    weights are the oracle's. The arrival counters must sit where no call's logits land, or a shorter
+    call after a longer one finds no last CTA and leaves the ids unwritten."""
+    rng = np.random.default_rng(77)
+    E, k, H = 16, 4, 256
+    w = O.f32_to_bf16(rng.normal(0, 0.05, (E, H)).astype(np.float32))
+    q, _ = make_stacks(rng, E, H, 128, O.DT_Q8_0)
+    layer = build_layer(q, E, k, H, 128, O.DT_Q8_0, router=w.reshape(E, H), mode=1, max_tokens=64)
+    router = M().Router(bf16_tensor(w.reshape(E, H)), k, 1, max_tokens=64)
+    for T in (16, 7, 64, 1, 33, 2, 64, 5):
+        x = O.f32_to_bf16(rng.normal(0, 1, (T, H)).astype(np.float32))
+        rid, rw = O.route(O.router_logits(x, w.reshape(E, H)), k, 1)
+        for got_ids, got_w in (layer.route(bf16_tensor(x)), router.route(bf16_tensor(x))):
+            assert np.array_equal(got_ids.cpu().numpy().astype(np.uint32), rid), T
+            assert np.array_equal(got_w.cpu().numpy().view(np.uint32), rw.view(np.uint32)), T
+
+
 def test_router_ties_go_to_lowest_id():
     # identical router rows give identical logits: the top-k must be the lowest ids (tests.rs:169-173)
     H, E, k = 256, 32, 4
