@@ -337,6 +337,8 @@ def run_ours(args):
     ys = {T: torch.empty((T, H), dtype=torch.bfloat16, device=dev) for T in RAGGED}
     # one peer-memory exchange per batch size (its regions hold world * T rows), shared by the layers
     peers = {T: M.PeerExpertParallelMoE(layers[0], rank, world, epr, max_tokens=T) for T in RAGGED} if ep else {}
+    for layer in layers if ep else []:  # every local layer runs world * T received rows, ~1/world of them live
+        layer.set_live_hint(1.0 / world)
 
     def call(T, li, xin, yout, marks=None):
         if ep:

@@ -170,8 +170,10 @@ __global__ void __launch_bounds__(P2P_THREADS) peer_dispatch_kernel(PeerPtrs pee
 }
 
 // Waits (thread 0, bounded by wait_ns) until flags[0..W) all carry `epoch`; false after the time
-// limit or when a flag of this epoch has its failed bit set.
-__device__ bool wait_flags(const uint64_t* flags, int W, uint32_t epoch, int32_t* status, uint64_t wait_ns) {
+// limit or, for return flags (whose low word is the failed bit; a dispatch flag's low word is its row
+// count), when a flag of this epoch reports a failed receive.
+__device__ bool wait_flags(const uint64_t* flags, int W, uint32_t epoch, int32_t* status, uint64_t wait_ns,
+                           bool return_flags) {
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
     const uint64_t t0 = p2p_now();
@@ -181,7 +183,7 @@ __device__ bool wait_flags(const uint64_t* flags, int W, uint32_t epoch, int32_t
       for (int r = 0; r < W && all; ++r) {
         const uint64_t f = ld_acquire_sys64(flags + r);
         all = (uint32_t)(f >> 32) == epoch;
-        failed |= all && (f & P2P_FLAG_FAILED);
+        failed |= return_flags && all && (f & P2P_FLAG_FAILED);
       }
       if (all) {
         ok = !failed;
@@ -208,7 +210,7 @@ __global__ void __launch_bounds__(P2P_THREADS) peer_receive_kernel(PeerPtrs peer
   int32_t* status = reinterpret_cast<int32_t*>(mine + L.status);
   uint32_t* recv_ok = reinterpret_cast<uint32_t*>(mine + L.recv_ok_epoch);
   __shared__ int cnt[P2P_MAX_WORLD];
-  if (!wait_flags(flags, W, epoch, status, wait_ns)) {
+  if (!wait_flags(flags, W, epoch, status, wait_ns, false)) {
     // sources that did not arrive: run nothing (all slots empty), so the forward reads no region
     for (size_t i = threadIdx.x; i < (size_t)W * cap * k; i += P2P_THREADS) ids[i] = MOE_ID_NONE;
     for (int r = threadIdx.x; r < W; r += P2P_THREADS) counts[r] = 0;
@@ -275,7 +277,7 @@ __global__ void __launch_bounds__(P2P_THREADS) peer_wait_return_kernel(PeerPtrs 
   unsigned char* mine = peers.base[me];
   const uint32_t epoch = call_epoch(mine, L, epoch_arg, 1);
   const bool ok = wait_flags(reinterpret_cast<const uint64_t*>(mine + L.ret_flag), W, epoch,
-                             reinterpret_cast<int32_t*>(mine + L.status), wait_ns);
+                             reinterpret_cast<int32_t*>(mine + L.status), wait_ns, true);
   if (threadIdx.x == 0) {
     if (!ok) *reinterpret_cast<uint32_t*>(mine + L.fail_epoch) = epoch;  // this epoch's combine adds no returned row
     *reinterpret_cast<uint32_t*>(mine + L.done_epoch) = epoch;  // the next device-held epoch follows it

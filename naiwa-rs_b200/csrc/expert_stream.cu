@@ -31,6 +31,48 @@ constexpr int ST_HEADER = 256;   // barriers and the abort flag, ahead of the ri
 
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
+// One warp stages one token row, as stage_row<true> does (same scale, same f16 values, same layout),
+// but with the lane's whole share of the row loaded at once: K <= 2048 bf16 (phase 0) or K <= 1024
+// f32 (phase 1) is at most 8 chunks of 8 values per lane, so every load is in flight together
+// instead of one L2 round trip per chunk, twice.
+__device__ __forceinline__ void stage_row_batched(const ExpertParams& p, int n, int src_row, uint32_t* xs, int ntm,
+                                                  float* tscale, int lane) {
+  constexpr int MAXC = 8;
+  const int chunks = p.K >> 3;
+  float v[MAXC][8];
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = lane + 32 * i;
+    if (c < chunks) load_chunk<true>(p, src_row, c, v[i]);
+  }
+  float m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i)
+    if (lane + 32 * i < chunks)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[i][j]));
+  m = warp_max(m);
+  float inv = 1.0f, sc = 1.0f;
+  if (m > 0.0f && m < __int_as_float(0x7f800000)) {
+    int ex;
+    frexpf(m, &ex);  // m < 2^ex
+    const int sh = max(-100, min(100, ex - 14));
+    sc = ldexpf(1.0f, sh);
+    inv = ldexpf(1.0f, -sh);
+  }
+  if (lane == 0) tscale[n] = sc;
+  const int nt = n >> 3, g = n & 7;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = lane + 32 * i;
+    if (c >= chunks) continue;
+    const int kb = c >> 2, s = (c >> 1) & 1, h = c & 1;
+    uint32_t* dst = xs + ((kb * ntm + nt) * 32 + g * 4) * 4 + s * 2 + h;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) dst[q * 4] = pack_f16x2(v[i][2 * q] * inv, v[i][2 * q + 1] * inv);
+  }
+}
+
 template <int NTM>
 __global__ void __launch_bounds__(ST_THREADS, 1) expert_stream_kernel(ExpertParams p, int stages) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -61,12 +103,15 @@ __global__ void __launch_bounds__(ST_THREADS, 1) expert_stream_kernel(ExpertPara
   const int units_k = p.K / 128;  // units along K of one 128-row unit row
   const int chunks = p.N / 128;   // unit rows per expert
   const int n_items = __ldcg(p.n_active) * chunks;
+  // a contiguous, expert-major range of items per CTA: consecutive items share their expert's tokens
+  const int it_begin = (int)((int64_t)n_items * blockIdx.x / gridDim.x);
+  const int it_end = (int)((int64_t)n_items * (blockIdx.x + 1) / gridDim.x);
 
   if (warp == ST_CONSUMERS) {  // ---- producer ----
     if (lane == 0) {
       uint32_t pos = 0;
       bool ok = true;
-      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      for (int it = it_begin; it < it_end && ok; ++it) {
         const int a = it / chunks, c = it - a * chunks;
         const int e = __ldcg(p.active + a);
         const int es = p.slot_of ? __ldcg(p.slot_of + e) : e;
@@ -102,7 +147,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) expert_stream_kernel(ExpertPara
   const int g = lane >> 2, cq = lane & 3;
   const int frag_off = warp * 4 * 512 + ((4 * g + (cq ^ ((g >> 1) & 3))) << 4);
   const int scale_off = 8 * 4 * 512 + warp * 128 + g * 16;
-  for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+  int staged_e = -1, staged_p0 = -1;  // whose tokens xs holds
+  for (int it = it_begin; it < it_end && ok; ++it) {
     const int a = it / chunks, c = it - a * chunks;
     const int e = __ldcg(p.active + a);
     const int base = __ldcg(p.offsets + e);
@@ -116,13 +162,17 @@ __global__ void __launch_bounds__(ST_THREADS, 1) expert_stream_kernel(ExpertPara
         pdl_trigger();
         waited = true;
       }
-      consumers_sync();  // the previous pass's reads of xs are done
-      if (threadIdx.x < TPP) spair[threadIdx.x] = threadIdx.x < ntok ? p.perm[base + p0 + threadIdx.x] : -1;
-      for (int n = warp; n < ntok; n += ST_CONSUMERS) {
-        const int src = p.phase == 0 ? p.perm[base + p0 + n] / p.width : base + p0 + n;
-        stage_row<true>(p, n, src, xs, NTM, tscale, lane);
+      if (staged_e != e || staged_p0 != p0) {
+        consumers_sync();  // the previous pass's reads of xs are done
+        if (threadIdx.x < TPP) spair[threadIdx.x] = threadIdx.x < ntok ? p.perm[base + p0 + threadIdx.x] : -1;
+        for (int n = warp; n < ntok; n += ST_CONSUMERS) {
+          const int src = p.phase == 0 ? p.perm[base + p0 + n] / p.width : base + p0 + n;
+          stage_row_batched(p, n, src, xs, NTM, tscale, lane);
+        }
+        consumers_sync();
+        staged_e = e;
+        staged_p0 = p0;
       }
-      consumers_sync();
       float acc[NTM][4];
 #pragma unroll
       for (int t = 0; t < NTM; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
@@ -204,6 +254,8 @@ static moe_status launch_stream_t(const ExpertParams& p, int grid, int stages, c
 // past the real active count stop at once).
 moe_status launch_expert_stream(ExpertParams p, int max_active, int sms, cudaStream_t st) {
   if (p.K % 128 || p.N % 128) return fail(MOE_ERR_INVALID, "expert stream: Q8_0 units need 128-multiples");
+  if (p.K > (p.phase == 0 ? 2048 : 1024))
+    return fail(MOE_ERR_UNSUPPORTED, "expert stream: rows wider than one batched staging load");
   if (p.tpp % 8 || p.tpp < 8 || p.tpp > MAX_TPP) return fail(MOE_ERR_INVALID, "expert stream: bad tokens per pass");
   const int stages = stream_stages(p.K, p.tpp);
   if (!stages) return fail(MOE_ERR_UNSUPPORTED, "expert stream: the tokens of one pass leave no room for the ring");
