@@ -431,8 +431,8 @@ def run_ours(args):
 
     # ---- stage timing: one captured step with events between the stages ---------------------------
     lib = M.lib()
-    if ep:  # route | dispatch plan + dispatch | receive | local forward | return | combine
-        names = ["route", "dispatch", "receive", "local_forward", "return", "combine"]
+    if ep:  # route | routed dispatch (plan, rows out, receive) | local forward | return | combine
+        names = ["route", "dispatch_receive", "local_forward", "return", "combine"]
     else:   # route | plan | gate/up | down | combine
         names = ["route", "plan", "gate_up", "down", "combine"]
     nev = len(RAGGED) * L
@@ -548,11 +548,11 @@ def run_ours(args):
         p.check()
     del graph, mgraph
 
-    # launches per step of this rank: route, then (N > 1) dispatch plan, dispatch, receive, the local
-    # forward on world * T rows, return, return wait, combine
+    # launches per step of this rank: route, then (N > 1) the routed dispatch, the local forward on
+    # world * T rows, return, combine
     def launches_for(T):
         if ep:
-            return 1 + 3 + _launches_local(world * T * K_TOP, epr) + 3
+            return 1 + 1 + _launches_local(world * T * K_TOP, epr) + 2
         return 1 + _launches_local(T * K_TOP, E)
     launches_per_step = L * sum(launches_for(T) for T in RAGGED)
 

@@ -334,11 +334,14 @@ moe_status moe_select_ids(const uint32_t* ids, int64_t n, int E, const uint32_t*
  * kernels that store rows straight into the peers' memory (CUDA IPC mappings, plain loads/stores,
  * no multicast). Each rank creates one peer object (cap_rows = the most tokens one rank sends per
  * call), exports its handle, gathers every rank's handle by any host channel and connects. Per call
- * (epoch = 1, 2, ... identical on every rank; or epoch = 0 in all five calls, which takes the epoch
- * after the last one whose combine waited on this rank from device memory, so that a captured CUDA
- * graph of whole steps can be replayed), on one stream:
+ * (epoch = 1, 2, ... identical on every rank; or epoch = 0 in every call, which takes the epoch after
+ * the last one whose combine completed on this rank from device memory, so that a captured CUDA
+ * graph of whole steps can be replayed), on one stream, either
+ *   moe_ep_peer_dispatch_routed -> moe_forward of the local layer on moe_ep_peer_recv_rows /
+ *   moe_ep_peer_recv_ids / moe_ep_peer_recv_weights (world * cap_rows rows) -> moe_ep_peer_return ->
+ *   moe_ep_peer_combine                                   (three launches besides the forward), or
  *   moe_ep_dispatch_plan (above) -> moe_ep_peer_dispatch -> moe_ep_peer_receive -> moe_forward of the
- *   local layer on moe_ep_peer_recv_rows (world * cap_rows rows) -> moe_ep_peer_return ->
+ *   local layer on moe_ep_peer_recv_rows and the received ids/weights -> moe_ep_peer_return ->
  *   moe_ep_peer_combine.
  * No host synchronisation: the counts travel with the rows. Waits for other ranks are bounded (about
  * five seconds); one that runs out records MOE_ERR_TIMEOUT (moe_ep_peer_check) and its kernel reads no
@@ -352,6 +355,20 @@ moe_status moe_ep_peer_connect(moe_ep_peer* peer, const void* handles);
 void moe_ep_peer_destroy(moe_ep_peer* peer);
 /* This rank's receive rows: [world * cap_rows, hidden] bf16, region s holding source s's rows. */
 void* moe_ep_peer_recv_rows(moe_ep_peer* peer);
+/* Source and destination in one launch: the plan of moe_ep_dispatch_plan (same rank_counts and
+ * token_rows, bit for bit; error_word as there) built from ids [T, top_k] (global expert ids; rank r
+ * owns [r * experts_per_rank, (r + 1) * experts_per_rank)), the rows of x [T, hidden] bf16 and their
+ * local ids/weights stored into the destinations' receive regions, every flag of this epoch published,
+ * then a bounded wait for every source's rows of this epoch. The local forward then reads the regions
+ * as they lie: ids of rows past a source's count are MOE_ID_NONE. */
+moe_status moe_ep_peer_dispatch_routed(moe_ep_peer* peer, const void* x, int T, const uint32_t* ids,
+                                       const float* weights, int experts_per_rank, uint32_t epoch,
+                                       int32_t* rank_counts, int32_t* token_rows, int32_t* error_word,
+                                       void* stream);
+/* This rank's received slots after moe_ep_peer_dispatch_routed: [world * cap_rows, top_k] local ids
+ * (uint32) and routing weights (float), the layout moe_forward takes. */
+void* moe_ep_peer_recv_ids(moe_ep_peer* peer);
+void* moe_ep_peer_recv_weights(moe_ep_peer* peer);
 /* Source: the plan's rows (rank_counts, send_token, send_ids, send_weights of moe_ep_dispatch_plan)
  * from x [T, hidden] bf16 into the destinations' receive regions, then this epoch's flags. */
 moe_status moe_ep_peer_dispatch(moe_ep_peer* peer, const void* x, int T, const int32_t* rank_counts,
@@ -363,7 +380,8 @@ moe_status moe_ep_peer_receive(moe_ep_peer* peer, uint32_t epoch, uint32_t* ids,
 /* Destination: y_local [world * cap_rows, hidden] bf16 (the local forward's output) back to the sources. */
 moe_status moe_ep_peer_return(moe_ep_peer* peer, const void* y_local, uint32_t epoch, void* stream);
 /* Source: waits for every destination's return of this epoch; y [T, hidden] = y_add (or 0) + the
- * token's returned rows in rank order, f32, rounded once (rank_counts / token_rows of the plan). */
+ * token's returned rows in rank order, f32, rounded once (rank_counts / token_rows of the plan). One
+ * launch; it completes the epoch (T = 0 only waits). */
 moe_status moe_ep_peer_combine(moe_ep_peer* peer, uint32_t epoch, int T, const int32_t* rank_counts,
                                const int32_t* token_rows, const void* y_add, void* y, void* stream);
 /* Synchronises `stream`, then reads and clears the peer status: MOE_OK, MOE_ERR_TIMEOUT (a wait for

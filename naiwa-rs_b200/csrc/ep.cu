@@ -17,22 +17,6 @@ namespace moe {
 constexpr int EP_THREADS = 1024;
 constexpr int EP_MAX_WORLD = 64;
 
-__device__ __forceinline__ uint64_t token_rank_mask(const uint32_t* __restrict__ ids, int t, int k, int epr, int world,
-                                                    int* bad) {
-  uint64_t m = 0;
-  const uint32_t limit = (uint32_t)epr * (uint32_t)world;
-  for (int j = 0; j < k; ++j) {
-    const uint32_t id = ids[(int64_t)t * k + j];
-    if (id == MOE_ID_NONE) continue;
-    if (id >= limit) {
-      *bad = 1;
-      continue;
-    }
-    m |= 1ull << (id / (uint32_t)epr);
-  }
-  return m;
-}
-
 // One CTA of 1024 threads. Pass 1 counts rows per destination rank; pass 2 walks the tokens in
 // chunks of 1024 and, rank by rank, places each chunk's rows after the earlier chunks' rows by a
 // block-wide exclusive scan of "token t has a row for rank r".

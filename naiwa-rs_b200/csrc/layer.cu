@@ -419,19 +419,21 @@ static bool q8_uses_gemm(int n_pairs, int E) {
   return (int64_t)n_pairs >= 8ll * E;
 }
 
-// Below the tcgen05 threshold a Q8_0 unit layer streams its weights either through registers (the
-// decode GEMV, expert_decode.cu) or through a shared-memory ring (expert_stream.cu); both give the
-// same bits. MOE_DECODE=stream|gemv pins the choice.
-static bool decode_uses_stream(int n_pairs, int E) {
+// Below the tcgen05 threshold a Q8_0 unit layer streams its weights through registers (the decode
+// GEMV, expert_decode.cu) or through one shared-memory ring per CTA (expert_stream.cu; measured
+// slower at every decode size on config 2, kept selectable). MOE_DECODE=gemv|stream pins the choice.
+enum DecodeKernel { DECODE_GEMV = 0, DECODE_STREAM = 1 };
+static DecodeKernel decode_kernel(int n_pairs, int E) {
   static const int forced = [] {
     const char* v = std::getenv("MOE_DECODE");
-    if (!v) return 0;
-    return std::string(v) == "stream" ? 1 : std::string(v) == "gemv" ? -1 : 0;
+    if (!v) return -1;
+    const std::string s(v);
+    return s == "stream" ? (int)DECODE_STREAM : s == "gemv" ? (int)DECODE_GEMV : -1;
   }();
-  if (forced) return forced > 0;
+  if (forced >= 0) return (DecodeKernel)forced;
   (void)n_pairs;
   (void)E;
-  return false;
+  return DECODE_GEMV;
 }
 
 moe_status moe_forward(moe_layer* L, const void* x, int T, const uint32_t* ids, const float* weights, int width,
@@ -565,9 +567,12 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   gp.tile_major = L->q8_tiles ? 1 : 0;
   gp.err = L->err;
   auto rowt_of = [&](const ExpertParams& q) { return pick_rowt(q.tiles, q.tpp, est, L->sms); };
-  const bool use_stream = L->q8_tiles && decode_uses_stream(n_live, E);
-  if (use_stream) MOE_TRY(launch_expert_stream(gp, max_active, L->sms, st));
-  else MOE_TRY(launch_expert_gemv(L->d.wdtype, gp, max_active, rowt_of(gp), st));
+  const DecodeKernel dk = L->q8_tiles ? decode_kernel(n_live, E) : DECODE_GEMV;
+  auto launch_pass = [&](const ExpertParams& q) -> moe_status {
+    if (dk == DECODE_STREAM) return launch_expert_stream(q, max_active, L->sms, st);
+    return launch_expert_gemv(L->d.wdtype, q, max_active, rowt_of(q), st);
+  };
+  MOE_TRY(launch_pass(gp));
   MOE_TRY(mark(events, 2, st));
 
   ExpertParams dp = gp;
@@ -585,8 +590,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   dp.h_in = L->h;
   dp.route_w = weights;
   dp.out = L->ypair;
-  if (use_stream) MOE_TRY(launch_expert_stream(dp, max_active, L->sms, st));
-  else MOE_TRY(launch_expert_gemv(L->d.wdtype, dp, max_active, rowt_of(dp), st));
+  MOE_TRY(launch_pass(dp));
   MOE_TRY(mark(events, 3, st));
   if (combine) MOE_TRY(launch_combine(L->ypair, ids, T, width, H, E, y, st, slot_of));
   if (L->slots) MOE_CUDA_TRY(cudaEventRecord(L->last_read, st));  // the slots' readers

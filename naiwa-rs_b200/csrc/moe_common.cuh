@@ -287,6 +287,24 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* 
   return r;
 }
 
+// Expert parallelism: bit r set when token t has a slot whose id falls in rank r's experts
+// [r * epr, (r + 1) * epr); *bad = 1 for an id past world * epr (skipped). world <= 64.
+__device__ __forceinline__ uint64_t token_rank_mask(const uint32_t* __restrict__ ids, int t, int k, int epr, int world,
+                                                    int* bad) {
+  uint64_t m = 0;
+  const uint32_t limit = (uint32_t)epr * (uint32_t)world;
+  for (int j = 0; j < k; ++j) {
+    const uint32_t id = ids[(int64_t)t * k + j];
+    if (id == MOE_ID_NONE) continue;
+    if (id >= limit) {
+      *bad = 1;
+      continue;
+    }
+    m |= 1ull << (id / (uint32_t)epr);
+  }
+  return m;
+}
+
 // A routed pair runs when its id names an expert (< E) that is resident: with an expert cache,
 // slot_of[id] >= 0; without one (slot_of null) every expert is. MOE_ID_NONE and non-resident
 // experts are skipped; ids >= E other than MOE_ID_NONE are the caller's error.

@@ -123,6 +123,9 @@ def lib():
             "moe_ep_peer_recv_rows": (P, [P]),
             "moe_ep_peer_dispatch": (i, [P, P, i, P, P, P, P, ctypes.c_uint32, P]),
             "moe_ep_peer_receive": (i, [P, ctypes.c_uint32, P, P, P]),
+            "moe_ep_peer_dispatch_routed": (i, [P, P, i, P, P, i, ctypes.c_uint32, P, P, P, P]),
+            "moe_ep_peer_recv_ids": (P, [P]),
+            "moe_ep_peer_recv_weights": (P, [P]),
             "moe_ep_peer_return": (i, [P, P, ctypes.c_uint32, P]),
             "moe_ep_peer_combine": (i, [P, ctypes.c_uint32, i, P, P, P, P, P]),
             "moe_ep_peer_check": (i, [P, P]),

@@ -201,15 +201,13 @@ class PeerExpertParallelMoE:
         self.recv_w = torch.empty((R, self.k), dtype=torch.float32, device=dev)
         self.y_local = torch.empty((R, self.H), dtype=torch.bfloat16, device=dev)
         self.recv_rows = lib().moe_ep_peer_recv_rows(self._h)
-        # the dispatch plan's buffers, sized for cap tokens (moe_ep_dispatch_plan)
-        rows = self.cap * min(world, self.k)
+        # the routed dispatch leaves this rank's slots in its own receive regions
+        self.region_ids = lib().moe_ep_peer_recv_ids(self._h)
+        self.region_w = lib().moe_ep_peer_recv_weights(self._h)
+        # the dispatch plan the routed dispatch writes, sized for cap tokens (moe_ep_dispatch_plan's layout)
         self.plan = {
             "rank_counts": torch.empty(world, dtype=torch.int32, device=dev),
-            "n_send": torch.empty(1, dtype=torch.int32, device=dev),
             "token_rows": torch.empty((self.cap, world), dtype=torch.int32, device=dev),
-            "send_token": torch.empty(rows, dtype=torch.int32, device=dev),
-            "send_ids": torch.empty((rows, self.k), dtype=torch.int32, device=dev),
-            "send_w": torch.empty((rows, self.k), dtype=torch.float32, device=dev),
             "error_word": torch.zeros(1, dtype=torch.int32, device=dev),
         }
         # the local forward runs world * cap received rows, about 1 / world of whose slots are live
@@ -223,8 +221,9 @@ class PeerExpertParallelMoE:
         calls), so a captured graph of calls can be replayed; nothing is allocated but the output when
         `out` is not given. `layer` runs this call's local experts instead of the constructor's (one
         exchange object can serve every layer of a stack: calls are ordered on the stream). `marks`:
-        five CUDA events recorded after the dispatch, the receive, the local forward, the return and
-        the combine (per-stage timing)."""
+        four CUDA events recorded after the dispatch (which ends with the receive), the local forward,
+        the return and the combine (per-stage timing; the shared expert, if any, runs between the
+        return and the combine, while the peers' rows come back)."""
         torch = _torch()
         T, H = xs.shape
         if T > self.cap:
@@ -242,27 +241,22 @@ class PeerExpertParallelMoE:
         def mark(i):
             if marks is not None:
                 marks[i].record(stream if stream is not None else torch.cuda.current_stream())
-        check(L.moe_ep_dispatch_plan(_ptr(ids), _ptr(w), T, self.k, self.epr, self.world, _ptr(P["rank_counts"]),
-                                     _ptr(P["n_send"]), _ptr(P["token_rows"]), _ptr(P["send_token"]),
-                                     _ptr(P["send_ids"]), _ptr(P["send_w"]), _ptr(P["error_word"]), st))
-        check(L.moe_ep_peer_dispatch(self._h, _ptr(xs), T, _ptr(P["rank_counts"]), _ptr(P["send_token"]),
-                                     _ptr(P["send_ids"]), _ptr(P["send_w"]), 0, st))
+        check(L.moe_ep_peer_dispatch_routed(self._h, _ptr(xs), T, _ptr(ids), _ptr(w), self.epr, 0,
+                                            _ptr(P["rank_counts"]), _ptr(P["token_rows"]), _ptr(P["error_word"]), st))
         mark(0)
+        R = self.world * self.cap
+        check(L.moe_forward(local._h, ctypes.c_void_p(self.recv_rows), R, ctypes.c_void_p(self.region_ids),
+                            ctypes.c_void_p(self.region_w), self.k, _ptr(self.y_local), st))
+        mark(1)
+        check(L.moe_ep_peer_return(self._h, _ptr(self.y_local), 0, st))
+        mark(2)
         y_shared = None
         if self.shared is not None:
             y_shared = self.shared.forward(xs, self.shared_w[:T], self.shared_ids[:T], stream=stream)
-        check(L.moe_ep_peer_receive(self._h, 0, _ptr(self.recv_ids), _ptr(self.recv_w), st))
-        mark(1)
-        R = self.world * self.cap
-        check(L.moe_forward(local._h, ctypes.c_void_p(self.recv_rows), R, _ptr(self.recv_ids),
-                            _ptr(self.recv_w), self.k, _ptr(self.y_local), st))
-        mark(2)
-        check(L.moe_ep_peer_return(self._h, _ptr(self.y_local), 0, st))
-        mark(3)
         y = out if out is not None else torch.empty((T, H), dtype=torch.bfloat16, device=xs.device)
         check(L.moe_ep_peer_combine(self._h, 0, T, _ptr(P["rank_counts"]), _ptr(P["token_rows"]),
                                     _ptr(y_shared), _ptr(y), st))
-        mark(4)
+        mark(3)
         return y
 
     __call__ = forward

@@ -7,7 +7,9 @@ ranks' receive waits run out after a short limit (moe_ep_peer_set_wait_limit), t
 carry the failed bit, and both combines add no returned row. The test checks, on each rank, that
 moe_ep_peer_check reports MOE_ERR_TIMEOUT, that epoch 2's output is exactly zero (no y_add, no
 returned row), and that epoch 3, on epoch 1's inputs, reproduces epoch 1's output bit for bit.
-Exits non-zero on any mismatch."""
+Epochs 4-6 repeat this through the one-launch routed dispatch (moe_ep_peer_dispatch_routed, whose
+receive is inside it): epoch 4 must equal epoch 1 bit for bit, rank 1 drops its call in epoch 5, and
+epoch 6 must equal epoch 4. Exits non-zero on any mismatch."""
 import ctypes
 import datetime
 import os
@@ -71,6 +73,21 @@ def main():
                                         None, y.data_ptr(), st))
             return y
 
+        R = ctypes.c_void_p(peer.region_ids), ctypes.c_void_p(peer.region_w)
+        P = peer.plan
+
+        def routed(e: int, send: bool):
+            if send:
+                check(L.moe_ep_peer_dispatch_routed(peer._h, x.data_ptr(), T, ids.data_ptr(), w.data_ptr(), E_per, e,
+                                                    P["rank_counts"].data_ptr(), P["token_rows"].data_ptr(),
+                                                    P["error_word"].data_ptr(), st))
+            check(L.moe_forward(layer._h, recv_rows, world * T, R[0], R[1], k, peer.y_local.data_ptr(), st))
+            check(L.moe_ep_peer_return(peer._h, peer.y_local.data_ptr(), e, st))
+            y = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+            check(L.moe_ep_peer_combine(peer._h, e, T, P["rank_counts"].data_ptr(), P["token_rows"].data_ptr(),
+                                        None, y.data_ptr(), st))
+            return y
+
         def status():
             return L.moe_ep_peer_check(peer._h, st)
 
@@ -82,13 +99,27 @@ def main():
         dist.barrier()
         y3 = epoch(3, True)
         s3 = status()
+        dist.barrier()
+        y4 = routed(4, True)
+        s4 = status()
+        dist.barrier()
+        y5 = routed(5, rank != 1)  # rank 1 drops its routed dispatch of epoch 5
+        s5 = status()
+        dist.barrier()
+        y6 = routed(6, True)
+        s6 = status()
         torch.cuda.synchronize()
         zero2 = bool((y2.float() == 0).all())
         same3 = torch.equal(y1, y3)
         nonzero1 = bool((y1.float() != 0).any())
         print(f"rank {rank}: status {s1} {s2} {s3}; epoch-2 output all zero {zero2}; epoch 3 == epoch 1 {same3}",
               flush=True)
-        ok = (s1 == MOE_OK and s2 == MOE_ERR_TIMEOUT and s3 == MOE_OK and zero2 and same3 and nonzero1)
+        zero5 = bool((y5.float() == 0).all())
+        same4, same6 = torch.equal(y4, y1), torch.equal(y6, y4)
+        print(f"rank {rank}: routed status {s4} {s5} {s6}; epoch-5 output all zero {zero5}; epoch 4 == epoch 1 "
+              f"{same4}; epoch 6 == epoch 4 {same6}", flush=True)
+        ok = (s1 == MOE_OK and s2 == MOE_ERR_TIMEOUT and s3 == MOE_OK and zero2 and same3 and nonzero1
+              and s4 == MOE_OK and s5 == MOE_ERR_TIMEOUT and s6 == MOE_OK and zero5 and same4 and same6)
         layer.check()
         flag = torch.tensor([1 if ok else 0], device="cuda")
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)

@@ -1,7 +1,10 @@
 """Worker of tests/test_gpu_ep.py::test_ep_peer_two_ranks (torch.distributed.run, one process per GPU):
 the NVLink peer-memory exchange (PeerExpertParallelMoE) against the NCCL one (ExpertParallelMoE),
 bit for bit, and both against a full-expert layer within the north-star tolerance, over several
-epochs with fresh inputs (region and flag reuse). Exits non-zero on a mismatch."""
+epochs with fresh inputs (region and flag reuse). The plan the one-launch routed dispatch writes
+(rank_counts, token_rows) must equal the oracle's ep_dispatch_plan bit for bit. A last epoch has rank
+1 send no token at all and rank 0 send tokens with an empty (MOE_ID_NONE) slot each. Exits non-zero
+on a mismatch."""
 import datetime
 import os
 import sys
@@ -60,8 +63,31 @@ def main():
             torch.cuda.synchronize()
             same = torch.equal(yp, yn)
             err = float((yp.float() - ref.float()).abs().max() / ref.float().abs().max())
-            print(f"rank {rank} epoch {epoch + 1}: peer == nccl {same}, rel err vs full {err:.2e}", flush=True)
-            ok = ok and same and err < 1e-2
+            rc, tr, _, _, _ = O.ep_dispatch_plan(ids.cpu().numpy().view(np.uint32), w.cpu().numpy(), E_per, world)
+            plan_ok = (np.array_equal(peer_ep.plan["rank_counts"].cpu().numpy(), rc)
+                       and np.array_equal(peer_ep.plan["token_rows"][:Tn].cpu().numpy(), tr))
+            print(f"rank {rank} epoch {epoch + 1}: peer == nccl {same}, plan == oracle {plan_ok}, "
+                  f"rel err vs full {err:.2e}", flush=True)
+            ok = ok and same and plan_ok and err < 1e-2
+        # ragged extreme: rank 1 sends nothing; rank 0's tokens each carry one empty slot
+        Tn = 17 if rank == 0 else 0
+        x = torch.from_numpy(O.f32_to_bf16(r2.normal(0, 1, (Tn, H)).astype(np.float32)).view(np.int16)) \
+            .view(torch.bfloat16).cuda()
+        idn = np.array([r2.permutation(E)[:k] for _ in range(Tn)], dtype=np.int64).reshape(Tn, k)
+        idn[:, 1] = O.ID_NONE
+        ids = torch.from_numpy(idn.astype(np.uint32).view(np.int32)).cuda()
+        w = torch.from_numpy(r2.dirichlet(np.ones(k), Tn).astype(np.float32).reshape(Tn, k)).cuda()
+        yp = peer_ep.forward(x, w, ids)
+        torch.cuda.synchronize()
+        if Tn:
+            ref = full.forward(x, w, ids)
+            torch.cuda.synchronize()
+            err = float((yp.float() - ref.float()).abs().max() / ref.float().abs().max())
+            print(f"rank {rank} ragged epoch: rel err vs full {err:.2e}", flush=True)
+            ok = ok and err < 1e-2
+        else:
+            print(f"rank {rank} ragged epoch: sent no token, output {tuple(yp.shape)}", flush=True)
+            ok = ok and tuple(yp.shape) == (0, H)
         peer_ep.check()
         flag = torch.tensor([1 if ok else 0], device="cuda")
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
