@@ -20,12 +20,18 @@
 // partial sum, so the weights are never rounded. Activations are staged as f16 with a per-token
 // power-of-two scale (a bf16 value scaled into f16's range is exact); the scale is undone in the
 // epilogue. BF16 weights feed bf16 MMAs with bf16 activations unchanged.
+#include <type_traits>
+
 #include "expert_frag.cuh"
 
 namespace moe {
 
-template <class WT, int ROWT, int NTM, int WARPS>
+// PH: the pass (0 gate/up, 1 down) fixed at compile time, or -1 to read p.phase. Q8_0 units compile
+// one kernel per pass, so each carries only its own token staging: gate/up copies rows converted
+// by the plan launch (stage_prepped), down loads its f32 rows in one batch (stage_row_f32_batched).
+template <class WT, int ROWT, int NTM, int WARPS, int PH>
 __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(ExpertParams p) {
+  const int phase = PH >= 0 ? PH : p.phase;
   constexpr int KS = WARPS / ROWT;
   constexpr int THREADS = WARPS * 32;
   constexpr int STAGES = 3;
@@ -36,7 +42,7 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(Exp
   // Gate/up follows the plan directly: wait for it. Down follows gate/up, so the plan (two kernels
   // back) has completed when it starts: it reads the plan's outputs through L2 and issues its first
   // weight loads before waiting for gate/up's h.
-  if (p.phase == 0) {
+  if (phase == 0) {
     pdl_wait();
     pdl_trigger();
   }
@@ -72,15 +78,24 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(Exp
       WT::load(p, es, tile, kb_begin, kb_end, lane, st[0]);
       WT::load(p, es, tile, kb_begin + G, kb_end, lane, st[1]);
     }
-    if (p.phase == 1 && p0 == 0) {  // h and the ypair rows belong to gate/up's grid until it completes
+    if (phase == 1 && p0 == 0) {  // h and the ypair rows belong to gate/up's grid until it completes
       pdl_wait();
       pdl_trigger();
     }
     if (threadIdx.x < tpp) spair[threadIdx.x] = threadIdx.x < ntok ? p.perm[base + p0 + threadIdx.x] : -1;
     for (int n = warp; n < ntok; n += WARPS) {
-      const int src = p.phase == 0 ? p.perm[base + p0 + n] / p.width : base + p0 + n;
-      stage_row<WT::kF16>(p, n, src, xs, ntm, tscale, lane);
+      const int src = phase == 0 ? p.perm[base + p0 + n] / p.width : base + p0 + n;
+      if constexpr (PH == 0) {
+        if (p.xq) stage_prepped(p, n, src, xs, ntm, tscale, lane);
+        else stage_row<WT::kF16>(p, n, src, xs, ntm, tscale, lane);
+      } else if constexpr (PH == 1) {
+        if (p.K <= 1024) stage_row_f32_batched(p, n, src, xs, ntm, tscale, lane);
+        else stage_row<WT::kF16>(p, n, src, xs, ntm, tscale, lane);
+      } else {
+        stage_row<WT::kF16>(p, n, src, xs, ntm, tscale, lane);
+      }
     }
+    if (PH == 0 && p.xq) cp_async_wait_all();
     __syncthreads();
 
     float acc[NTM][4];
@@ -108,7 +123,7 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(Exp
             const int n = t * 8 + 2 * c + j;
             if (t < nt_used && n < ntok) {
               const float sc = tscale[n];
-              if (p.phase == 0) {
+              if (phase == 0) {
                 const float gv = acc[t][j] * sc, uv = acc[t][2 + j] * sc;
                 const int I = p.N >> 1;
                 p.out[(int64_t)(base + p0 + n) * I + tile * 8 + g] = gv / (1.0f + __expf(-gv)) * uv;
@@ -134,7 +149,7 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(Exp
         r[(g + 8) * tpp + n0 + 1] = acc[t][3];
       }
       __syncthreads();
-      if (p.phase == 0) {
+      if (phase == 0) {
         const int cols = ROWT * 8;
         const int I = p.N >> 1;
         for (int i = threadIdx.x; i < ntok * cols; i += THREADS) {
@@ -210,18 +225,27 @@ size_t expert_smem_bytes(int K, int tpp, int rowt, int warps) {
   return (size_t)K * tpp * 2 + (ks > 1 ? (size_t)warps * 16 * tpp * 4 : 0) + MAX_TPP * 4 * 2 + 64;
 }
 
-template <class WT, int ROWT, int NTM, int WARPS>
-static moe_status launch3(const ExpertParams& p, int grid, size_t smem, cudaStream_t st) {
+template <class WT, int ROWT, int NTM, int WARPS, int PH>
+static moe_status launch4(const ExpertParams& p, int grid, size_t smem, cudaStream_t st) {
   static bool attr[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr[dev & 63]) {
-    MOE_CUDA_TRY(cudaFuncSetAttribute(expert_gemv_kernel<WT, ROWT, NTM, WARPS>,
+    MOE_CUDA_TRY(cudaFuncSetAttribute(expert_gemv_kernel<WT, ROWT, NTM, WARPS, PH>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     attr[dev & 63] = true;
   }
-  MOE_CUDA_TRY(launch_pdl(expert_gemv_kernel<WT, ROWT, NTM, WARPS>, dim3(grid), dim3(WARPS * 32), smem, st, p));
+  MOE_CUDA_TRY(launch_pdl(expert_gemv_kernel<WT, ROWT, NTM, WARPS, PH>, dim3(grid), dim3(WARPS * 32), smem, st, p));
   return MOE_OK;
+}
+
+template <class WT, int ROWT, int NTM, int WARPS>
+static moe_status launch3(const ExpertParams& p, int grid, size_t smem, cudaStream_t st) {
+  if constexpr (std::is_same<WT, WQ8U>::value) {
+    if (p.phase == 0) return launch4<WT, ROWT, NTM, WARPS, 0>(p, grid, smem, st);
+    return launch4<WT, ROWT, NTM, WARPS, 1>(p, grid, smem, st);
+  }
+  return launch4<WT, ROWT, NTM, WARPS, -1>(p, grid, smem, st);
 }
 
 template <class WT, int ROWT, int WARPS>

@@ -154,6 +154,73 @@ __device__ __forceinline__ void load_chunk(const ExpertParams& p, int src_row, i
   }
 }
 
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// One warp stages one token row converted beforehand (TokenPrep, plan.cu): the row's 16-byte pieces
+// go straight to their B-fragment slots by asynchronous copies, all in flight together, and the
+// row's scale is the one the conversion picked. The caller waits (cp_async_wait_all) and syncs.
+__device__ __forceinline__ void stage_prepped(const ExpertParams& p, int n, int src_row, uint32_t* xs, int ntm,
+                                              float* tscale, int lane) {
+  const int pieces = p.K >> 3;  // per 32-column block four pieces of 16 bytes
+  const uint4* srow = reinterpret_cast<const uint4*>(p.xq) + (size_t)src_row * pieces;
+  const int nt = n >> 3, g = n & 7;
+  for (int i = lane; i < pieces; i += 32) {
+    const int kb = i >> 2, c = i & 3;
+    cp_async16(xs + ((kb * ntm + nt) * 32 + g * 4 + c) * 4, srow + i);
+  }
+  if (lane == 0) tscale[n] = p.xq_scale[src_row];
+}
+
+// One warp stages one f32 row of at most 1024 values (the down pass's h) exactly as stage_row<true>
+// does (same scale, same f16 values, same layout), with the lane's whole share loaded at once
+// instead of one L2 round trip per chunk, twice.
+__device__ __forceinline__ void stage_row_f32_batched(const ExpertParams& p, int n, int src_row, uint32_t* xs,
+                                                      int ntm, float* tscale, int lane) {
+  constexpr int MAXC = 4;
+  const int chunks = p.K >> 3;
+  float4 v[MAXC][2];
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = lane + 32 * i;
+    if (c < chunks) {
+      const float4* src = reinterpret_cast<const float4*>(p.h_in + (int64_t)src_row * p.K + c * 8);
+      v[i][0] = src[0];
+      v[i][1] = src[1];
+    }
+  }
+  float m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i)
+    if (lane + 32 * i < chunks)
+      m = fmaxf(fmaxf(fmaxf(m, fmaxf(fabsf(v[i][0].x), fabsf(v[i][0].y))), fmaxf(fabsf(v[i][0].z), fabsf(v[i][0].w))),
+                fmaxf(fmaxf(fabsf(v[i][1].x), fabsf(v[i][1].y)), fmaxf(fabsf(v[i][1].z), fabsf(v[i][1].w))));
+  m = warp_max(m);
+  float inv = 1.0f, sc = 1.0f;
+  if (m > 0.0f && m < __int_as_float(0x7f800000)) {
+    int ex;
+    frexpf(m, &ex);  // m < 2^ex
+    const int sh = max(-100, min(100, ex - 14));
+    sc = ldexpf(1.0f, sh);
+    inv = ldexpf(1.0f, -sh);
+  }
+  if (lane == 0) tscale[n] = sc;
+  const int nt = n >> 3, g = n & 7;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = lane + 32 * i;
+    if (c >= chunks) continue;
+    const int kb = c >> 2, s = (c >> 1) & 1, h = c & 1;
+    uint32_t* dst = xs + ((kb * ntm + nt) * 32 + g * 4) * 4 + s * 2 + h;
+    dst[0] = pack_f16x2(v[i][0].x * inv, v[i][0].y * inv);
+    dst[4] = pack_f16x2(v[i][0].z * inv, v[i][0].w * inv);
+    dst[8] = pack_f16x2(v[i][1].x * inv, v[i][1].y * inv);
+    dst[12] = pack_f16x2(v[i][1].z * inv, v[i][1].w * inv);
+  }
+}
+
 // One warp stages one token row: (f16 path) the row's max magnitude gives a power-of-two scale
 // that puts the row in [2^13, 2^14); the second sweep re-reads the row (L1/L2 hit), converts and
 // scatters it into B-fragment order.

@@ -58,6 +58,10 @@ static void free_scratch(moe_layer* L) {
   cudaFree(L->plan_ws);
   cudaFree(L->h);
   cudaFree(L->ypair);
+  cudaFree(L->xq);
+  cudaFree(L->xq_scale);
+  L->xq = nullptr;
+  L->xq_scale = nullptr;
   cudaFree(L->route_ws);
   L->route_ws = nullptr;
   L->route_ws_bytes = 0;
@@ -107,6 +111,10 @@ static moe_status alloc_scratch(moe_layer* L, int max_tokens) {
   MOE_TRY(dalloc(&L->plan_ws, L->plan_ws_bytes, &acc));
   MOE_TRY(dalloc(&L->h, sizeof(float) * (size_t)cap * I, &acc));
   MOE_TRY(dalloc(&L->ypair, sizeof(float) * (size_t)cap * H, &acc));
+  if (L->q8_tiles) {  // a call has at most cap rows (width >= 1)
+    MOE_TRY(dalloc(&L->xq, (size_t)cap * H * 2, &acc));
+    MOE_TRY(dalloc(&L->xq_scale, sizeof(float) * cap, &acc));
+  }
   L->route_ws_bytes = route_workspace_bytes(max_tokens, E);
   MOE_TRY(dalloc(&L->route_ws, L->route_ws_bytes, &acc));
   MOE_CUDA_TRY(cudaMemset(L->route_ws, 0, L->route_ws_bytes));  // arrival counters start at zero
@@ -489,16 +497,21 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
       L->copies_pending = false;
     }
   }
-  PlanOut po{L->counts, L->offsets, L->perm, L->active, L->n_active, L->err, slot_of};
-  MOE_TRY(mark(events, 0, st));
-  MOE_TRY(plan_pairs(ids, n_pairs, E, po, L->plan_ws, L->plan_ws_bytes, st));
-  MOE_TRY(mark(events, 1, st));
   const int max_active = n_pairs < E ? n_pairs : E;
   // the kernel-path choices below follow the pairs expected to be live (moe_layer_set_live_hint);
   // grid bounds keep using every slot
   const int n_live = L->live_hint < 1.0f ? std::max(1, (int)((double)n_pairs * L->live_hint)) : n_pairs;
   const double est = (double)E * (1.0 - std::pow(1.0 - 1.0 / E, (double)n_live));
-  if (L->tc && (!L->q8_tiles || q8_uses_gemm(n_live, E))) {
+  const bool use_tc = L->tc && (!L->q8_tiles || q8_uses_gemm(n_live, E));
+  const DecodeKernel dk = L->q8_tiles ? decode_kernel(n_live, E) : DECODE_GEMV;
+  // the decode GEMV on Q8_0 units stages tokens converted once by the plan launch
+  const bool prep = !use_tc && L->q8_tiles && dk == DECODE_GEMV && L->xq && plan_preps_tokens(n_pairs);
+  const TokenPrep tp{static_cast<const __nv_bfloat16*>(x), T, H, L->xq, L->xq_scale};
+  PlanOut po{L->counts, L->offsets, L->perm, L->active, L->n_active, L->err, slot_of};
+  MOE_TRY(mark(events, 0, st));
+  MOE_TRY(plan_pairs(ids, n_pairs, E, po, L->plan_ws, L->plan_ws_bytes, st, prep ? &tp : nullptr));
+  MOE_TRY(mark(events, 1, st));
+  if (use_tc) {
     const int w = L->d.wdtype;
     const int bn = tc_token_tile(n_live, E);
     MOE_TRY(tc_tile_list(L->counts, L->active, L->n_active, bn, L->tile_list, L->n_tiles, st));
@@ -565,9 +578,12 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   gp.n_active = L->n_active;
   gp.slot_of = slot_of;
   gp.tile_major = L->q8_tiles ? 1 : 0;
+  if (prep) {
+    gp.xq = L->xq;
+    gp.xq_scale = L->xq_scale;
+  }
   gp.err = L->err;
   auto rowt_of = [&](const ExpertParams& q) { return pick_rowt(q.tiles, q.tpp, est, L->sms); };
-  const DecodeKernel dk = L->q8_tiles ? decode_kernel(n_live, E) : DECODE_GEMV;
   auto launch_pass = [&](const ExpertParams& q) -> moe_status {
     if (dk == DECODE_STREAM) return launch_expert_stream(q, max_active, L->sms, st);
     return launch_expert_gemv(L->d.wdtype, q, max_active, rowt_of(q), st);
@@ -587,6 +603,8 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   dp.phase = 1;
   dp.tpp = choose_tpp(I, n_live / (est > 1.0 ? est : 1.0));
   dp.x = nullptr;
+  dp.xq = nullptr;
+  dp.xq_scale = nullptr;
   dp.h_in = L->h;
   dp.route_w = weights;
   dp.out = L->ypair;

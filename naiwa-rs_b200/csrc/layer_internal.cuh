@@ -44,6 +44,8 @@ struct moe_layer {
   size_t plan_ws_bytes = 0;
   float* h = nullptr;
   float* ypair = nullptr;
+  uint32_t* xq = nullptr;     // Q8_0 units: token rows converted by the plan launch for the decode GEMV
+  float* xq_scale = nullptr;
   void* route_ws = nullptr;
   size_t route_ws_bytes = 0;
   // tensor-core path (Q4_K / FP8 / Q8_0 at 128-multiples): tile-major weights, f16 staging, TMA maps

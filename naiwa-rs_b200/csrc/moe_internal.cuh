@@ -27,8 +27,21 @@ struct PlanOut {
   int32_t* err;       // [1] or null
   const int32_t* slot_of = nullptr;  // [E] cache slot of each expert (-1: not resident) or null (all resident)
 };
+// Token rows converted once per call for the decode GEMV's gate/up pass: each row's values scaled by
+// a power of two into f16 (the scale that stage_row picks) and laid out in B-fragment block order,
+// per 32-column block kb 64 bytes whose 16-byte piece c holds the (k, k+1) pairs
+// k = 32 kb + 16 s + 8 h + 2 c at word 2 s + h. A CTA then stages a token with 16-byte copies.
+struct TokenPrep {
+  const __nv_bfloat16* x;  // [T, K]
+  int T, K;
+  uint32_t* xq;            // [T, K / 2] words
+  float* scale;            // [T]
+};
+// prep (optional): the single-CTA plan launch also converts the token rows, in extra CTAs.
 moe_status plan_pairs(const uint32_t* ids, int n_pairs, int E, const PlanOut& o, void* ws, size_t ws_bytes,
-                      cudaStream_t st);
+                      cudaStream_t st, const TokenPrep* prep = nullptr);
+// Whether plan_pairs converts the rows for a call of n_pairs pairs (its single-CTA path).
+bool plan_preps_tokens(int n_pairs);
 size_t plan_workspace_bytes(int n_pairs, int E);
 
 struct ExpertParams {
@@ -56,6 +69,8 @@ struct ExpertParams {
   const int32_t* slot_of;     // [E] cache slot of each expert, or null: weights indexed by expert id
   int tile_major;             // Q8_0 only: weights in 128 x 128 units (repack_q8_units)
   int32_t* err;               // [1] error word (a bounded wait that ran out), or null
+  const uint32_t* xq = nullptr;     // phase 0, Q8_0 units: the TokenPrep rows (null: stage from x)
+  const float* xq_scale = nullptr;  // their scales
 };
 moe_status launch_expert_gemv(int wdtype, ExpertParams p, int max_active, int rowt, cudaStream_t st);
 // The Q8_0 unit-layout pass through a shared-memory weight stream (expert_stream.cu): same results

@@ -56,11 +56,78 @@ __device__ __forceinline__ void rank_chunk(const uint32_t* __restrict__ ids, int
 }
 
 
-// Whole plan in one CTA (n_pairs <= PLAN_SINGLE_MAX).
+// One warp converts token row t of a TokenPrep: the row's largest magnitude gives the power-of-two
+// scale that puts it in [2^13, 2^14) (stage_row's rule, so the f16 values are the same bits), then
+// every (k, k+1) pair goes to its word in the block-ordered row. Rows of up to 2048 values are
+// loaded once, every load in flight together; longer rows are read twice.
+__device__ void prep_row(const TokenPrep& q, int t, int lane) {
+  constexpr int MAXC = 8;
+  const int chunks = q.K >> 3;
+  const __nv_bfloat16* row = q.x + (size_t)t * q.K;
+  uint32_t* out = q.xq + (size_t)t * (q.K >> 1);
+  uint4 raw[MAXC];
+  float m = 0.0f;
+  for (int c0 = 0; c0 < chunks; c0 += 32 * MAXC) {
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = c0 + lane + 32 * i;
+      if (c < chunks) raw[i] = ldg_nc(row + c * 8);
+    }
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      if (c0 + lane + 32 * i >= chunks) continue;
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(b2[j]);
+        m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+  }
+  m = warp_max(m);
+  float inv = 1.0f, sc = 1.0f;
+  if (m > 0.0f && m < __int_as_float(0x7f800000)) {
+    int ex;
+    frexpf(m, &ex);  // m < 2^ex
+    const int sh = max(-100, min(100, ex - 14));
+    sc = ldexpf(1.0f, sh);
+    inv = ldexpf(1.0f, -sh);
+  }
+  if (lane == 0) q.scale[t] = sc;
+  for (int c0 = 0; c0 < chunks; c0 += 32 * MAXC) {
+    if (chunks > 32 * MAXC) {  // the row did not fit the registers: read this round again
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = c0 + lane + 32 * i;
+        if (c < chunks) raw[i] = ldg_nc(row + c * 8);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = c0 + lane + 32 * i;
+      if (c >= chunks) continue;
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
+      const int kb = c >> 2, s = (c >> 1) & 1, h = c & 1;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(b2[j]);
+        out[(kb * 4 + j) * 4 + s * 2 + h] = pack_f16x2(f.x * inv, f.y * inv);
+      }
+    }
+  }
+}
+
+// Whole plan in one CTA (n_pairs <= PLAN_SINGLE_MAX); CTAs 1.. convert the token rows of `prep`
+// (one warp per row) when it is given.
 __global__ void __launch_bounds__(PLAN_THREADS) plan_single_kernel(const uint32_t* __restrict__ ids, int n_pairs,
-                                                                    int E, PlanOut o) {
-  pdl_wait();  // ids (and, for the later passes, the earlier passes' output)
+                                                                    int E, PlanOut o, TokenPrep prep) {
+  pdl_wait();  // ids and x (and, for the later passes, the earlier passes' output)
   pdl_trigger();
+  if (blockIdx.x > 0) {
+    const int t = (blockIdx.x - 1) * PLAN_WARPS + (threadIdx.x >> 5);
+    if (t < prep.T) prep_row(prep, t, threadIdx.x & 31);
+    return;
+  }
   extern __shared__ int psm[];
   int* cnt = psm;                      // [E]
   int* base = cnt + PLAN_MAX_E;        // [E]
@@ -161,8 +228,10 @@ size_t plan_workspace_bytes(int n_pairs, int E) {
 static size_t single_smem(int E) { return (size_t)(2 * PLAN_MAX_E + 64 + (PLAN_WARPS + 1) * E) * sizeof(int); }
 static size_t scatter_smem(int E) { return (size_t)(PLAN_MAX_E + (PLAN_WARPS + 1) * E) * sizeof(int); }
 
+bool plan_preps_tokens(int n_pairs) { return n_pairs <= PLAN_SINGLE_MAX; }
+
 moe_status plan_pairs(const uint32_t* ids, int n_pairs, int E, const PlanOut& o, void* ws, size_t ws_bytes,
-                      cudaStream_t st) {
+                      cudaStream_t st, const TokenPrep* prep) {
   if (E <= 0 || E > PLAN_MAX_E) return fail(MOE_ERR_INVALID, "moe_plan_pairs: need 0 < E <= 1024");
   if (n_pairs < 0) return fail(MOE_ERR_INVALID, "moe_plan_pairs: n_pairs < 0");
   if (!o.counts || !o.offsets || !o.perm || !o.active || !o.n_active)
@@ -182,7 +251,16 @@ moe_status plan_pairs(const uint32_t* ids, int n_pairs, int E, const PlanOut& o,
     attr_done[dev & 63] = true;
   }
   if (n_pairs <= PLAN_SINGLE_MAX) {
-    MOE_CUDA_TRY(launch_pdl(plan_single_kernel, dim3(1), dim3(PLAN_THREADS), single_smem(E), st, ids, n_pairs, E, o));
+    TokenPrep tp{};
+    int grid = 1;
+    if (prep && prep->T > 0) {
+      if (!prep->x || !prep->xq || !prep->scale || prep->K % 32 || ((uintptr_t)prep->x & 15))
+        return fail(MOE_ERR_INVALID, "plan_pairs: bad token rows to convert");
+      tp = *prep;
+      grid += ceil_div(prep->T, PLAN_WARPS);
+    }
+    MOE_CUDA_TRY(launch_pdl(plan_single_kernel, dim3(grid), dim3(PLAN_THREADS), single_smem(E), st, ids, n_pairs, E, o,
+                            tp));
     MOE_CUDA_TRY(cudaGetLastError());
     return MOE_OK;
   }
