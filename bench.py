@@ -423,9 +423,9 @@ def run_ours(args):
     torch.cuda.synchronize()
     weight_bytes = {T: local_distinct[T] * BYTES_PER_EXPERT for T in RAGGED}
     # DRAM bytes (read + write) over algorithmic weight bytes in one ncu --set full capture of each
-    # path on this workload: the GEMV at T = 32 (371.6 / 367.7 MB gate/up, 188.5 / 183.8 MB down) and
+    # path on this workload: the GEMV at T = 32 (373.2 / 367.7 MB gate/up, 190.7 / 183.8 MB down) and
     # the tcgen05 GEMM at T = 256 (446.9 / 427.8 MB gate/up, 227.5 / 213.9 MB down)
-    gemv_ratio, gemm_ratio = (371.6 + 188.5) / (367.7 + 183.8), (446.9 + 227.5) / (427.8 + 213.9)
+    gemv_ratio, gemm_ratio = (373.2 + 190.7) / (367.7 + 183.8), (446.9 + 227.5) / (427.8 + 213.9)
     traffic_per_step = sum(weight_bytes[T] * (gemm_ratio if T * K_TOP * world >= 8 * E else gemv_ratio)
                            for T in RAGGED)
 
