@@ -16,6 +16,7 @@
 
 #include "layer_internal.cuh"
 #include <cmath>
+#include <sys/mman.h>
 
 namespace moe {
 
@@ -145,13 +146,44 @@ moe_status moe::launch_slot_edits(int32_t* slot_of, const SlotEdits& ed, cudaStr
   return MOE_OK;
 }
 
+// Pinned host memory for the expert store. The reference advises the kernel to back its pinned
+// expert stacks with transparent huge pages before pinning them (host_memory.rs:30-55): the DMA
+// engine then walks a 2 MiB page per 2 MiB of experts instead of 512 small ones, and pinning is
+// faster. Here: an anonymous mapping rounded up to 2 MiB, madvise(MADV_HUGEPAGE) (advice only; a
+// kernel without transparent huge pages ignores it), then cudaHostRegister. If the mapping or the
+// registration fails, cudaHostAlloc as before. The block's length is recorded so that free_cache
+// undoes whichever was done.
+static moe_status host_pin_alloc(moe_layer* L, size_t bytes, void** out) {
+  constexpr size_t kHugePage = 2u << 20;
+  const size_t len = (bytes + kHugePage - 1) / kHugePage * kHugePage;
+  void* p = mmap(nullptr, len, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS, -1, 0);
+  if (p != MAP_FAILED) {
+#ifdef MADV_HUGEPAGE
+    madvise(p, len, MADV_HUGEPAGE);
+#endif
+    if (cudaHostRegister(p, len, cudaHostRegisterPortable) == cudaSuccess) {
+      L->hs_blocks.emplace_back(p, len);
+      *out = p;
+      return MOE_OK;
+    }
+    cudaGetLastError();  // clear the failed registration
+    munmap(p, len);
+  }
+  MOE_CUDA_TRY(cudaHostAlloc(out, bytes, cudaHostAllocPortable));
+  L->hs_blocks.emplace_back(*out, 0);
+  return MOE_OK;
+}
+
 static void free_cache(moe_layer* L) {
-  if (L->hs_gu_q) cudaFreeHost(L->hs_gu_q);
-  if (L->hs_gu_s) cudaFreeHost(L->hs_gu_s);
-  if (L->hs_dn_q) cudaFreeHost(L->hs_dn_q);
-  if (L->hs_dn_s) cudaFreeHost(L->hs_dn_s);
-  if (L->hs_gu_scale) cudaFreeHost(L->hs_gu_scale);
-  if (L->hs_dn_scale) cudaFreeHost(L->hs_dn_scale);
+  for (auto& b : L->hs_blocks) {
+    if (b.second) {
+      cudaHostUnregister(b.first);
+      munmap(b.first, b.second);
+    } else {
+      cudaFreeHost(b.first);
+    }
+  }
+  L->hs_blocks.clear();
   L->hs_gu_q = L->hs_gu_s = L->hs_dn_q = L->hs_dn_s = nullptr;
   L->hs_gu_scale = L->hs_dn_scale = nullptr;
   cudaFree(L->slot_of);
@@ -165,10 +197,11 @@ static void free_cache(moe_layer* L) {
 
 // Moves a projection's E-expert device buffer into pinned host memory and replaces it by a bank of
 // `slots` experts. stride: bytes per expert.
-static moe_status to_host_store(uint8_t** dev_buf, uint8_t** host_buf, int64_t stride, int E, int slots, int64_t* acct) {
+static moe_status to_host_store(moe_layer* L, uint8_t** dev_buf, uint8_t** host_buf, int64_t stride, int E, int slots,
+                                int64_t* acct) {
   if (!*dev_buf || stride == 0) return MOE_OK;
   void* h = nullptr;
-  MOE_CUDA_TRY(cudaHostAlloc(&h, (size_t)(stride * E), cudaHostAllocPortable));
+  MOE_TRY(host_pin_alloc(L, (size_t)(stride * E), &h));
   *host_buf = static_cast<uint8_t*>(h);
   MOE_CUDA_TRY(cudaMemcpy(h, *dev_buf, (size_t)(stride * E), cudaMemcpyDeviceToHost));
   cudaFree(*dev_buf);
@@ -179,19 +212,19 @@ static moe_status to_host_store(uint8_t** dev_buf, uint8_t** host_buf, int64_t s
 
 static moe_status setup_cache(moe_layer* L, int64_t* acct) {
   const int E = L->d.num_experts, S = L->slots;
-  MOE_TRY(to_host_store(&L->gu_q, &L->hs_gu_q, L->gu_q_stride, E, S, acct));
-  MOE_TRY(to_host_store(&L->gu_s, &L->hs_gu_s, L->gu_s_stride, E, S, acct));
-  MOE_TRY(to_host_store(&L->dn_q, &L->hs_dn_q, L->dn_q_stride, E, S, acct));
-  MOE_TRY(to_host_store(&L->dn_s, &L->hs_dn_s, L->dn_s_stride, E, S, acct));
+  MOE_TRY(to_host_store(L, &L->gu_q, &L->hs_gu_q, L->gu_q_stride, E, S, acct));
+  MOE_TRY(to_host_store(L, &L->gu_s, &L->hs_gu_s, L->gu_s_stride, E, S, acct));
+  MOE_TRY(to_host_store(L, &L->dn_q, &L->hs_dn_q, L->dn_q_stride, E, S, acct));
+  MOE_TRY(to_host_store(L, &L->dn_s, &L->hs_dn_s, L->dn_s_stride, E, S, acct));
   if (L->gu_scale) {
     uint8_t* g = reinterpret_cast<uint8_t*>(L->gu_scale);
     uint8_t* hg = nullptr;
-    MOE_TRY(to_host_store(&g, &hg, L->gu_scale_stride * 4, E, S, acct));
+    MOE_TRY(to_host_store(L, &g, &hg, L->gu_scale_stride * 4, E, S, acct));
     L->gu_scale = reinterpret_cast<float*>(g);
     L->hs_gu_scale = reinterpret_cast<float*>(hg);
     uint8_t* d = reinterpret_cast<uint8_t*>(L->dn_scale);
     uint8_t* hd = nullptr;
-    MOE_TRY(to_host_store(&d, &hd, L->dn_scale_stride * 4, E, S, acct));
+    MOE_TRY(to_host_store(L, &d, &hd, L->dn_scale_stride * 4, E, S, acct));
     L->dn_scale = reinterpret_cast<float*>(d);
     L->hs_dn_scale = reinterpret_cast<float*>(hd);
   }

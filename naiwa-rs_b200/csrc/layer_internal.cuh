@@ -75,6 +75,8 @@ struct moe_layer {
   uint8_t* hs_dn_s = nullptr;
   float* hs_gu_scale = nullptr;
   float* hs_dn_scale = nullptr;
+  // how each host-store buffer was pinned: mapped + registered (length > 0) or cudaHostAlloc (0)
+  std::vector<std::pair<void*, size_t>> hs_blocks;
   int64_t gu_scale_stride = 0, dn_scale_stride = 0;  // floats per expert (tensor-core FP8 scales)
   int32_t* slot_of = nullptr;                         // device [E]
   std::vector<int> slot_expert;                       // [slots], -1 empty
