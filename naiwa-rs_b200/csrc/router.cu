@@ -15,6 +15,8 @@
 // meet in an xor butterfly 16,8,4,2,1), which the oracle restates operation for operation.
 // Selection is a warp argmax over 64-bit keys (total-order value, then lowest index), so ids are
 // exact; weights use det_exp and IEEE-rounded division and are exact as well.
+#include <cstdlib>
+
 #include "moe_internal.cuh"
 
 namespace moe {
@@ -148,29 +150,104 @@ __device__ void select_token(const RouteParams& p, float* l, float* a, uint32_t*
 // ws_count_end[-1 - b], the end of the workspace counting down: its address does not depend on T, so
 // a workspace reused with another T keeps every counter at zero between calls (at the front, after
 // the logits, a shorter call's counters would land on a longer call's logits)
-template <int TB>
+// EW experts per warp (EB = 8 EW per CTA). EW = 1: tokens staged as bf16 and converted at each use
+// (latency-bound small batches, most CTAs). EW = 2 (TB >= 4): the block's tokens staged once as f32
+// in two float4 planes per token (xf[t][q][c] = elements 4q..4q+3 of chunk c, so a warp's loads are
+// conflict-free) and each warp's two router rows applied to every staged token, which halves the
+// conversions and shared-memory reads per multiply-add. Every logit sees the same operations in the
+// same order either way.
+template <int TB, int EW>
 __global__ void __launch_bounds__(ROUTER_THREADS) route_kernel(RouteParams p, float* __restrict__ ws_logits,
                                                                unsigned* __restrict__ ws_count_end) {
+  constexpr int EB = ROUTER_EB * EW;
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ int s_last;
   const int H = p.H, E = p.E;
   const int t0 = blockIdx.x * TB;
   const int nt = min(TB, p.T - t0);
-  const int e0 = blockIdx.y * ROUTER_EB;
+  const int e0 = blockIdx.y * EB;
   const int chunks = H / 8;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  uint4* xs = reinterpret_cast<uint4*>(smem);  // [TB][H/8]
+  uint4* xs = reinterpret_cast<uint4*>(smem);  // EW = 1: [TB][H/8] bf16 chunks
+  float4* xf = reinterpret_cast<float4*>(smem);  // EW = 2: [TB][2][H/8]
   pdl_wait();  // x may come from the kernel before
   pdl_trigger();
 
   for (int i = threadIdx.x; i < TB * chunks; i += ROUTER_THREADS) {
     const int t = i / chunks, c = i - t * chunks;
-    xs[i] = t < nt ? ldg_nc(p.x + (size_t)(t0 + t) * H + c * 8) : make_uint4(0, 0, 0, 0);
+    const uint4 v = t < nt ? ldg_nc(p.x + (size_t)(t0 + t) * H + c * 8) : make_uint4(0, 0, 0, 0);
+    if constexpr (EW == 1) {
+      xs[i] = v;
+    } else {
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+      const float2 a = __bfloat1622float2(h2[0]), b = __bfloat1622float2(h2[1]);
+      const float2 cc = __bfloat1622float2(h2[2]), d = __bfloat1622float2(h2[3]);
+      xf[(t * 2) * chunks + c] = make_float4(a.x, a.y, b.x, b.y);
+      xf[(t * 2 + 1) * chunks + c] = make_float4(cc.x, cc.y, d.x, d.y);
+    }
   }
   __syncthreads();
 
-  // each warp owns experts e0 + warp, e0 + warp + 8; chunk loads are issued four at a time
-  for (int e = e0 + warp; e < min(E, e0 + ROUTER_EB); e += ROUTER_WARPS) {
+  if constexpr (EW == 2) {
+    constexpr int LOADS = ROUTER_LOADS / 2;
+    const int ea = e0 + 2 * warp, eb = ea + 1;
+    if (ea < E) {
+      const bool has_b = eb < E;
+      const __nv_bfloat16* wa = p.w + (size_t)ea * H;
+      const __nv_bfloat16* wb = p.w + (size_t)(has_b ? eb : ea) * H;
+      float acc[2][TB];
+#pragma unroll
+      for (int t = 0; t < TB; ++t) acc[0][t] = acc[1][t] = 0.0f;
+      for (int c0 = lane; c0 < chunks; c0 += LOADS * 32) {
+        uint4 va[LOADS], vb[LOADS];
+#pragma unroll
+        for (int u = 0; u < LOADS; ++u)
+          if (c0 + 32 * u < chunks) {
+            va[u] = ldg_nc(wa + (c0 + 32 * u) * 8);
+            vb[u] = ldg_nc(wb + (c0 + 32 * u) * 8);
+          }
+#pragma unroll
+        for (int u = 0; u < LOADS; ++u) {
+          const int c = c0 + 32 * u;
+          if (c >= chunks) break;
+          float fa[8], fb[8];
+          const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&va[u]);
+          const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&vb[u]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 x = __bfloat1622float2(a2[j]), y = __bfloat1622float2(b2[j]);
+            fa[2 * j] = x.x;
+            fa[2 * j + 1] = x.y;
+            fb[2 * j] = y.x;
+            fb[2 * j + 1] = y.y;
+          }
+#pragma unroll
+          for (int t = 0; t < TB; ++t) {
+            const float4 x0 = xf[(t * 2) * chunks + c], x1 = xf[(t * 2 + 1) * chunks + c];
+            const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              acc[0][t] = __fmaf_rn(xv[j], fa[j], acc[0][t]);
+              acc[1][t] = __fmaf_rn(xv[j], fb[j], acc[1][t]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+#pragma unroll
+        for (int t = 0; t < TB; ++t) {
+          float v = acc[r][t];
+#pragma unroll
+          for (int o = 16; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(FULL, v, o));
+          if (lane == 0 && t < nt && (r == 0 || has_b)) ws_logits[(size_t)(t0 + t) * E + (r ? eb : ea)] = v;
+        }
+      }
+    }
+  }
+
+  // EW = 1: each warp owns expert e0 + warp; chunk loads are issued ROUTER_LOADS at a time
+  for (int e = e0 + warp; EW == 1 && e < min(E, e0 + EB); e += ROUTER_WARPS) {
     float acc[TB];
 #pragma unroll
     for (int t = 0; t < TB; ++t) acc[t] = 0.0f;
@@ -229,8 +306,8 @@ __global__ void __launch_bounds__(ROUTER_THREADS) route_kernel(RouteParams p, fl
   if (threadIdx.x == 0) ws_count_end[-1 - (int)blockIdx.x] = 0u;  // ready for the next call on this stream
 }
 
-static size_t route_smem(int TB, int H, int E) {
-  const size_t stage = (size_t)TB * H * 2;
+static size_t route_smem(int TB, int EW, int H, int E) {
+  const size_t stage = (size_t)TB * H * (EW == 2 ? 4 : 2);
   const size_t select = (size_t)TB * E * 4 + (size_t)TB * (E > 64 ? E : 64) * 4 + (size_t)TB * ((E + 31) / 32) * 4;
   return stage > select ? stage : select;
 }
@@ -240,19 +317,28 @@ size_t route_workspace_bytes(int T, int E) {
   return logits + (size_t)(T > 0 ? T : 1) * 4;
 }
 
-template <int TB>
+template <int TB, int EW>
 static moe_status launch_route(const RouteParams& p, float* logits, unsigned* counts, cudaStream_t st) {
-  const size_t sm = route_smem(TB, p.H, p.E);
+  const size_t sm = route_smem(TB, EW, p.H, p.E);
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    MOE_CUDA_TRY(cudaFuncSetAttribute(route_kernel<TB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    MOE_CUDA_TRY(cudaFuncSetAttribute(route_kernel<TB, EW>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     attr_set[dev & 63] = true;
   }
-  dim3 grid(ceil_div(p.T, TB), ceil_div(p.E, ROUTER_EB));
-  MOE_CUDA_TRY(launch_pdl(route_kernel<TB>, grid, dim3(ROUTER_THREADS), sm, st, p, logits, counts));
+  dim3 grid(ceil_div(p.T, TB), ceil_div(p.E, ROUTER_EB * EW));
+  MOE_CUDA_TRY(launch_pdl(route_kernel<TB, EW>, grid, dim3(ROUTER_THREADS), sm, st, p, logits, counts));
   return MOE_OK;
+}
+
+// MOE_ROUTER_NARROW=1 keeps one expert per warp at every batch size (for comparison).
+static bool route_narrow() {
+  static const bool on = [] {
+    const char* v = std::getenv("MOE_ROUTER_NARROW");
+    return v && v[0] == '1';
+  }();
+  return on;
 }
 
 moe_status route_validate(const RouteParams& p) {
@@ -294,13 +380,16 @@ moe_status route_tokens(const RouteParams& p, void* ws, size_t ws_bytes, cudaStr
   if ((int64_t)p.T * eblocks >= 16LL * sms) TB = 8;
   else if ((int64_t)p.T * eblocks >= 8LL * sms) TB = 4;
   else if ((int64_t)p.T * eblocks >= 4LL * sms) TB = 2;
-  while (TB > 1 && route_smem(TB, p.H, p.E) > 200 * 1024) TB >>= 1;
-  if (route_smem(TB, p.H, p.E) > 200 * 1024) return fail(MOE_ERR_INVALID, "moe_route: hidden too large");
+  // large batches (4 or more tokens per CTA) take two experts per warp on f32-staged tokens
+  const bool wide = TB >= 4 && route_smem(TB, 2, p.H, p.E) <= 200 * 1024 && !route_narrow();
+  while (TB > 1 && route_smem(TB, 1, p.H, p.E) > 200 * 1024) TB >>= 1;
+  if (route_smem(TB, 1, p.H, p.E) > 200 * 1024) return fail(MOE_ERR_INVALID, "moe_route: hidden too large");
+  if (wide) return TB == 8 ? launch_route<8, 2>(p, logits, counts, st) : launch_route<4, 2>(p, logits, counts, st);
   switch (TB) {
-    case 8: return launch_route<8>(p, logits, counts, st);
-    case 4: return launch_route<4>(p, logits, counts, st);
-    case 2: return launch_route<2>(p, logits, counts, st);
-    default: return launch_route<1>(p, logits, counts, st);
+    case 8: return launch_route<8, 1>(p, logits, counts, st);
+    case 4: return launch_route<4, 1>(p, logits, counts, st);
+    case 2: return launch_route<2, 1>(p, logits, counts, st);
+    default: return launch_route<1, 1>(p, logits, counts, st);
   }
 }
 

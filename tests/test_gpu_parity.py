@@ -58,7 +58,10 @@ def build_layer(q, E, k, H, I, dtype, router=None, bias=None, mode=1, n_group=1,
 # ---- router ------------------------------------------------------------------------------------
 
 @pytest.mark.parametrize("T,H,E,k,mode", [(1, 2048, 128, 8, 1), (37, 2048, 128, 8, 1), (64, 1024, 16, 2, 0),
-                                          (300, 1024, 16, 2, 1), (5, 512, 64, 6, 0)])
+                                          (300, 1024, 16, 2, 1), (5, 512, 64, 6, 0),
+                                          # two experts per warp on f32-staged tokens (4 or 8 per CTA)
+                                          (256, 2048, 128, 8, 1), (129, 2048, 128, 8, 1), (300, 1024, 64, 6, 0),
+                                          (301, 512, 72, 4, 1)])
 def test_router_softmax_bit_exact(T, H, E, k, mode):
     rng = np.random.default_rng(T * 7 + E)
     x = O.f32_to_bf16(rng.normal(0, 1, (T, H)).astype(np.float32))
