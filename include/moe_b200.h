@@ -45,7 +45,10 @@ typedef enum {
   MOE_DTYPE_BF16 = 0,          /* 2 B / weight, row-major */
   MOE_DTYPE_Q8_0 = 1,          /* 34 B / 32 weights: f16 d, int8 qs[32] */
   MOE_DTYPE_Q4_K = 2,          /* 144 B / 256 weights: f16 d, f16 dmin, u8 scales[12], u8 qs[128] */
-  MOE_DTYPE_FP8_E4M3_B128 = 3  /* 1 B / weight e4m3 + one f32 scale per 128x128 block ([E, N/128, K/128]) */
+  MOE_DTYPE_FP8_E4M3_B128 = 3, /* 1 B / weight e4m3 + one f32 scale per 128x128 block ([E, N/128, K/128]) */
+  MOE_DTYPE_Q2_0 = 4           /* 18 B / 64 weights: f16 d, 2-bit codes (weight j at bits 2*(j%4) of byte
+                                * j/4), weight = (code - 1) * d: the reference's resident-pool format
+                                * (src/moe/resident.rs:29-45); hidden and inter multiples of 128 */
 } moe_wdtype;
 
 typedef enum {
@@ -468,6 +471,17 @@ size_t moe_gguf_get_str(const moe_gguf* file, const char* key, char* buf, size_t
  * converted to bf16 into memory the file object owns), NULL when the file has none. Other fields
  * (device, max_tokens, router mode, cache_slots, ...) are left as the caller set them. */
 moe_status moe_gguf_layer_desc(moe_gguf* file, int layer, moe_layer_desc* desc);
+
+/* ---- the resident Q2_0 pool --------------------------------------------------------------------
+ * The reference keeps a model's always-needed expert block resident by requantising its stacks to
+ * Q2_0 and running them through the ordinary expert kernels (resident.rs:92-182, quantize_q2_0
+ * :46-88). Requantises a stacked [E, N, K] projection held on the device in src_dtype (BF16, Q8_0 or
+ * Q4_K; K a multiple of 256 for Q4_K, of 64 otherwise) into Q2_0 bytes on the device
+ * (E * N * K / 64 * 18 of them): each 64-weight block's f16 scale is searched over
+ * amax / {1, 1.25, 1.5, 1.75, 2} for the smallest squared error, codes = clamp(round(x / d) + 1, 0, 3),
+ * an all-zero block decodes to zeros. The result is a moe_layer_desc stack with wdtype
+ * MOE_DTYPE_Q2_0 (the decode GEMV streams it: 0.28 B per weight). */
+moe_status moe_requantize_q2_0(int src_dtype, const void* src, int E, int N, int K, void* dst, void* stream);
 
 /* Library version string. */
 const char* moe_version(void);

@@ -286,6 +286,10 @@ moe_status launch_expert_gemv(int wdtype, ExpertParams p, int max_active, int ro
   }
   if (wdtype == MOE_DTYPE_Q8_0) return launch1<WQ8>(p, grid, smem, rowt, st);
   if (wdtype == MOE_DTYPE_BF16) return launch1<WBF16>(p, grid, smem, rowt, st);
+  if (wdtype == MOE_DTYPE_Q2_0) {
+    if (p.K % 128) return fail(MOE_ERR_INVALID, "decode expert kernel: Q2_0 needs K % 128 == 0");
+    return launch1<WQ2>(p, grid, smem, rowt, st);
+  }
   return fail(MOE_ERR_UNSUPPORTED, "decode expert kernel: weight format not built yet");
 }
 

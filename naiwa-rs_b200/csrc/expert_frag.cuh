@@ -90,6 +90,67 @@ struct WQ8Stream {
   }
 };
 
+// Q2_0 (repack.cu): per (tile, 128-column group) a lane's 16 B of codes (word w = the group's k16 steps
+// 2w, 2w + 1) and 8 B of scales {d(g), d(g+8)} for the group's two 64-column blocks. A pair of codes
+// becomes an exact f16x2 of (code - 1) by one shift, one mask-or (1024 + code) and one subtract of
+// 1025; a block's four k16 MMAs chain in f32 and its scale is applied once in f32 afterwards.
+struct WQ2 {
+  static constexpr bool kF16 = true;
+  static constexpr int GROUP = 4;  // 32-column blocks per stage: one 128-column group
+  struct Stage {
+    uint4 q;
+    uint2 s;
+  };
+  __device__ static __forceinline__ void load(const ExpertParams& p, int e, int tile, int kb0, int kb_end, int lane,
+                                              Stage& st) {
+    if (kb0 >= kb_end) return;
+    const int64_t grp = (int64_t)tile * (p.kb_count >> 2) + (kb0 >> 2);
+    st.q = ldg_stream(p.wq + (int64_t)e * p.q_stride + grp * 512 + lane * 16);
+    const uint2* sp = reinterpret_cast<const uint2*>(p.wsc + (int64_t)e * p.s_stride + grp * 64 + (lane >> 2) * 8);
+    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(st.s.x), "=r"(st.s.y) : "l"(sp));
+  }
+  template <int NTM>
+  __device__ static __forceinline__ void compute(const Stage& st, int kb0, int kb_end, const uint32_t* xs, int ntm,
+                                                 int nt_used, int lane, float (&acc)[NTM][4]) {
+    const uint32_t w[4] = {st.q.x, st.q.y, st.q.z, st.q.w};
+    const uint32_t sw[2] = {st.s.x, st.s.y};
+    const __half2 bias = __float2half2_rn(1025.0f);
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) {
+      const int kb = kb0 + 2 * blk;  // the block's first 32-column block of the staged tokens
+      if (kb >= kb_end) break;
+      uint32_t a[4][4];
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        const int sg = 4 * blk + s;  // k16 step within the group
+        const uint32_t word = w[sg >> 1];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t v = ((word >> (2 * ((sg & 1) * 4 + q))) & 0x00030003u) | 0x64006400u;  // 1024 + code
+          __half2 h = __hsub2(*reinterpret_cast<__half2*>(&v), bias);                     // code - 1
+          a[s][q] = *reinterpret_cast<uint32_t*>(&h);
+        }
+      }
+      const __half2 s2 = *reinterpret_cast<const __half2*>(&sw[blk]);
+      const float slo = __low2float(s2), shi = __high2float(s2);
+#pragma unroll
+      for (int t = 0; t < NTM; ++t) {
+        if (t < nt_used) {
+          const uint4 b0 = lds128(xs + ((kb * ntm + t) * 32 + lane) * 4);
+          const uint4 b1 = lds128(xs + (((kb + 1) * ntm + t) * 32 + lane) * 4);
+          float tmp[4];
+          mma_f16_zero(tmp, a[0], b0.x, b0.y);
+          mma_f16(tmp, a[1], b0.z, b0.w);
+          mma_f16(tmp, a[2], b1.x, b1.y);
+          mma_f16(tmp, a[3], b1.z, b1.w);
+          ffma2(acc[t][0], acc[t][1], slo, tmp[0], tmp[1]);
+          ffma2(acc[t][2], acc[t][3], shi, tmp[2], tmp[3]);
+        }
+      }
+    }
+  }
+};
+
 // BF16: per (tile, block) 1 KB = two k16 steps of 512 B; lane's 16 B = its 8 A values.
 using WQ8 = WQ8Stream<false>;
 using WQ8U = WQ8Stream<true>;

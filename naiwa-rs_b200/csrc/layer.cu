@@ -262,6 +262,7 @@ static int64_t ggml_bytes(int wdtype, int64_t n) {
     case MOE_DTYPE_Q8_0: return n / 32 * 34;
     case MOE_DTYPE_Q4_K: return n / 256 * 144;
     case MOE_DTYPE_FP8_E4M3_B128: return n;
+    case MOE_DTYPE_Q2_0: return n / 64 * 18;
   }
   return -1;
 }
@@ -298,8 +299,9 @@ static moe_status validate_desc(const moe_layer_desc* d) {
     return fail(MOE_ERR_INVALID, "FP8 128x128-block weights need hidden and inter multiples of 128");
   if (d->wdtype == MOE_DTYPE_FP8_E4M3_B128 && (!d->gate_scale || !d->up_scale || !d->down_scale))
     return fail(MOE_ERR_INVALID, "FP8 weights need gate_scale, up_scale and down_scale");
-  if (d->wdtype < MOE_DTYPE_BF16 || d->wdtype > MOE_DTYPE_FP8_E4M3_B128)
-    return fail(MOE_ERR_UNSUPPORTED, "unknown weight format");
+  if (d->wdtype == MOE_DTYPE_Q2_0 && (d->hidden % 128 || d->inter % 128))
+    return fail(MOE_ERR_INVALID, "Q2_0 weights need hidden and inter multiples of 128 (two blocks per group)");
+  if (d->wdtype < MOE_DTYPE_BF16 || d->wdtype > MOE_DTYPE_Q2_0) return fail(MOE_ERR_UNSUPPORTED, "unknown weight format");
   if (!d->gate || !d->up || !d->down) return fail(MOE_ERR_INVALID, "null expert stack");
   if (d->max_tokens <= 0) return fail(MOE_ERR_INVALID, "max_tokens must be positive");
   if (d->cache_slots < 0) return fail(MOE_ERR_INVALID, "cache_slots must be >= 0");

@@ -19,6 +19,15 @@
 // lane l = 4g + c's fragment stored in slot 4g + (c ^ ((g >> 1) & 3)) (the GEMM's dequant threads,
 // one per weight row, read all four slots of their g; the swizzle spreads the eight g of a warp
 // over all 32 banks).
+//
+// Q2_0 (the reference's resident-pool format: 64 weights per 18-byte block, f16 d, 2-bit codes,
+// weight = (code - 1) d): per expert, per 16-row tile and 128-column group (two blocks), 512
+// contiguous bytes of codes in which lane l = 4g + c's 16 bytes are four 32-bit words, word w
+// holding the k16 steps 2w and 2w + 1 of the group: for step s and fragment pair q (0: row g, columns
+// 2c..2c+1 of the step's first 8; 1: row g+8, same; 2: row g, columns 8+2c..; 3: row g+8, same), with
+// p = (s & 1) * 4 + q, the pair's first code at bits 2p and its second at bits 16 + 2p, so one shift
+// and one mask-or turn a pair into an f16x2 of 1024 + code. Scales apart: per tile and group, 8 x 8 B
+// (lane g's {d(g), d(g+8)} of the group's two blocks).
 #include "moe_internal.cuh"
 
 namespace moe {
@@ -186,14 +195,72 @@ moe_status repack_q8_units(const uint8_t* a, const uint8_t* b, int E, int N_src,
   return MOE_OK;
 }
 
+// one thread per (e, tile, 128-column group, lane): 16 bytes of codes
+__global__ void repack_q2_kernel(RepackSrc s, int E, int tiles, uint8_t* __restrict__ dq) {
+  const int GR = s.K / 128;
+  const int64_t total = (int64_t)E * tiles * GR * 32;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int lane = (int)(i & 31);
+  int64_t rest = i >> 5;
+  const int gr = (int)(rest % GR); rest /= GR;
+  const int tile = (int)(rest % tiles);
+  const int e = (int)(rest / tiles);
+  const int row_bytes = s.K / 64 * 18;
+  const int g = lane >> 2, c = lane & 3;
+  uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int step = 0; step < 8; ++step)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int r = g + 8 * (q & 1);
+      const int col = gr * 128 + step * 16 + 8 * (q >> 1) + 2 * c;  // the pair's first column
+      const uint8_t* row = src_row(s, e, tile, r, row_bytes);
+      const uint8_t* blk = row + (col / 64) * 18;
+      const int j0 = col % 64, j1 = j0 + 1;
+      const uint32_t c0 = (blk[2 + j0 / 4] >> (2 * (j0 % 4))) & 3u;
+      const uint32_t c1 = (blk[2 + j1 / 4] >> (2 * (j1 % 4))) & 3u;
+      const int pq = (step & 1) * 4 + q;
+      w[step >> 1] |= (c0 << (2 * pq)) | (c1 << (16 + 2 * pq));
+    }
+  reinterpret_cast<uint4*>(dq)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// one thread per (e, tile, group, g): 8 bytes of scales {d(g), d(g+8)} of the group's two blocks
+__global__ void repack_q2_scales_kernel(RepackSrc s, int E, int tiles, uint8_t* __restrict__ ds) {
+  const int GR = s.K / 128;
+  const int64_t total = (int64_t)E * tiles * GR * 8;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int g = (int)(i & 7);
+  int64_t rest = i >> 3;
+  const int gr = (int)(rest % GR); rest /= GR;
+  const int tile = (int)(rest % tiles);
+  const int e = (int)(rest / tiles);
+  const int row_bytes = s.K / 64 * 18;
+  uint16_t out[4];
+#pragma unroll
+  for (int b = 0; b < 2; ++b) {
+    const uint8_t* p0 = src_row(s, e, tile, g, row_bytes) + (gr * 2 + b) * 18;
+    const uint8_t* p1 = src_row(s, e, tile, g + 8, row_bytes) + (gr * 2 + b) * 18;
+    out[2 * b] = (uint16_t)(p0[0] | (p0[1] << 8));
+    out[2 * b + 1] = (uint16_t)(p1[0] | (p1[1] << 8));
+  }
+  uint2 v;
+  memcpy(&v, out, 8);
+  reinterpret_cast<uint2*>(ds)[i] = v;
+}
+
 // Device bytes of one expert's projection in the device layout.
 int64_t device_q_bytes(int wdtype, int N, int K) {
   if (wdtype == MOE_DTYPE_Q8_0) return (int64_t)N * K;
   if (wdtype == MOE_DTYPE_BF16) return (int64_t)N * K * 2;
+  if (wdtype == MOE_DTYPE_Q2_0) return (int64_t)N * K / 4;
   return 0;
 }
 int64_t device_s_bytes(int wdtype, int N, int K) {
   if (wdtype == MOE_DTYPE_Q8_0) return (int64_t)(N / 16) * ((K / 32 + 3) / 4) * 128;
+  if (wdtype == MOE_DTYPE_Q2_0) return (int64_t)(N / 16) * (K / 128) * 64;
   return 0;
 }
 
@@ -214,6 +281,15 @@ moe_status repack_projection(int wdtype, const uint8_t* a, const uint8_t* b, int
     repack_q8_kernel<<<blocks_for((int64_t)E * tiles * KB * 32, t), t, 0, st>>>(s, E, tiles, dq);
     MOE_CUDA_TRY(cudaGetLastError());
     repack_q8_scales_kernel<<<blocks_for((int64_t)E * tiles * ((KB + 3) / 4) * 8, t), t, 0, st>>>(s, E, tiles, ds);
+    MOE_CUDA_TRY(cudaGetLastError());
+    return MOE_OK;
+  }
+  if (wdtype == MOE_DTYPE_Q2_0) {
+    if (K % 128) return fail(MOE_ERR_INVALID, "repack: Q2_0 needs K % 128 == 0");
+    s.expert_bytes = (int64_t)N_src * (K / 64) * 18;
+    repack_q2_kernel<<<blocks_for((int64_t)E * tiles * (K / 128) * 32, t), t, 0, st>>>(s, E, tiles, dq);
+    MOE_CUDA_TRY(cudaGetLastError());
+    repack_q2_scales_kernel<<<blocks_for((int64_t)E * tiles * (K / 128) * 8, t), t, 0, st>>>(s, E, tiles, ds);
     MOE_CUDA_TRY(cudaGetLastError());
     return MOE_OK;
   }

@@ -6,11 +6,12 @@ src/moe/expert.rs:59-117); `route` is the router + top-k upstream of them. All c
 libmoe_b200.so; torch tensors are only the containers for device memory and streams.
 """
 from ._lib import (  # noqa: F401
-    DTYPE_BF16, DTYPE_FP8_E4M3_B128, DTYPE_Q4_K, DTYPE_Q8_0, MOE_ID_NONE, MoeError, ROUTER_SIGMOID_GROUP,
+    DTYPE_BF16, DTYPE_FP8_E4M3_B128, DTYPE_Q2_0, DTYPE_Q4_K, DTYPE_Q8_0, MOE_ID_NONE, MoeError, ROUTER_SIGMOID_GROUP,
     ROUTER_SOFTMAX, ROUTER_SOFTMAX_RENORM, lib,
 )
 from .layer import (  # noqa: F401
-    ExpertLoadContext, MoeConfig, RoutedExperts, RoutedExpertsProvider, Router, plan_pairs, route_tokens,
+    ExpertLoadContext, MoeConfig, RoutedExperts, RoutedExpertsProvider, Router, plan_pairs, requantize_q2_0,
+    route_tokens,
 )
 from .ep import ExpertParallelMoE, PeerExpertParallelMoE, ep_combine, ep_dispatch, ep_pack_rows  # noqa: F401,E402
 from .doorbell import Ring  # noqa: F401,E402

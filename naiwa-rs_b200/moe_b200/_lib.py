@@ -24,7 +24,7 @@ STATUS_NAMES = {
     5: "MOE_ERR_BAD_IDS", 6: "MOE_ERR_UNSUPPORTED", 7: "MOE_ERR_WORKER",
 }
 
-DTYPE_BF16, DTYPE_Q8_0, DTYPE_Q4_K, DTYPE_FP8_E4M3_B128 = 0, 1, 2, 3
+DTYPE_BF16, DTYPE_Q8_0, DTYPE_Q4_K, DTYPE_FP8_E4M3_B128, DTYPE_Q2_0 = 0, 1, 2, 3, 4
 ROUTER_SOFTMAX, ROUTER_SOFTMAX_RENORM, ROUTER_SIGMOID_GROUP = 0, 1, 2
 
 
@@ -80,6 +80,7 @@ def lib():
             "moe_layer_create": (i, [ctypes.POINTER(LayerDesc), ctypes.POINTER(ctypes.c_void_p)]),
             "moe_layer_warmup": (i, [P, i]),
             "moe_route": (i, [P, P, i, P, P, P]),
+            "moe_requantize_q2_0": (i, [i, P, i, i, i, P, P]),
             "moe_forward": (i, [P, P, i, P, P, i, P, P]),
             "moe_forward_marked": (i, [P, P, i, P, P, i, P, P, ctypes.POINTER(ctypes.c_void_p)]),
             "moe_layer_destroy": (None, [P]),

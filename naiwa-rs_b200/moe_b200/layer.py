@@ -269,8 +269,35 @@ class RoutedExpertsProvider:
         for layer in self.layers.values():
             layer.warmup(max_tokens)
 
+    def build_resident(self, ctx: ExpertLoadContext) -> RoutedExperts:
+        """The reference's resident pool (resident.rs:92-182): the block's expert stacks requantised to
+        Q2_0 on the layer's device (moe_requantize_q2_0) and kept resident, run by the same expert
+        kernels. ctx holds BF16, Q8_0 or Q4_K stacks (host or CUDA); hidden and inter must be
+        multiples of 128."""
+        import dataclasses
+
+        c = ctx.config
+        E, H, I = c.num_experts, c.hidden_size, c.moe_intermediate_size
+        stacks = [requantize_q2_0(s, ctx.wdtype, E, n, k, device=ctx.device)
+                  for s, (n, k) in zip((ctx.gate, ctx.up, ctx.down), ((I, H), (I, H), (H, I)))]
+        rctx = dataclasses.replace(ctx, wdtype=_lib.DTYPE_Q2_0, gate=stacks[0], up=stacks[1], down=stacks[2],
+                                   gate_scale=None, up_scale=None, down_scale=None, _keep=[])
+        return self.build(rctx)
+
 
 # ---- stateless kernels ---------------------------------------------------------------------------
+
+def requantize_q2_0(stack, src_dtype: int, E: int, N: int, K: int, device: int = 0, stream=None):
+    """A stacked [E, N, K] projection (GGML bytes of src_dtype: BF16, Q8_0 or Q4_K; numpy uint8 or a
+    CUDA uint8 tensor) requantised to Q2_0 on the device: a CUDA uint8 tensor of E*N*K/64*18 bytes
+    (moe_requantize_q2_0, the reference's quantize_q2_0 scale-ladder search)."""
+    torch = _torch()
+    dev = torch.device("cuda", device)
+    src = torch.from_numpy(np.ascontiguousarray(stack).reshape(-1)).to(dev) if isinstance(stack, np.ndarray) \
+        else stack.reshape(-1).contiguous()
+    out = torch.empty(E * N * K // 64 * 18, dtype=torch.uint8, device=dev)
+    check(lib().moe_requantize_q2_0(int(src_dtype), _ptr(src), E, N, K, _ptr(out), ctypes.c_void_p(_stream(stream))))
+    return out
 
 def route_tokens(x, w_router, k: int, mode: int, bias=None, n_group: int = 1, topk_group: int = 1,
                  routed_scale: float = 1.0, stream=None):

@@ -136,6 +136,63 @@ void orc_q8_0_dequantize(const uint8_t* blocks, int64_t n, float* out) {
   }
 }
 
+/* Q2_0, the reference's resident-pool format (src/moe/resident.rs:29-45): 64 weights per 18-byte
+ * block, an f16 scale d then 16 bytes of 2-bit codes (weight j at bits 2*(j%4) of byte j/4), weight
+ * value (code - 1) * d, so codes 0..3 stand for -1, 0, +1, +2. The quantiser restates
+ * resident.rs:46-88: d is searched over amax / {1, 1.25, 1.5, 1.75, 2}, each rounded to f16; a
+ * weight's code is clamp(round(x / d) + 1, 0, 3) with round-half-away; the candidate with the
+ * smallest squared error is kept, the first on ties; an all-zero block is d = 0 with every code 1
+ * (so it decodes to zeros), and a block whose candidates all round to d = 0 keeps codes 0 and d = 0. */
+void orc_q2_0_quantize(const float* x, int64_t n, uint8_t* out) {
+  static const float ladder[5] = {1.0f, 1.25f, 1.5f, 1.75f, 2.0f};
+  for (int64_t b = 0; b < n / 64; ++b) {
+    const float* xb = x + b * 64;
+    uint8_t* o = out + b * 18;
+    float amax = 0.0f;
+    for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(xb[i]));
+    memset(o + 2, 0, 16);
+    if (amax == 0.0f) {
+      o[0] = o[1] = 0;
+      memset(o + 2, 0x55, 16);
+      continue;
+    }
+    float best_err = INFINITY, best_scale = 0.0f;
+    uint8_t best[64], codes[64];
+    memset(best, 0, sizeof(best));
+    for (int f = 0; f < 5; ++f) {
+      const float scale = orc_f16_to_f32(orc_f32_to_f16(amax / ladder[f]));
+      if (scale == 0.0f) continue;
+      const float inv = 1.0f / scale;
+      float err = 0.0f;
+      for (int j = 0; j < 64; ++j) {
+        int c = (int)roundf(xb[j] * inv) + 1;
+        c = c < 0 ? 0 : c > 3 ? 3 : c;
+        codes[j] = (uint8_t)c;
+        const float res = xb[j] - ((float)c - 1.0f) * scale;
+        err += res * res;
+      }
+      if (err < best_err) {
+        best_err = err;
+        best_scale = scale;
+        memcpy(best, codes, 64);
+      }
+    }
+    const uint16_t dh = orc_f32_to_f16(best_scale);
+    memcpy(o, &dh, 2);
+    for (int j = 0; j < 64; ++j) o[2 + j / 4] |= (uint8_t)(best[j] << (2 * (j % 4)));
+  }
+}
+
+void orc_q2_0_dequantize(const uint8_t* blocks, int64_t n, float* out) {
+  for (int64_t b = 0; b < n / 64; ++b) {
+    const uint8_t* o = blocks + b * 18;
+    uint16_t dh;
+    memcpy(&dh, o, 2);
+    const float d = orc_f16_to_f32(dh);
+    for (int j = 0; j < 64; ++j) out[b * 64 + j] = ((float)((o[2 + j / 4] >> (2 * (j % 4))) & 3) - 1.0f) * d;
+  }
+}
+
 /* GGML Q4_K (public ggml block_q4_K): 8 sub-blocks of 32 with 6-bit scale/min pairs packed in
  * 12 bytes, w = d*sc*q - dmin*m. The packing and unpacking below are the published
  * get_scale_min_k4 rule; the quantizer is this oracle's own (a min/max fit per sub-block),
@@ -253,6 +310,7 @@ int64_t orc_block_bytes(int dtype, int64_t n_weights) {
     case 1: return n_weights / 32 * 34;
     case 2: return n_weights / 256 * 144;
     case 3: return n_weights;
+    case 4: return n_weights / 64 * 18;
     default: return -1;
   }
 }
@@ -260,7 +318,7 @@ int64_t orc_block_bytes(int dtype, int64_t n_weights) {
 /* src/moe/expert.rs:123-145: row-block formats never cross an expert, so expert e of a stacked
  * [E, N, K] tensor is bytes [e*stride, (e+1)*stride) with stride = N * (K/block) * type_size. */
 int orc_expert_range(int dtype, int E, int N, int K, int e, int64_t* begin, int64_t* end) {
-  int block = dtype == 1 ? 32 : dtype == 2 ? 256 : 1;
+  int block = dtype == 1 ? 32 : dtype == 2 ? 256 : dtype == 4 ? 64 : 1;
   if (K % block != 0 || e < 0 || e >= E) return -1;
   int64_t stride = orc_block_bytes(dtype, (int64_t)N * K);
   *begin = (int64_t)e * stride;
@@ -632,6 +690,8 @@ static void dequant_rows(int dtype, const uint8_t* q, const float* scales, int N
       }
     } else if (dtype == 1) {
       orc_q8_0_dequantize(src, K, dst);
+    } else if (dtype == 4) {
+      orc_q2_0_dequantize(src, K, dst);
     } else {
       orc_q4_k_dequantize(src, K, dst);
     }
@@ -719,9 +779,9 @@ static void* ref_worker(void* arg) {
 int orc_moe_forward_ref(int dtype, const uint8_t* gate, const uint8_t* up, const uint8_t* down, const float* gs,
                         const float* us, const float* ds, const float* x, const uint32_t* ids, const float* w, int T,
                         int k, int E, int H, int I, int n_threads, float* y) {
-  if (dtype < 0 || dtype > 3 || T < 0 || k <= 0 || E <= 0 || H <= 0 || I <= 0) return -1;
+  if (dtype < 0 || dtype > 4 || T < 0 || k <= 0 || E <= 0 || H <= 0 || I <= 0) return -1;
   if ((dtype == 3 && (H % 128 || I % 128 || !gs || !us || !ds)) || (dtype == 1 && (H % 32 || I % 32)) ||
-      (dtype == 2 && (H % 256 || I % 256)))
+      (dtype == 2 && (H % 256 || I % 256)) || (dtype == 4 && (H % 64 || I % 64)))
     return -1;
   if (n_threads < 1) n_threads = 1;
   const int n = T * k;

@@ -37,6 +37,8 @@ float orc_silu(float x);
 void orc_q8_0_quantize(const float* x, int64_t n, uint8_t* out);
 void orc_q8_0_dequantize(const uint8_t* blocks, int64_t n, float* out);
 /* Q4_K: 144-byte super-blocks of 256 {f16 d; f16 dmin; u8 scales[12]; u8 qs[128]}. */
+void orc_q2_0_quantize(const float* x, int64_t n, uint8_t* out);
+void orc_q2_0_dequantize(const uint8_t* blocks, int64_t n, float* out);
 void orc_q4_k_quantize(const float* x, int64_t n, uint8_t* out);
 void orc_q4_k_dequantize(const uint8_t* blocks, int64_t n, float* out);
 /* FP8 e4m3 with one f32 scale per 128x128 block of an [N, K] matrix (N, K multiples of 128). */

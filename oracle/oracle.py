@@ -19,7 +19,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "liboracle.so")
 _lib = None
 
-DT_BF16, DT_Q8_0, DT_Q4_K, DT_FP8 = 0, 1, 2, 3
+DT_BF16, DT_Q8_0, DT_Q4_K, DT_FP8, DT_Q2_0 = 0, 1, 2, 3, 4
 
 
 def build() -> str:
@@ -51,6 +51,8 @@ def lib():
             "orc_q8_0_quantize": (None, [P, i64, P]),
             "orc_q8_0_dequantize": (None, [P, i64, P]),
             "orc_q4_k_quantize": (None, [P, i64, P]),
+            "orc_q2_0_quantize": (None, [P, i64, P]),
+            "orc_q2_0_dequantize": (None, [P, i64, P]),
             "orc_q4_k_dequantize": (None, [P, i64, P]),
             "orc_fp8_b128_quantize": (None, [P, i, i, P, P]),
             "orc_fp8_b128_dequantize": (None, [P, P, i, i, P]),
@@ -122,6 +124,10 @@ def quantize(dtype: int, w: np.ndarray):
         out = np.empty(w.size // 256 * 144, dtype=np.uint8)
         lib().orc_q4_k_quantize(_p(w), w.size, _p(out))
         return out, None
+    if dtype == DT_Q2_0:
+        out = np.empty(w.size // 64 * 18, dtype=np.uint8)
+        lib().orc_q2_0_quantize(_p(w), w.size, _p(out))
+        return out, None
     if dtype == DT_FP8:
         n, k = w.shape[-2], w.shape[-1]
         lead = int(np.prod(w.shape[:-2])) if w.ndim > 2 else 1
@@ -149,6 +155,8 @@ def dequantize(dtype: int, blob: np.ndarray, shape, scales=None) -> np.ndarray:
         lib().orc_q8_0_dequantize(_p(blob), n, _p(out))
     elif dtype == DT_Q4_K:
         lib().orc_q4_k_dequantize(_p(blob), n, _p(out))
+    elif dtype == DT_Q2_0:
+        lib().orc_q2_0_dequantize(_p(blob), n, _p(out))
     elif dtype == DT_FP8:
         nn, kk = shape[-2], shape[-1]
         lead = n // (nn * kk)

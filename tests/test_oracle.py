@@ -118,6 +118,39 @@ def test_q4_k_round_trip_error_is_bounded():
         assert np.all(err <= 1.5 * step + 1e-6)
 
 
+def test_q2_0_pack_round_trips_through_the_decoder():  # resident.rs:190-218
+    """The reference's own known answers for its Q2_0 packer: a sin-pattern row decodes within half a
+    step of its block maximum (err <= 0.55 amax), and a zero block decodes to zeros, not to -d."""
+    x = (np.sin(np.arange(4096, dtype=np.float32) * np.float32(0.017)) * np.float32(1.5) - np.float32(0.25)).astype(np.float32)
+    q, _ = O.quantize(O.DT_Q2_0, x)
+    assert q.size == 4096 // 64 * 18 == O.block_bytes(O.DT_Q2_0, 4096)
+    back = O.dequantize(O.DT_Q2_0, q, x.shape)
+    assert np.abs(x - back).max() <= np.abs(x).max() * 0.55
+    z, _ = O.quantize(O.DT_Q2_0, np.zeros(128, np.float32))
+    assert np.all(O.dequantize(O.DT_Q2_0, z, (128,)) == 0.0)
+    # layout: f16 d then 16 code bytes, weight j at bits 2*(j%4) of byte j/4, value (code - 1) * d
+    blk = q[:18]
+    d = np.frombuffer(blk[:2].tobytes(), dtype=np.float16)[0].astype(np.float32)
+    codes = np.array([(blk[2 + j // 4] >> (2 * (j % 4))) & 3 for j in range(64)], dtype=np.float32)
+    assert np.array_equal(back[:64], (codes - 1.0) * d)
+
+
+def test_q2_0_scale_ladder_beats_the_block_maximum():
+    """The quantiser keeps the ladder candidate with the least squared error, so it is never worse
+    than the plain block-maximum scale (ladder fraction 1)."""
+    rng = np.random.default_rng(5)
+    x = rng.normal(0, 0.02, 64 * 200).astype(np.float32)
+    q, _ = O.quantize(O.DT_Q2_0, x)
+    back = O.dequantize(O.DT_Q2_0, q, x.shape)
+    err = ((x - back).reshape(-1, 64) ** 2).sum(1)
+    for b, blk in enumerate(x.reshape(-1, 64)):
+        amax = np.abs(blk).max()
+        d = np.float32(np.float16(amax))
+        codes = np.clip(np.sign(blk / d) * np.floor(np.abs(blk / d) + 0.5) + 1, 0, 3)
+        naive = ((blk - (codes - 1) * d) ** 2).sum()
+        assert err[b] <= naive * (1 + 1e-6)
+
+
 def test_fp8_e4m3_codes():
     L = O.lib()
     # every finite code round-trips
