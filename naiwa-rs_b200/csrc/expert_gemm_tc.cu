@@ -191,6 +191,7 @@ struct GemmParams {
   float* out;             // phase 0: h [pairs, N_rows/2]; phase 1: ypair [pairs, N_rows]
   int32_t* err;
   const int32_t* slot_of;  // [E] cache slot of each expert, or null: weights indexed by expert id
+  int32_t* work;           // work-item counter of this launch (zero at launch)
 };
 
 // Weight formats. Weights stream through a shared-memory ring in "units" (one contiguous 1-D bulk
@@ -365,12 +366,14 @@ __host__ __device__ constexpr int gemm_smem_bytes() {
 
 // ---- the GEMM ------------------------------------------------------------------------------------
 //
-// Persistent: one CTA per SM walks the work items w = blockIdx.x, blockIdx.x + gridDim.x, ... of
-// the launch, item w = (token tile w / tiles, weight tile w % tiles), so CTAs running side by side
-// share a token tile in L2 and stream different weight tiles. Every item costs about the same
-// (a 128 x N x 16 MMA takes the same issue slot for any N <= 64, and the dequant work does not
-// depend on N), so the static schedule balances. Warp roles, all hand-offs through mbarriers and
-// all rings continuing across item boundaries:
+// Persistent: one or two CTAs per SM take the launch's work items from a global counter (one
+// atomicAdd per item by the weight-streaming thread, which runs ahead of every other role and hands
+// each index to them through a small shared-memory ring), item w = (token tile w / tiles, weight
+// tile w % tiles), so CTAs running side by side share a token tile in L2 and stream different weight
+// tiles. Taking items as they free up absorbs what a static split cannot: the SMs' different rates
+// (measured: the CTAs of a static round-robin launch finished up to 15-25% apart) and items of
+// different token counts. Warp roles, all hand-offs through mbarriers and all rings continuing
+// across item boundaries:
 //   * warps 0..15 dequantise chunk q (a global chunk counter) from the weight ring into tensor-memory
 //     stage q % ASTAGES once the MMAs of chunk q - ASTAGES released it (stage_free), and arrive a_full;
 //     after the last chunk of a weight unit they arrive raw_free for its ring slot;
@@ -388,6 +391,32 @@ __host__ __device__ constexpr int gemm_smem_bytes() {
 struct Item {
   int e, es, base, n0, nval, nmma, tile;  // es: the expert's weight slot
 };
+
+// Work-item ring: the weight-streaming thread publishes the index of the CTA's j-th item (or -1 once
+// the launch's counter has run past the last item) in slot j % ITEM_RING and arrives item_full;
+// every consuming role (token loader, MMA issuer, each dequant and epilogue warp) reads it and
+// arrives item_free, after which the slot can take item j + ITEM_RING.
+constexpr int ITEM_RING = 8;
+
+template <class C>
+__host__ __device__ constexpr int item_consumers() {
+  return 2 + C::DQW + EPI_WARPS;
+}
+
+// The j-th item index for a consuming role: w >= 0, -1 when the launch has no more items, -2 when
+// the wait gave up (timeout or abort). Warp-collective when `warp_wide` (every lane gets the same
+// value; lane 0 releases the slot), else called by one thread.
+__device__ __forceinline__ int take_item(uint64_t* item_full, uint64_t* item_free, const volatile int* s_item, int j,
+                                         volatile int* abort, bool warp_wide) {
+  const int slot = j % ITEM_RING;
+  bool ok = mbar_wait(&item_full[slot], (j / ITEM_RING) & 1, abort);
+  if (warp_wide) ok = __all_sync(FULL, ok);
+  if (!ok) return -2;
+  const int w = s_item[slot];
+  if (warp_wide) __syncwarp();
+  if (!warp_wide || (threadIdx.x & 31) == 0) mbar_arrive(&item_free[slot]);
+  return w;
+}
 
 template <int BN>
 __device__ __forceinline__ Item decode_item(const GemmParams& p, int w) {
@@ -435,6 +464,10 @@ __device__ __forceinline__ void epilogue_blocks(const GemmParams& p, const Item&
     if (cb < cb0 || cb >= cb1 || c0 >= it.nmma) continue;
     float v[16];
     tmem_ld16(tbase + (uint32_t)c0, v);
+    // All shuffles and arithmetic of the block first, with no branch between the 16 tokens, then the
+    // predicated stores: a branch per token (the gate lanes' SiLU, or the valid-column test) makes
+    // the scheduler run each token's shuffle -> exp -> reciprocal -> store chain to completion before
+    // the next one starts (measured ~3,500 SM cycles per 16-token gate/up block, ~50 per down store).
     if (p.phase == 0) {
       const int col = it.tile * 64 + quad * 16 + (lane >> 4) * 8 + (lane & 7);
 #pragma unroll
@@ -442,19 +475,26 @@ __device__ __forceinline__ void epilogue_blocks(const GemmParams& p, const Item&
         const int n = c0 + i;
         const float sc = __shfl_sync(FULL, csc[n >> 5], n & 31);
         const float up = __shfl_down_sync(FULL, v[i], 8);
-        if (!(lane & 8) && n < it.nval) {
-          const float g = v[i] * sc, uu = up * sc;
-          p.out[(int64_t)(it.base + it.n0 + n) * (p.N_rows >> 1) + col] = __fdividef(g, 1.0f + __expf(-g)) * uu;
-        }
+        const float g = v[i] * sc, uu = up * sc;  // meaningful on the gate lanes only
+        v[i] = __fdividef(g, 1.0f + __expf(-g)) * uu;
       }
+      float* dst = p.out + (int64_t)(it.base + it.n0 + c0) * (p.N_rows >> 1) + col;
+      const bool gate_lane = !(lane & 8);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (gate_lane && c0 + i < it.nval) dst[(int64_t)i * (p.N_rows >> 1)] = v[i];
     } else {
+      int pr[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int n = c0 + i;
-        const float sc = __shfl_sync(FULL, csc[n >> 5], n & 31);
-        const int pr = __shfl_sync(FULL, cpr[n >> 5], n & 31);
-        if (n < it.nval) p.out[(int64_t)pr * p.N_rows + it.tile * BM + quad * 32 + lane] = v[i] * sc;
+        v[i] *= __shfl_sync(FULL, csc[n >> 5], n & 31);
+        pr[i] = __shfl_sync(FULL, cpr[n >> 5], n & 31);
       }
+      float* dst = p.out + it.tile * BM + quad * 32 + lane;
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (c0 + i < it.nval) dst[(int64_t)pr[i] * p.N_rows] = v[i];
     }
   }
 }
@@ -499,9 +539,12 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
   uint64_t* acc_full = stage_free + C::STG;
   uint64_t* acc_free = acc_full + C::NACC;
   uint64_t* mma_done = acc_free + C::NACC;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* item_full = mma_done + 1;
+  uint64_t* item_free = item_full + ITEM_RING;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_free + ITEM_RING);
   __shared__ volatile int s_abort;
   __shared__ int s_units_issued, s_tiles_issued;
+  __shared__ volatile int s_item[ITEM_RING];
 
   pdl_wait();  // the tile list, the gathered tokens and the error word come from earlier kernels
   pdl_trigger();
@@ -512,7 +555,6 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kchunks = p.K / BK;
   const int units = kchunks / W::CHUNKS_PER_UNIT;
-  const int G = gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < R; ++s) {
@@ -531,6 +573,10 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
       mbar_init(&acc_free[s], EPI_WARPS + (dequant_joins_epilogue<C>(p) ? C::DQW : 0));
     }
     mbar_init(mma_done, 1);
+    for (int s = 0; s < ITEM_RING; ++s) {
+      mbar_init(&item_full[s], 1);
+      mbar_init(&item_free[s], item_consumers<C>());
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     s_abort = 0;
     s_units_issued = 0;
@@ -551,7 +597,17 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
     // ---------------- weight units -> ring ----------------
     if (lane == 0) {
       int g = 0;
-      for (int w = blockIdx.x; w < n_items && !*abort; w += G) {
+      for (int j = 0; !*abort; ++j) {
+        const int islot = j % ITEM_RING;
+        if (j >= ITEM_RING && !mbar_wait(&item_free[islot], ((j / ITEM_RING) - 1) & 1, abort)) {
+          s_abort = 1;
+          break;
+        }
+        int w = atomicAdd(p.work, 1);
+        if (w >= n_items) w = -1;
+        s_item[islot] = w;
+        mbar_arrive(&item_full[islot]);  // release: the index is visible to the roles that wait on it
+        if (w < 0) break;
         const Item it = decode_item<C::BN>(p, w);
         for (int u = 0; u < units; ++u, ++g) {
           const int slot = g % R;
@@ -570,7 +626,12 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
     // ---------------- token tiles -> B stages ----------------
     if (lane == 0) {
       int q = 0;
-      for (int w = blockIdx.x; w < n_items && !*abort; w += G) {
+      for (int j = 0; !*abort; ++j) {
+        const int w = take_item(item_full, item_free, s_item, j, abort, false);
+        if (w < 0) {
+          if (w == -2) s_abort = 1;
+          break;
+        }
         const Item it = decode_item<C::BN>(p, w);
         const int boxes = (it.nmma + TMA_ROWS - 1) / TMA_ROWS;  // only the tile's own token rows
         for (int kc = 0; kc < kchunks; ++kc, ++q) {
@@ -593,8 +654,13 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
     // ---------------- MMA issue ----------------
     if (lane == 0) {
       const uint64_t bdesc0 = smem_desc(smem_u32(sB));
-      int q = 0, j = 0;
-      for (int w = blockIdx.x; w < n_items && !*abort; w += G, ++j) {
+      int q = 0;
+      for (int j = 0; !*abort; ++j) {
+        const int w = take_item(item_full, item_free, s_item, j, abort, false);
+        if (w < 0) {
+          if (w == -2) s_abort = 1;
+          break;
+        }
         const Item it = decode_item<C::BN>(p, w);
         const int acc = j % C::NACC;
         if (j >= C::NACC && !mbar_wait(&acc_free[acc], ((j / C::NACC) - 1) & 1, abort)) {
@@ -630,8 +696,12 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
   } else if (warp >= C::EPI_WARP0) {
     // ---------------- epilogue ----------------
     const int quad = warp & 3;  // tensor-memory lanes 32 quad .. +31
-    int j = 0;
-    for (int w = blockIdx.x; w < n_items; w += G, ++j) {
+    for (int j = 0;; ++j) {
+      const int w = take_item(item_full, item_free, s_item, j, abort, true);
+      if (w < 0) {
+        if (w == -2 && lane == 0) s_abort = 1;
+        break;
+      }
       const Item it = decode_item<C::BN>(p, w);
       const int acc = j % C::NACC;
       const bool ok = __all_sync(FULL, mbar_wait(&acc_full[acc], (j / C::NACC) & 1, abort));
@@ -657,7 +727,12 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
     const uint32_t lane_base = tmem + ((uint32_t)(drow & ~31) << 16) + (uint32_t)C::A_COL0;
     int q = 0, g = 0, j_item = 0;
     bool stop = false;
-    for (int w = blockIdx.x; w < n_items && !stop; w += G) {
+    while (!stop) {
+      const int w = take_item(item_full, item_free, s_item, j_item, abort, true);
+      if (w < 0) {
+        stop = w == -2;
+        break;
+      }
       const Item it = decode_item<C::BN>(p, w);
       for (int kc = 0; kc < kchunks; ++kc, ++q) {
         if (C::DQG > 1 && q % C::DQG != grp) continue;
@@ -773,7 +848,11 @@ __global__ void __launch_bounds__(TL_THREADS) tile_list_kernel(const int32_t* __
     if (threadIdx.x == TL_THREADS - 1) s_base = start + nt;
     __syncthreads();
   }
-  if (threadIdx.x == 0) *n_list = s_base;
+  if (threadIdx.x == 0) {
+    n_list[0] = s_base;
+    n_list[1] = 0;  // work-item counters of the gate/up and down launches that follow
+    n_list[2] = 0;
+  }
 }
 
 // Sorted, f16 copy of the tokens (one warp per sorted pair): each row scaled by a power of two so
@@ -1056,6 +1135,8 @@ static moe_status launch_tc(const TcArgs& a, cudaStream_t st) {
   p.out = a.out;
   p.err = a.err;
   p.slot_of = a.slot_of;
+  p.work = a.work;
+  if (!p.work) return fail(MOE_ERR_INVALID, "tensor-core path: no work-item counter");
   static int sms[64] = {};
   if (!sms[dev & 63]) MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev));
   // persistent: CTAS_PER_SM CTAs per SM (or one per work item when there are fewer); the token

@@ -125,7 +125,8 @@ static moe_status alloc_scratch(moe_layer* L, int max_tokens) {
     MOE_TRY(dalloc(&L->h16, (size_t)cap * I * 2, &acc));
     MOE_TRY(dalloc(&L->hscale, sizeof(float) * cap, &acc));
     MOE_TRY(dalloc(&L->tile_list, sizeof(int32_t) * ((size_t)cap / TC_BN_MIN + E + 1), &acc));
-    MOE_TRY(dalloc(&L->n_tiles, sizeof(int32_t), &acc));
+    // [0] the tile-list length, [1] / [2] the work-item counters of the gate/up and down GEMM launches
+    MOE_TRY(dalloc(&L->n_tiles, 4 * sizeof(int32_t), &acc));
     MOE_TRY(make_row_tmap(L->tmap_x, L->x16, cap, H));
     MOE_TRY(make_row_tmap(L->tmap_h, L->h16, cap, I));
   }
@@ -560,6 +561,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
     ga.phase = 0;
     ga.tile_list = L->tile_list;
     ga.n_tiles = L->n_tiles;
+    ga.work = L->n_tiles + 1;
     ga.offsets = L->offsets;
     ga.active = L->active;
     ga.perm = L->perm;
@@ -585,6 +587,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
     da.tscale = L->hscale;
     da.out = L->ypair;
     da.tmap = L->tmap_h;
+    da.work = L->n_tiles + 2;
     MOE_TRY(tc_gemm(w, da, st));
     MOE_TRY(mark(events, 3, st));
     if (combine) MOE_TRY(launch_combine(L->ypair, ids, T, width, H, E, y, st, slot_of));

@@ -106,6 +106,7 @@ struct TcArgs {
   int n_pairs, max_active;            // grid bound: token tiles <= n_pairs / bn + max_active
   int bn = 128;                       // tokens per work item: 32 / 64 (decode shapes) or 128 (prefill)
   const int32_t* slot_of = nullptr;  // [E] cache slot of each expert, or null
+  int32_t* work = nullptr;            // the launch's work-item counter: zero when the launch starts
 };
 constexpr int TC_BN_MIN = 32;  // smallest token tile (sizes the tile list)
 // Token tile for a forward of n_pairs pairs over E experts: 32 or 64 for decode batches (mean tokens
@@ -121,6 +122,8 @@ moe_status tc_repack(int wdtype, const uint8_t* a, const uint8_t* b, const float
 // pdl: programmatic launch (the decode shapes' pipeline)
 moe_status tc_gather(const void* x_bf16, const float* x_f32, int K, int width, const int32_t* perm, int n_pairs,
                      const int32_t* n_valid, void* out_f16, float* scale, cudaStream_t st, bool pdl);
+// n_list[0]: the list length; n_list[1] and n_list[2] (the work-item counters of the two GEMM launches
+// that follow, gate/up and down) are zeroed.
 moe_status tc_tile_list(const int32_t* counts, const int32_t* active, const int32_t* n_active, int bn, int32_t* list,
                         int32_t* n_list, cudaStream_t st);
 moe_status tc_gemm(int wdtype, const TcArgs& a, cudaStream_t st);
