@@ -46,11 +46,22 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(Exp
     pdl_wait();
     pdl_trigger();
   }
-  if (a_idx >= __ldcg(p.n_active)) return;
-  const int e = __ldcg(p.active + a_idx);
-  const int es = p.slot_of ? __ldcg(p.slot_of + e) : e;  // weights: the expert's cache slot
-  const int base = __ldcg(p.offsets + e);
-  const int count = __ldcg(p.offsets + e + 1) - base;
+  int e, es, base, count;  // es: the expert's weight slot
+  if (p.act_rec) {  // one 16-byte load of the plan's record for this active index
+    const int4 r = __ldcg(p.act_rec + a_idx);
+    if (r.x < 0) return;
+    e = r.x;
+    es = r.y;
+    base = r.z;
+    count = r.w;
+  } else {
+    if (a_idx >= __ldcg(p.n_active)) return;
+    e = __ldcg(p.active + a_idx);
+    es = p.slot_of ? __ldcg(p.slot_of + e) : e;
+    base = __ldcg(p.offsets + e);
+    count = __ldcg(p.offsets + e + 1) - base;
+  }
+  (void)e;
   const int ntm = NTM;
   const int tpp = NTM * 8;
   const int K = p.K;

@@ -392,10 +392,12 @@ struct Item {
   int e, es, base, n0, nval, nmma, tile;  // es: the expert's weight slot
 };
 
-// Work-item ring: the weight-streaming thread publishes the index of the CTA's j-th item (or -1 once
-// the launch's counter has run past the last item) in slot j % ITEM_RING and arrives item_full;
-// every consuming role (token loader, MMA issuer, each dequant and epilogue warp) reads it and
-// arrives item_free, after which the slot can take item j + ITEM_RING.
+// Work-item ring: the weight-streaming thread decodes the CTA's j-th item (its chain of dependent
+// global loads: tile list -> active expert -> cache slot and offsets) and publishes it in slot
+// j % ITEM_RING (e = -1 once the launch's counter has run past the last item), then arrives
+// item_full; every consuming role (token loader, MMA issuer, each dequant and epilogue warp) copies
+// it from shared memory and arrives item_free, after which the slot can take item j + ITEM_RING.
+// The streaming thread runs ahead of the other roles, so none of them waits on those loads.
 constexpr int ITEM_RING = 8;
 
 template <class C>
@@ -403,19 +405,19 @@ __host__ __device__ constexpr int item_consumers() {
   return 2 + C::DQW + EPI_WARPS;
 }
 
-// The j-th item index for a consuming role: w >= 0, -1 when the launch has no more items, -2 when
-// the wait gave up (timeout or abort). Warp-collective when `warp_wide` (every lane gets the same
-// value; lane 0 releases the slot), else called by one thread.
-__device__ __forceinline__ int take_item(uint64_t* item_full, uint64_t* item_free, const volatile int* s_item, int j,
-                                         volatile int* abort, bool warp_wide) {
+// The j-th item for a consuming role: 1 with *it filled, 0 when the launch has no more items, -1
+// when the wait gave up (timeout or abort). Warp-collective when `warp_wide` (every lane gets the
+// same result; lane 0 releases the slot), else called by one thread.
+__device__ __forceinline__ int take_item(uint64_t* item_full, uint64_t* item_free, const Item* s_items, int j,
+                                         volatile int* abort, bool warp_wide, Item* it) {
   const int slot = j % ITEM_RING;
   bool ok = mbar_wait(&item_full[slot], (j / ITEM_RING) & 1, abort);
   if (warp_wide) ok = __all_sync(FULL, ok);
-  if (!ok) return -2;
-  const int w = s_item[slot];
+  if (!ok) return -1;
+  *it = s_items[slot];
   if (warp_wide) __syncwarp();
   if (!warp_wide || (threadIdx.x & 31) == 0) mbar_arrive(&item_free[slot]);
-  return w;
+  return it->e >= 0 ? 1 : 0;
 }
 
 template <int BN>
@@ -544,7 +546,7 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_free + ITEM_RING);
   __shared__ volatile int s_abort;
   __shared__ int s_units_issued, s_tiles_issued;
-  __shared__ volatile int s_item[ITEM_RING];
+  __shared__ Item s_items[ITEM_RING];
 
   pdl_wait();  // the tile list, the gathered tokens and the error word come from earlier kernels
   pdl_trigger();
@@ -603,12 +605,13 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
           s_abort = 1;
           break;
         }
-        int w = atomicAdd(p.work, 1);
-        if (w >= n_items) w = -1;
-        s_item[islot] = w;
-        mbar_arrive(&item_full[islot]);  // release: the index is visible to the roles that wait on it
-        if (w < 0) break;
-        const Item it = decode_item<C::BN>(p, w);
+        const int w = atomicAdd(p.work, 1);
+        Item it;
+        if (w < n_items) it = decode_item<C::BN>(p, w);
+        else it.e = -1;
+        s_items[islot] = it;
+        mbar_arrive(&item_full[islot]);  // release: the item is visible to the roles that wait on it
+        if (it.e < 0) break;
         for (int u = 0; u < units; ++u, ++g) {
           const int slot = g % R;
           if (g >= R && !mbar_wait(&raw_free[slot], ((g / R) - 1) & 1, abort)) {
@@ -627,12 +630,12 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
     if (lane == 0) {
       int q = 0;
       for (int j = 0; !*abort; ++j) {
-        const int w = take_item(item_full, item_free, s_item, j, abort, false);
-        if (w < 0) {
-          if (w == -2) s_abort = 1;
+        Item it;
+        const int got = take_item(item_full, item_free, s_items, j, abort, false, &it);
+        if (got <= 0) {
+          if (got < 0) s_abort = 1;
           break;
         }
-        const Item it = decode_item<C::BN>(p, w);
         const int boxes = (it.nmma + TMA_ROWS - 1) / TMA_ROWS;  // only the tile's own token rows
         for (int kc = 0; kc < kchunks; ++kc, ++q) {
           const int b = q % C::STG;
@@ -656,12 +659,12 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
       const uint64_t bdesc0 = smem_desc(smem_u32(sB));
       int q = 0;
       for (int j = 0; !*abort; ++j) {
-        const int w = take_item(item_full, item_free, s_item, j, abort, false);
-        if (w < 0) {
-          if (w == -2) s_abort = 1;
+        Item it;
+        const int got = take_item(item_full, item_free, s_items, j, abort, false, &it);
+        if (got <= 0) {
+          if (got < 0) s_abort = 1;
           break;
         }
-        const Item it = decode_item<C::BN>(p, w);
         const int acc = j % C::NACC;
         if (j >= C::NACC && !mbar_wait(&acc_free[acc], ((j / C::NACC) - 1) & 1, abort)) {
           s_abort = 1;
@@ -697,12 +700,12 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
     // ---------------- epilogue ----------------
     const int quad = warp & 3;  // tensor-memory lanes 32 quad .. +31
     for (int j = 0;; ++j) {
-      const int w = take_item(item_full, item_free, s_item, j, abort, true);
-      if (w < 0) {
-        if (w == -2 && lane == 0) s_abort = 1;
+      Item it;
+      const int got = take_item(item_full, item_free, s_items, j, abort, true, &it);
+      if (got <= 0) {
+        if (got < 0 && lane == 0) s_abort = 1;
         break;
       }
-      const Item it = decode_item<C::BN>(p, w);
       const int acc = j % C::NACC;
       const bool ok = __all_sync(FULL, mbar_wait(&acc_full[acc], (j / C::NACC) & 1, abort));
       if (!ok) {
@@ -728,12 +731,12 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
     int q = 0, g = 0, j_item = 0;
     bool stop = false;
     while (!stop) {
-      const int w = take_item(item_full, item_free, s_item, j_item, abort, true);
-      if (w < 0) {
-        stop = w == -2;
+      Item it;
+      const int got = take_item(item_full, item_free, s_items, j_item, abort, true, &it);
+      if (got <= 0) {
+        stop = got < 0;
         break;
       }
-      const Item it = decode_item<C::BN>(p, w);
       for (int kc = 0; kc < kchunks; ++kc, ++q) {
         if (C::DQG > 1 && q % C::DQG != grp) continue;
         const int gu = g + kc / W::CHUNKS_PER_UNIT, slot = gu % R;

@@ -54,6 +54,8 @@ static void free_scratch(moe_layer* L) {
   cudaFree(L->offsets);
   cudaFree(L->perm);
   cudaFree(L->active);
+  cudaFree(L->act_rec);
+  L->act_rec = nullptr;
   cudaFree(L->n_active);
   cudaFree(L->err);
   cudaFree(L->plan_ws);
@@ -105,6 +107,7 @@ static moe_status alloc_scratch(moe_layer* L, int max_tokens) {
   MOE_TRY(dalloc(&L->offsets, sizeof(int32_t) * (E + 1), &acc));
   MOE_TRY(dalloc(&L->perm, sizeof(int32_t) * cap, &acc));
   MOE_TRY(dalloc(&L->active, sizeof(int32_t) * E, &acc));
+  MOE_TRY(dalloc(&L->act_rec, sizeof(int4) * E, &acc));
   MOE_TRY(dalloc(&L->n_active, sizeof(int32_t), &acc));
   MOE_TRY(dalloc(&L->err, sizeof(int32_t), &acc));
   MOE_CUDA_TRY(cudaMemset(L->err, 0, sizeof(int32_t)));
@@ -543,7 +546,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   // the decode GEMV on Q8_0 units stages tokens converted once by the plan launch
   const bool prep = !use_tc && L->q8_tiles && dk == DECODE_GEMV && L->xq && plan_preps_tokens(n_pairs);
   const TokenPrep tp{static_cast<const __nv_bfloat16*>(x), T, H, L->xq, L->xq_scale};
-  PlanOut po{L->counts, L->offsets, L->perm, L->active, L->n_active, L->err, slot_of};
+  PlanOut po{L->counts, L->offsets, L->perm, L->active, L->n_active, L->err, slot_of, L->act_rec};
   MOE_TRY(mark(events, 0, st));
   MOE_TRY(plan_pairs(ids, n_pairs, E, po, L->plan_ws, L->plan_ws_bytes, st, prep ? &tp : nullptr));
   MOE_TRY(mark(events, 1, st));
@@ -614,6 +617,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   gp.perm = L->perm;
   gp.active = L->active;
   gp.n_active = L->n_active;
+  gp.act_rec = L->act_rec;
   gp.slot_of = slot_of;
   gp.tile_major = L->q8_tiles ? 1 : 0;
   if (prep) {

@@ -38,6 +38,7 @@ struct moe_layer {
   int32_t* offsets = nullptr;
   int32_t* perm = nullptr;
   int32_t* active = nullptr;
+  int4* act_rec = nullptr;  // [E] per-active-index {expert, slot, offset, count} records of the plan
   int32_t* n_active = nullptr;
   int32_t* err = nullptr;
   void* plan_ws = nullptr;

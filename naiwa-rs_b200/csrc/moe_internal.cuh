@@ -26,6 +26,9 @@ struct PlanOut {
   int32_t* n_active;  // [1]
   int32_t* err;       // [1] or null
   const int32_t* slot_of = nullptr;  // [E] cache slot of each expert (-1: not resident) or null (all resident)
+  // [E] or null: per active index a < n_active {expert, weight slot, offset, count}, {-1, 0, 0, 0}
+  // past it, so a decode CTA learns its expert with one 16-byte load instead of a dependent chain
+  int4* act_rec = nullptr;
 };
 // Token rows converted once per call for the decode GEMV's gate/up pass: each row's values scaled by
 // a power of two into f16 (the scale that stage_row picks) and laid out in B-fragment block order,
@@ -69,6 +72,7 @@ struct ExpertParams {
   const int32_t* slot_of;     // [E] cache slot of each expert, or null: weights indexed by expert id
   int tile_major;             // Q8_0 only: weights in 128 x 128 units (repack_q8_units)
   int32_t* err;               // [1] error word (a bounded wait that ran out), or null
+  const int4* act_rec = nullptr;    // the plan's per-active-index records (PlanOut::act_rec), or null
   const uint32_t* xq = nullptr;     // phase 0, Q8_0 units: the TokenPrep rows (null: stage from x)
   const float* xq_scale = nullptr;  // their scales
 };

@@ -117,6 +117,13 @@ __device__ void prep_row(const TokenPrep& q, int t, int lane) {
   }
 }
 
+// The per-active-index record of expert e (called once per e < E): active index a when it has pairs,
+// else one of the E - total trailing {-1, 0, 0, 0} records (e - a experts without pairs precede it).
+__device__ __forceinline__ void write_act_rec(const PlanOut& o, int e, int a, int total, int off, int count) {
+  if (count > 0) o.act_rec[a] = make_int4(e, o.slot_of ? o.slot_of[e] : e, off, count);
+  else o.act_rec[total + (e - a)] = make_int4(-1, 0, 0, 0);
+}
+
 // Whole plan in one CTA (n_pairs <= PLAN_SINGLE_MAX); CTAs 1.. convert the token rows of `prep`
 // (one warp per row) when it is given.
 __global__ void __launch_bounds__(PLAN_THREADS) plan_single_kernel(const uint32_t* __restrict__ ids, int n_pairs,
@@ -153,6 +160,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_single_kernel(const uint32_
     o.offsets[threadIdx.x] = off;
     base[threadIdx.x] = off;
     if (c > 0) o.active[a] = threadIdx.x;
+    if (o.act_rec) write_act_rec(o, threadIdx.x, a, total, off, c);
   }
   if (threadIdx.x == E - 1) o.offsets[E] = off + c;
   if (threadIdx.x == 0) *o.n_active = total;
@@ -195,6 +203,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_scan_kernel(int n_chunks, i
     o.counts[e] = total_e;
     o.offsets[e] = off;
     if (total_e > 0) o.active[a] = e;
+    if (o.act_rec) write_act_rec(o, e, a, total, off, total_e);
     int run = off;  // chunk bases in place
     for (int c = 0; c < n_chunks; ++c) {
       int v = chunk_counts[(size_t)c * E + e];
