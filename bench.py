@@ -262,10 +262,10 @@ def cpu_baseline_from_layer(stacks_host, router_host, budget_s=12.0):
 
 def _launches_local(pairs, E_local):
     """Kernel launches of one moe_forward over `pairs` routed pairs: plan (one CTA up to 8 K pairs,
-    else histogram / scan / scatter), the decode GEMV pair below 8 tokens per expert or the tcgen05
+    else histogram / scan / scatter), the decode GEMV pair below 4 tokens per expert or the tcgen05
     path at or above it (tile list, token gather, gate/up GEMM, h gather, down GEMM), combine."""
     plan = 1 if pairs <= PLAN_SINGLE_MAX else 3
-    experts = 5 if pairs >= 8 * E_local else 2
+    experts = 5 if pairs >= 4 * E_local else 2
     return plan + experts + 1
 
 
@@ -423,10 +423,10 @@ def run_ours(args):
     torch.cuda.synchronize()
     weight_bytes = {T: local_distinct[T] * BYTES_PER_EXPERT for T in RAGGED}
     # DRAM bytes (read + write) over algorithmic weight bytes in one ncu --set full capture of each
-    # path on this workload: the GEMV at T = 32 (373.2 / 367.7 MB gate/up, 190.7 / 183.8 MB down) and
-    # the tcgen05 GEMM at T = 256 (446.9 / 427.8 MB gate/up, 227.5 / 213.9 MB down)
-    gemv_ratio, gemm_ratio = (373.2 + 190.7) / (367.7 + 183.8), (446.9 + 227.5) / (427.8 + 213.9)
-    traffic_per_step = sum(weight_bytes[T] * (gemm_ratio if T * K_TOP * world >= 8 * E else gemv_ratio)
+    # path on this workload: the GEMV at T = 32 (372.1 / 367.7 MB gate/up, 189.4 / 183.8 MB down) and
+    # the tcgen05 GEMM at T = 256 (441.2 / 427.8 MB gate/up, 222.7 / 213.9 MB down)
+    gemv_ratio, gemm_ratio = (372.1 + 189.4) / (367.7 + 183.8), (441.2 + 222.7) / (427.8 + 213.9)
+    traffic_per_step = sum(weight_bytes[T] * (gemm_ratio if T * K_TOP * world >= 4 * E else gemv_ratio)
                            for T in RAGGED)
 
     # ---- stage timing: one captured step with events between the stages ---------------------------
@@ -565,7 +565,7 @@ def run_ours(args):
             "data": "synthetic: seeded N(0,0.02) Q8_0 experts and router, N(0,1) bf16 activations",
             "config": decode_config(world, args.layers),
             "roofline": {"kernel": ("expert FFN on this GPU's experts" + (" (rank 0)" if ep else "") +
-                                    ": decode GEMV below 8 tokens per expert, tcgen05 GEMM at or above (gate/up+"
+                                    ": decode GEMV below 4 tokens per expert, tcgen05 GEMM at or above (gate/up+"
                                     "SwiGLU and down*weight, Q8_0 units)"),
                          "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "peak_source": peak_kind,

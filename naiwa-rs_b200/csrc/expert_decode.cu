@@ -62,6 +62,11 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(Exp
     count = __ldcg(p.offsets + e + 1) - base;
   }
   (void)e;
+  // a record that names a slot or a pair range outside the buffers latches an error and is skipped
+  if (es < 0 || (p.n_wslots > 0 && es >= p.n_wslots) || base < 0 || count <= 0 || base + count > p.n_pairs) {
+    if (threadIdx.x == 0 && p.err) atomicExch(p.err, (int)MOE_ERR_INVALID);
+    return;
+  }
   const int ntm = NTM;
   const int tpp = NTM * 8;
   const int K = p.K;
@@ -93,9 +98,18 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(Exp
       pdl_wait();
       pdl_trigger();
     }
-    if (threadIdx.x < tpp) spair[threadIdx.x] = threadIdx.x < ntok ? p.perm[base + p0 + threadIdx.x] : -1;
+    if (threadIdx.x < tpp) {
+      int pr = threadIdx.x < ntok ? p.perm[base + p0 + threadIdx.x] : -1;
+      if (pr >= p.n_pairs || (threadIdx.x < ntok && pr < 0)) {  // outside the call's pairs: skipped, latched
+        if (p.err) atomicExch(p.err, (int)MOE_ERR_INVALID);
+        pr = -1;
+      }
+      spair[threadIdx.x] = pr;
+    }
+    __syncthreads();
     for (int n = warp; n < ntok; n += WARPS) {
-      const int src = phase == 0 ? p.perm[base + p0 + n] / p.width : base + p0 + n;
+      if (phase == 0 && spair[n] < 0) continue;
+      const int src = phase == 0 ? spair[n] / p.width : base + p0 + n;
       if constexpr (PH == 0) {
         if (p.xq) stage_prepped(p, n, src, xs, ntm, tscale, lane);
         else stage_row<WT::kF16>(p, n, src, xs, ntm, tscale, lane);
@@ -140,6 +154,7 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(Exp
                 p.out[(int64_t)(base + p0 + n) * I + tile * 8 + g] = gv / (1.0f + __expf(-gv)) * uv;
               } else {
                 const int pr = spair[n];
+                if (pr < 0) continue;
                 const float w = p.route_w[pr] * sc;
                 float* o = p.out + (int64_t)pr * p.N + tile * 16;
                 o[g] = acc[t][j] * w;
@@ -189,6 +204,7 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) expert_gemv_kernel(Exp
 #pragma unroll
           for (int s = 0; s < KS; ++s) sum += red[((size_t)s * ROWT * 16 + rl) * tpp + n];
           const int pr = spair[n];
+          if (pr < 0) continue;
           p.out[(int64_t)pr * p.N + row] = sum * tscale[n] * p.route_w[pr];
         }
       }

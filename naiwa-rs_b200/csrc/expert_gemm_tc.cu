@@ -1,5 +1,5 @@
 // expert_gemm_tc.cu — grouped expert GEMM on the 5th-generation tensor cores: prefill-size
-// batches (Q4_K / FP8 / Q8_0) and decode batches of 8 or more tokens per expert (Q8_0).
+// batches (Q4_K / FP8 / Q8_0) and decode batches of 4 or more tokens per expert (Q8_0).
 //
 // Reference: the fork's grouped MoE kernels behind MoEExperts::forward, driven by
 // PrefillStream::dispatch (src/moe/prefill_stream.rs:1178-1216) and forward_batched (:2080-2102),

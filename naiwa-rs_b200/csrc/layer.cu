@@ -453,9 +453,10 @@ static int pick_rowt(int tiles, int tpp, double est_active, int sms) {
 static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_t* ids, const float* weights,
                                int width, void* y, void* stream, void* const* events, bool combine = true);
 
-// A Q8_0 unit-layout layer runs the tcgen05 GEMM once the batch averages 8 or more tokens per
+// A Q8_0 unit-layout layer runs the tcgen05 GEMM once the batch averages 4 or more tokens per
 // expert (below that the GEMV streams the weights faster: it splits K across warps, so few experts
-// still fill the GPU, and its MMA work is still small); MOE_Q8_PATH=gemv|gemm pins the choice.
+// still fill the GPU, and its MMA work is still small; measured on config 2, T = 32 is a tie and
+// T = 64 is 4% faster on the GEMM); MOE_Q8_PATH=gemv|gemm pins the choice.
 static bool q8_uses_gemm(int n_pairs, int E) {
   static const int forced = [] {
     const char* v = std::getenv("MOE_Q8_PATH");
@@ -463,7 +464,7 @@ static bool q8_uses_gemm(int n_pairs, int E) {
     return std::string(v) == "gemm" ? 1 : std::string(v) == "gemv" ? -1 : 0;
   }();
   if (forced) return forced > 0;
-  return (int64_t)n_pairs >= 8ll * E;
+  return (int64_t)n_pairs >= 4ll * E;
 }
 
 // Below the tcgen05 threshold a Q8_0 unit layer streams its weights through registers (the decode
@@ -618,6 +619,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   gp.active = L->active;
   gp.n_active = L->n_active;
   gp.act_rec = L->act_rec;
+  gp.n_wslots = L->slots ? L->slots + L->staging : E;
   gp.slot_of = slot_of;
   gp.tile_major = L->q8_tiles ? 1 : 0;
   if (prep) {

@@ -73,6 +73,7 @@ struct ExpertParams {
   int tile_major;             // Q8_0 only: weights in 128 x 128 units (repack_q8_units)
   int32_t* err;               // [1] error word (a bounded wait that ran out), or null
   const int4* act_rec = nullptr;    // the plan's per-active-index records (PlanOut::act_rec), or null
+  int n_wslots = 0;                 // weight slots the kernel may index (0: not checked)
   const uint32_t* xq = nullptr;     // phase 0, Q8_0 units: the TokenPrep rows (null: stage from x)
   const float* xq_scale = nullptr;  // their scales
 };
