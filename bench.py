@@ -260,12 +260,19 @@ def cpu_baseline_from_layer(stacks_host, router_host, budget_s=12.0):
                       f"{ncpu} threads on {model}"}
 
 
-def _launches_local(pairs, E_local):
-    """Kernel launches of one moe_forward over `pairs` routed pairs: plan (one CTA up to 8 K pairs,
-    else histogram / scan / scatter), the decode GEMV pair below 4 tokens per expert or the tcgen05
-    path at or above it (tile list, token gather, gate/up GEMM, h gather, down GEMM), combine."""
+def _uses_gemm(live_pairs, E_local, sms=148):
+    """The layer's Q8_0 path choice (layer.cu, q8_uses_gemm): the tcgen05 GEMM from 4 live tokens per
+    expert when its gate/up items (E x 2I/128) fill two CTAs per SM, else from 16."""
+    fills = E_local * (2 * I // 128) >= 2 * sms
+    return live_pairs >= (4 if fills else 16) * E_local
+
+
+def _launches_local(pairs, E_local, live_pairs=None):
+    """Kernel launches of one moe_forward over `pairs` routed pairs (`live_pairs` of them live): plan
+    (one CTA up to 8 K pairs, else histogram / scan / scatter), the decode GEMV pair or the tcgen05
+    path (tile list, token gather, gate/up GEMM, h gather, down GEMM), combine."""
     plan = 1 if pairs <= PLAN_SINGLE_MAX else 3
-    experts = 5 if pairs >= 4 * E_local else 2
+    experts = 5 if _uses_gemm(pairs if live_pairs is None else live_pairs, E_local) else 2
     return plan + experts + 1
 
 
@@ -426,7 +433,7 @@ def run_ours(args):
     # path on this workload: the GEMV at T = 32 (372.1 / 367.7 MB gate/up, 189.4 / 183.8 MB down) and
     # the tcgen05 GEMM at T = 256 (441.2 / 427.8 MB gate/up, 222.7 / 213.9 MB down)
     gemv_ratio, gemm_ratio = (372.1 + 189.4) / (367.7 + 183.8), (441.2 + 222.7) / (427.8 + 213.9)
-    traffic_per_step = sum(weight_bytes[T] * (gemm_ratio if T * K_TOP * world >= 4 * E else gemv_ratio)
+    traffic_per_step = sum(weight_bytes[T] * (gemm_ratio if _uses_gemm(T * K_TOP, E // world) else gemv_ratio)
                            for T in RAGGED)
 
     # ---- stage timing: one captured step with events between the stages ---------------------------
@@ -552,7 +559,7 @@ def run_ours(args):
     # world * T rows, return, combine
     def launches_for(T):
         if ep:
-            return 1 + 1 + _launches_local(world * T * K_TOP, epr) + 2
+            return 1 + 1 + _launches_local(world * T * K_TOP, epr, T * K_TOP) + 2
         return 1 + _launches_local(T * K_TOP, E)
     launches_per_step = L * sum(launches_for(T) for T in RAGGED)
 

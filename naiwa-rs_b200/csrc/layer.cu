@@ -456,15 +456,20 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
 // A Q8_0 unit-layout layer runs the tcgen05 GEMM once the batch averages 4 or more tokens per
 // expert (below that the GEMV streams the weights faster: it splits K across warps, so few experts
 // still fill the GPU, and its MMA work is still small; measured on config 2, T = 32 is a tie and
-// T = 64 is 4% faster on the GEMM); MOE_Q8_PATH=gemv|gemm pins the choice.
-static bool q8_uses_gemm(int n_pairs, int E) {
+// T = 64 is 4% faster on the GEMM). When the GEMM's gate/up work items (one per expert and 128-row
+// tile) cannot fill the CTA slots (an expert-parallel rank's 16 experts: 192 items for 296 slots),
+// the GEMV keeps batches up to 16 tokens per expert (measured at 8 ranks: 8 tokens per expert 28%
+// faster on the GEMV, 16 tokens per expert 7% faster on the GEMM). MOE_Q8_PATH=gemv|gemm pins the
+// choice.
+static bool q8_uses_gemm(int n_pairs, int E, int gate_up_tiles, int sms) {
   static const int forced = [] {
     const char* v = std::getenv("MOE_Q8_PATH");
     if (!v) return 0;
     return std::string(v) == "gemm" ? 1 : std::string(v) == "gemv" ? -1 : 0;
   }();
   if (forced) return forced > 0;
-  return (int64_t)n_pairs >= 4ll * E;
+  const bool fills = (int64_t)E * gate_up_tiles >= 2ll * sms;
+  return (int64_t)n_pairs >= (fills ? 4ll : 16ll) * E;
 }
 
 // Below the tcgen05 threshold a Q8_0 unit layer streams its weights through registers (the decode
@@ -542,7 +547,7 @@ static moe_status forward_impl(moe_layer* L, const void* x, int T, const uint32_
   // grid bounds keep using every slot
   const int n_live = L->live_hint < 1.0f ? std::max(1, (int)((double)n_pairs * L->live_hint)) : n_pairs;
   const double est = (double)E * (1.0 - std::pow(1.0 - 1.0 / E, (double)n_live));
-  const bool use_tc = L->tc && (!L->q8_tiles || q8_uses_gemm(n_live, E));
+  const bool use_tc = L->tc && (!L->q8_tiles || q8_uses_gemm(n_live, E, 2 * I / 128, L->sms));
   const DecodeKernel dk = L->q8_tiles ? decode_kernel(n_live, E) : DECODE_GEMV;
   // the decode GEMV on Q8_0 units stages tokens converted once by the plan launch
   const bool prep = !use_tc && L->q8_tiles && dk == DECODE_GEMV && L->xq && plan_preps_tokens(n_pairs);

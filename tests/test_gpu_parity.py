@@ -259,12 +259,14 @@ def test_from_qtensors_matches_dequantised_reference():  # prefill_stream.rs:191
 # ---- expert FFN: random layers against the dequantised reference ---------------------------------
 
 @pytest.mark.parametrize("dtype", [O.DT_Q8_0, O.DT_BF16])
-@pytest.mark.parametrize("T", [1, 5, 33, 100])
+@pytest.mark.parametrize("T", [1, 5, 33, 100, 140])
 def test_forward_matches_dequantised_reference(dtype, T):
+    """A Q8_0 layer this small (too few GEMM work items to fill the GPU) keeps the decode GEMV below 16
+    tokens per expert: T = 1, 5 and 33 run the GEMV, T = 100 and 140 the tcgen05 GEMM."""
     rng = np.random.default_rng(100 + T + dtype)
     E, k, H, I = 16, 4, 256, 128
     q, d = make_stacks(rng, E, H, I, dtype)
-    layer = build_layer(q, E, k, H, I, dtype, max_tokens=128)
+    layer = build_layer(q, E, k, H, I, dtype, max_tokens=max(128, T))
     x = rng.normal(0, 1, (T, H)).astype(np.float32)
     xb = O.bf16_to_f32(O.f32_to_bf16(x))
     ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.uint32)
