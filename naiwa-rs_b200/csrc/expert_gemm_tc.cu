@@ -658,6 +658,7 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
     if (lane == 0) {
       const uint64_t bdesc0 = smem_desc(smem_u32(sB));
       int q = 0;
+      bool issued = false;  // a CTA may take no item at all when the others drain the counter first
       for (int j = 0; !*abort; ++j) {
         Item it;
         const int got = take_item(item_full, item_free, s_items, j, abort, false, &it);
@@ -687,13 +688,23 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS_PER_SM)
             umma_f16_ts(dcol, acol + (uint32_t)(k * 8), bd + (uint32_t)(((k >> 2) * (C::BN * 128) + (k & 3) * 32) >> 4),
                         idesc, (kc > 0 || k > 0) ? 1u : 0u);
           umma_commit(&stage_free[sa]);
+          issued = true;
         }
         if (*abort) break;
         umma_commit(&acc_full[acc]);
       }
-      // drain: every MMA this thread issued has completed once mma_done flips
-      umma_commit(mma_done);
-      if (!mbar_wait(mma_done, 0, nullptr)) s_abort = 1;
+      // drain: every MMA this thread issued has completed once mma_done flips (no commit at all when
+      // the CTA issued no MMA)
+      if (issued) {
+        umma_commit(mma_done);
+        if (!mbar_wait(mma_done, 0, nullptr)) s_abort = 1;
+      }
+      // The commits of the last STG chunks arrive on stage_free barriers nobody else waits for any
+      // more. Each arrive-on is a write to this CTA's shared memory: wait (bounded) until every one
+      // has landed, so none can land after the CTA has exited, in the shared memory of whatever
+      // CTA the SM runs next.
+      for (int c = q > C::STG ? q - C::STG : 0; c < q; ++c)
+        if (!mbar_wait(&stage_free[c % C::STG], (c / C::STG) & 1, nullptr)) s_abort = 1;
     }
     __syncwarp();
   } else if (warp >= C::EPI_WARP0) {

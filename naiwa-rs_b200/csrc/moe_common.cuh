@@ -95,21 +95,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return false;
 }
 
-// L2 policy for expert weights: evict first. Each weight byte is read once per layer call, and the
-// gigabytes streamed per step would otherwise push out what is reused (router matrices, token rows,
-// plan arrays, h and the pair outputs).
-__device__ __forceinline__ uint64_t l2_evict_first() {
-  uint64_t pol;
-  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-  return pol;
-}
-
-// 1-D bulk copy of expert weights into shared memory (evict-first in L2, as ldg_stream).
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(l2_evict_first())
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -193,13 +182,13 @@ __device__ __forceinline__ uint32_t total_key_u(float f) {
   return (uint32_t)b ^ 0x80000000u;
 }
 
-// Streaming 16-byte weight load: no L1 allocation, evict-first in L2. The data is read-only for the
-// kernel's lifetime, so the asm is not volatile and may be scheduled freely.
+// Streaming 16-byte load that does not allocate in L1 (weights are read once per launch). The
+// data is read-only for the kernel's lifetime, so the asm is not volatile and may be scheduled freely.
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   uint4 v;
-  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p), "l"(l2_evict_first()));
+               : "l"(p));
   return v;
 }
 
