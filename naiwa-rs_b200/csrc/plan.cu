@@ -49,7 +49,10 @@ __device__ __forceinline__ void rank_chunk(const uint32_t* __restrict__ ids, int
     whist[PLAN_WARPS * E + e] = run;  // chunk count of e (one extra row of scratch)
   }
   __syncthreads();
-  if (good) perm[base[id] + whist[warp * E + id] + lrank] = p;
+  if (good) {  // a position outside the call's pairs (ids that changed under the plan) is never written
+    const int pos = base[id] + whist[warp * E + id] + lrank;
+    if (pos >= 0 && pos < n_pairs) perm[pos] = p;
+  }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += PLAN_THREADS) base[e] += whist[PLAN_WARPS * E + e];
   __syncthreads();
