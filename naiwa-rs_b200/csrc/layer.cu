@@ -314,12 +314,40 @@ static moe_status validate_desc(const moe_layer_desc* d) {
 
 extern "C" {
 
+// The per-thread stack (local memory: register spills of some kernel variants) is reserved once
+// per device, before any forward runs. Left to the driver, the local-memory pool grows the first
+// time a kernel needs a larger frame; the test order decides when that happens, and when it fell
+// inside a chain of programmatically overlapped launches the forward ended in an illegal memory
+// access (five runs of the GPU test files in non-default orders ended that way; the two runs made
+// in those orders with the pool reserved up front passed). The limit is a per-process setting of this device's context:
+// MOE_STACK_RESERVE (bytes)
+// changes the reserve, 0 leaves the limit to the driver. 16 KB per thread reserves about 5 GB on a
+// 148-SM B200 (16 KB x 2,048 threads x 148 SMs).
+static moe_status reserve_local_memory(int dev) {
+  static std::mutex mu;
+  static bool done[64] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 0 || dev >= 64 || done[dev]) return MOE_OK;
+  static const size_t want = [] {
+    const char* v = std::getenv("MOE_STACK_RESERVE");
+    return v ? (size_t)std::strtoull(v, nullptr, 10) : (size_t)16384;
+  }();
+  if (want) {
+    size_t cur = 0;
+    MOE_CUDA_TRY(cudaDeviceGetLimit(&cur, cudaLimitStackSize));
+    if (cur < want) MOE_CUDA_TRY(cudaDeviceSetLimit(cudaLimitStackSize, want));
+  }
+  done[dev] = true;
+  return MOE_OK;
+}
+
 moe_status moe_layer_create(const moe_layer_desc* desc, moe_layer** out) {
   if (!out) return fail(MOE_ERR_INVALID, "moe_layer_create: null out");
   *out = nullptr;
   MOE_TRY(validate_desc(desc));
   DeviceGuard guard(desc->device);
   if (!guard.ok) return fail(MOE_ERR_CUDA, "moe_layer_create: cannot select device");
+  MOE_TRY(reserve_local_memory(desc->device));
   moe_layer* L = new moe_layer();
   L->d = *desc;
   L->dev = desc->device;
