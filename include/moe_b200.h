@@ -95,7 +95,10 @@ typedef struct {
 } moe_layer_desc;
 
 /* Replaces RoutedExpertsProvider::build (src/moe/provider.rs:316-615): validates the shape,
- * copies and repacks the expert stacks into device memory, allocates scratch for max_tokens. */
+ * copies and repacks the expert stacks into device memory, allocates scratch for max_tokens.
+ * The first layer created on a device raises that device's cudaLimitStackSize to 16 KB per thread
+ * (MOE_STACK_RESERVE=<bytes> changes it, 0 leaves the limit alone) for the rest of the process, so
+ * the driver never grows its local-memory pool in the middle of the forward's overlapped launches. */
 moe_status moe_layer_create(const moe_layer_desc* desc, moe_layer** out);
 
 /* Replaces the provider's warmup (src/moe/provider.rs:192-303): grows scratch to max_tokens. */
